@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the HeartMuLa per-frame decode path on B200.
+
+Workload: a 60 s song, 4 takes x 2 CFG rows = 8 rows, 750
+frames after a 600-token prompt, BASELINE architecture (28-layer 3072-wide
+backbone, 4-layer 1024-wide decoder, 8 codebooks of 8197) with random int8/fp16
+weights.  One step = one whole song decode: 750 replays of the one-frame CUDA
+graph (KV 600 -> 1350).  Weights (3.7 GB per frame) exceed L2, so no flush is
+needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank decodes its own 4 takes (weak scaling) and the finished
+token streams are gathered with NCCL; timing is the max over ranks.
+``--impl reference`` times the reference engine's own CPU path (restated in
+oracle/, bf16 with every host thread) on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "audio s/s per GPU at 4 takes+CFG; µs per frame (3B + 7 decoder passes)"
+UNIT = "audio-s/s"
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--takes", type=int, default=4)
+    ap.add_argument("--frames", type=int, default=750)
+    ap.add_argument("--prompt", type=int, default=600)
+    ap.add_argument("--cpu-frames", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-pdl", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- clocks
+class Clocks(threading.Thread):
+    """Samples SM clock and clock-event reasons through NVML during the timed region."""
+
+    NAMES = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+             0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+             0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        super().__init__(daemon=True)
+        self.index, self.samples, self.reasons, self.stop_ = index, [], 0, threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def run(self):
+        while self.nv and not self.stop_.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            except Exception:
+                pass
+            time.sleep(0.1)
+
+    def result(self):
+        self.stop_.set()
+        self.join(timeout=2)
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": [n for b, n in self.NAMES.items() if self.reasons & b and b != 0x1],
+                "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- workload
+def model_tensors(device, seed=0):
+    from estudiocanciones_b200.checkpoint import BASELINE_SHAPE, synthetic_tensors
+    return synthetic_tensors(BASELINE_SHAPE, seed=seed, device=device, gamma_one=True)
+
+
+def frame_bytes(m, B, mean_len):
+    """Algorithmic HBM bytes of one frame: every int8 weight byte and fp16 scale read
+    once, the backbone K/V of every row over its attended length, the decoder K/V,
+    the embedding rows and the logits/activations written once."""
+    bb, dec = m.backbone, m.decoder
+    w_bb = sum(l.nbytes for b in bb.blocks for l in (b.qkv, b.o, b.w13, b.w2))
+    w_dec = sum(l.nbytes for b in dec.blocks for l in (b.qkv, b.o, b.w13, b.w2))
+    w = w_bb + 7 * (w_dec + m.projection.nbytes) + m.c0_head.nbytes + sum(h.nbytes for h in m.audio_head)
+    b0 = bb.blocks[0]
+    kv = B * len(bb.blocks) * b0.kvh * b0.hd * 2 * 2 * mean_len
+    d0 = dec.blocks[0]
+    kv_dec = B * len(dec.blocks) * d0.kvh * d0.hd * 2 * 2 * (2 + sum(range(3, 9)))
+    emb = B * (8 + 7) * bb.dim
+    logits = 8 * B * m.vocab * 2
+    return w + kv + kv_dec + emb + logits
+
+
+def gemv_roofline(m, rt, peak, reps=10):
+    """Dominant kernel (the fused int8 GEMV): the 112 backbone GEMV launches of one frame
+    back to back (4 per layer, real prologues/epilogues), timed with CUDA events on the
+    launching stream; algorithmic bytes = weights + scales + activations in/out."""
+    from estudiocanciones_b200.engine import FramePlan
+    from estudiocanciones_b200._lib import HM_EPI_ROPE_KV, HM_EPI_SILU
+    bb = rt.bb
+    B = rt.B
+    p = FramePlan(rt.ctx)
+    nbytes = 0
+    for b in m.backbone.blocks:
+        p._gemv(b.qkv, B, p.src_rms(bb.x, bb.ss, b.n1), epi=HM_EPI_ROPE_KV, rope=m.backbone.rope, pos=rt.pos, S=1,
+                blk=b, q_out=bb.q)
+        p._gemv(b.o, B, p.src_f16(bb.o), y=bb.x, res=bb.x, ss_out=bb.ss)
+        p._gemv(b.w13, B, p.src_rms(bb.x, bb.ss, b.n2), epi=HM_EPI_SILU, y=bb.mm)
+        p._gemv(b.w2, B, p.src_f16(bb.mm), y=bb.x, res=bb.x, ss_out=bb.ss)
+        D = b.dim
+        nbytes += b.qkv.nbytes + B * D * 2 + B * (b.qkv.N - b.kvh * b.hd) * 2 + b.kvh * b.hd * 2 * 2 * B
+        nbytes += b.o.nbytes + B * b.o.K * 2 + 2 * B * D * 2
+        nbytes += b.w13.nbytes + B * D * 2 + B * b.ffn * 2
+        nbytes += b.w2.nbytes + B * b.ffn * 2 + 2 * B * D * 2
+    p.run()
+    torch.cuda.synchronize()
+    # the launches are replayed from a CUDA graph so host launch cost does not enter
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            p.run()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(reps):
+        g.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    del g
+    sec = t0.elapsed_time(t1) / 1000 / (reps * p.n_kernels)
+    per_launch = nbytes / p.n_kernels
+    achieved = per_launch / sec / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "kernel": "gemv_i8_kernel (112 backbone launches, R=8)",
+            "bytes_per_launch": int(per_launch), "us_per_launch": round(sec * 1e6, 3)}
+
+
+def traffic_from_profile():
+    f = ROOT / "profiles" / "gemv_traffic.json"
+    if f.exists():
+        try:
+            return json.loads(f.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- CPU path (reference arm / baseline)
+def cpu_reference_timer(a, tensors_cpu):
+    """The reference's own CPU path (app/engine.py CPU branch: bf16 weights dequantised at
+    load, F.linear, masked SDPA, _frame_from_h) restated in oracle/, all host threads."""
+    from oracle.heartmula_oracle import OracleModel
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, N, P = 2 * a.takes, a.takes, a.prompt
+    o = OracleModel(tensors_cpu, mode="cpu", dtype=torch.bfloat16)
+    L = P + a.frames + 2 + 256
+    o.alloc(B, L)
+    g = torch.Generator().manual_seed(0)
+    for ly in o.bb:
+        ly.kc[:, :, :P] = torch.randn(ly.kc[:, :, :P].shape, generator=g).to(ly.kc.dtype)
+        ly.vc[:, :, :P] = torch.randn(ly.vc[:, :, :P].shape, generator=g).to(ly.vc.dtype)
+    tok = torch.randint(0, 8192, (B, 8), generator=g)
+    state = {"pos": P, "tok": tok}
+
+    def frames(n):
+        t = time.perf_counter()
+        for _ in range(n):
+            pos = torch.full((B, 1), state["pos"])
+            state["tok"] = o.step(state["tok"], pos, N, 1.5, 50, 1.0)
+            state["pos"] += 1
+        return time.perf_counter() - t
+    return frames, torch.get_num_threads()
+
+
+def run_reference(a, world, rank):
+    if rank != 0:
+        return
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    t = {k: v.cpu() for k, v in model_tensors(dev).items()}
+    frames, cores = cpu_reference_timer(a, t)
+    del t
+    for _ in range(a.warmup):
+        frames(a.cpu_frames)
+    times = [frames(a.cpu_frames) for _ in range(a.steps)]
+    sec = sum(times)
+    n = a.steps * a.cpu_frames
+    value = a.takes * n * 0.08 / sec
+    sample = f"{a.cpu_frames} frames per step of config 1 (8 rows, KV from {a.prompt}) on the CPU path, bf16"
+    out = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": round(1000 * sec / a.steps, 2), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "impl": "reference", "us_per_frame": round(1e6 * sec / n, 1),
+           "config": {"workload": "config1: 60 s song, 4 takes x CFG = 8 rows, KV 600->1350 (CPU sample)",
+                      "model": "HeartMuLa BASELINE shape (28x3072 backbone, 4x1024 decoder), random int8"},
+           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(a, world, rank, local):
+    from estudiocanciones_b200 import kernels
+    from estudiocanciones_b200.engine import HeartMuLaLite
+    dev = torch.device("cuda", local)
+    torch.manual_seed(1000 + rank)
+    t = model_tensors(dev, seed=0)
+    m = HeartMuLaLite(t, device=dev)
+    del t
+    N, B, P, F_ = a.takes, 2 * a.takes, a.prompt, a.frames
+    L = P + F_ + 2 + 256
+    m.alloc(N, B, L)
+    rt = m._rt
+    g = torch.Generator(device=dev).manual_seed(0)
+    for blk in m.backbone.blocks:
+        blk.kc[:, :, :P].normal_(generator=g)
+        blk.vc[:, :, :P].normal_(generator=g)
+    rt.tok_in.copy_(torch.randint(0, 8192, (B, 8), generator=g, device=dev))
+    rt.pos.fill_(P)
+    rt.pdl = not a.no_pdl
+    graph = rt.graph_for(1.5, 50, 1.0)
+    plan = rt.plan_for(1.5, 50, 1.0, with_backbone=True, commit=True)
+    gathered = [torch.empty_like(rt.stream_out[:F_]) for _ in range(world)] if world > 1 else None
+
+    def step():
+        rt.pos.fill_(P)
+        rt.frame.zero_()
+        for _ in range(F_):
+            graph.replay()
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather(gathered, rt.stream_out[:F_])
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.result()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps, world)
+    err = kernels.read_errors(dev)
+    if err:
+        raise RuntimeError(f"kernel error bits {err}")
+    us_frame = 1000 * ms / F_
+    value = world * a.takes * F_ * 0.08 / (ms / 1000)
+    peak, peak_kind = peaks()
+    mean_len = P + (F_ + 1) / 2
+    fb = frame_bytes(m, B, mean_len)
+    roof = gemv_roofline(m, rt, peak)
+    roof["traffic"] = traffic_from_profile()
+    roof["peak_kind"] = f"{peak_kind} hbm_gbs (burst)"
+    frame_gbs = fb / (us_frame * 1e-6) / 1e9
+    out = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "fp16 activations x int8 weights (fp32 accumulate)", "data": "synthetic",
+           "us_per_frame": round(us_frame, 2), "frames_per_s": round(1e6 / us_frame, 1),
+           "audio_s_per_s_per_gpu": round(value / world, 3),
+           "config": {"workload": f"config1: 60 s song, {a.takes} takes x CFG = {B} rows per GPU, {F_} frames "
+                                  f"after a {P}-token prompt (KV {P}->{P + F_}), one CUDA graph per frame",
+                      "model": "HeartMuLa BASELINE shape (28x3072 backbone 24/8 heads, 4x1024 decoder 8/2 heads, "
+                               "8x8197 codebooks), random int8 weights",
+                      "parallelism": f"takes sharded, {world} GPU(s), NCCL gather of token streams",
+                      "l2": "inputs larger than L2 (3.7 GB weights per frame)",
+                      "pdl": not a.no_pdl},
+           "roofline": roof,
+           "frame_roofline": {"bytes_per_frame": int(fb), "achieved": round(frame_gbs, 1), "peak": peak,
+                              "unit": "GB/s", "frac": round(frame_gbs / peak, 4)},
+           "gpu_launches": int(plan.n_kernels * F_ * a.steps),
+           "clocks": clk}
+    # ---- end to end through the public API: host prompt ids -> generate -> host token streams
+    if not a.no_e2e:
+        text = torch.randint(0, 128256, (P,), generator=torch.Generator().manual_seed(rank)).pin_memory()
+        del rt, graph
+        m.release()
+
+        def e2e_step():
+            res = m.generate_ids(text, 10, max_ms=F_ * 80, n=a.takes, cfg_scale=1.5, seed=rank,
+                                 stop_at_eos=False)
+            return [r.cpu() for r in res]
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(a.e2e_steps):
+            res = e2e_step()
+        torch.cuda.synchronize()
+        sec = max_over_ranks((time.perf_counter() - t0) / a.e2e_steps, world)
+        d2h = sum(r.numel() * 8 for r in res) + math.ceil(F_ / 25) * 25 * a.takes
+        out["e2e"] = {"value": round(world * a.takes * F_ * 0.08 / sec, 3), "unit": UNIT,
+                      "h2d_bytes_per_step": P * 8, "d2h_bytes_per_step": int(d2h),
+                      "ms_per_step": round(1000 * sec, 2),
+                      "includes": "prompt H2D, GPU text-embedding gather, prefill, 750 frames, EOS checks, D2H"}
+    # ---- CPU baseline: the reference CPU path on this host, rank 0 at N=1
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        tcpu = {k: v.cpu() for k, v in model_tensors(dev, seed=0).items()}
+        torch.cuda.empty_cache()
+        frames, cores = cpu_reference_timer(a, tcpu)
+        del tcpu
+        frames(1)
+        sec = frames(a.cpu_frames)
+        out["cpu_baseline"] = {"value": round(a.takes * a.cpu_frames * 0.08 / sec, 4), "unit": UNIT,
+                               "cores": cores, "kind": "port",
+                               "sample": f"{a.cpu_frames} frames of config 1 (8 rows, KV from {P}) through the "
+                                         f"reference CPU path (bf16), after 1 warm-up frame",
+                               "us_per_frame": round(1e6 * sec / a.cpu_frames, 1)}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def main():
+    a = args_()
+    world, rank, local = dist_setup()
+    try:
+        if a.impl == "reference":
+            run_reference(a, world, rank)
+        else:
+            run_ours(a, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,339 @@
+// Split-K GQA decode attention over the static KV cache (sm_100a).
+//
+// Replaces `_attn` + `_attn_combine` (app/kernels.py:112-167) as launched by
+// Stack.decode (app/engine.py:194-204).  Row r (batch r / S) attends to cache
+// positions [0, pos[r]], read from device memory so one CUDA graph serves every
+// frame.  The G = Hq/Hk query heads of a KV head share one pass over its K/V
+// (no KV copy per group).
+//
+// Grid (nsplit, Hk, R), 128 threads.  Each CTA streams its position range in
+// tiles of 32 positions; the K and V rows of a tile are contiguous in the cache
+// ([B, Hk, L, hd] layout), so each tile is two 1-D bulk copies into a
+// double-buffered shared-memory ring completed on mbarriers.  Scores and the
+// PV product run in fp32 on CUDA cores (the kernel is HBM-bound: 2*G*hd FMAs
+// per 4*hd bytes); probabilities are rounded to fp16 before the PV product
+// and the normaliser keeps the fp32 sum, as in _attn.  With nsplit > 1 the
+// last CTA of each (row, KV head) merges the split partials (log-sum-exp) and
+// re-arms its ticket.
+#include "hm_common.cuh"
+
+namespace {
+
+constexpr int kTP = 32;       // positions per tile
+constexpr int kThreads = 128;
+constexpr int kMaxG = 8;
+
+struct AttnParams {
+  const __half* q;
+  const __half* kc;
+  const __half* vc;
+  const int64_t* pos;
+  __half* o;
+  int R, S, Hq, Hk, L, nsplit;
+  float scale;
+  float* ws;
+  int* counters;
+  int* err;
+};
+
+template <int HD>
+struct AttnSmem {
+  __half k[2][kTP][HD];
+  __half v[2][kTP][HD];
+  float q[kMaxG][HD];
+  float s[kMaxG][kTP];
+  float red[kMaxG][HD];
+  float alpha[kMaxG], m[kMaxG], l[kMaxG];
+  uint64_t bar[2];
+  int flag;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ AttnParams P) {
+  constexpr int CPT = HD / 32;  // 16-byte chunks of a K row per thread (4 threads per position)
+  constexpr int U = HD / 128;   // half2 columns per thread in the PV product
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  AttnSmem<HD>& sm = *reinterpret_cast<AttnSmem<HD>*>(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sp = blockIdx.x, kh = blockIdx.y, r = blockIdx.z;
+  const int G = P.Hq / P.Hk;
+
+  if (tid == 0) {
+    mbar_init(&sm.bar[0], 1);
+    mbar_init(&sm.bar[1], 1);
+    fence_barrier_init();
+  }
+  pdl_trigger();
+  pdl_wait();
+
+  const int64_t p_last = P.pos[r];
+  const int b = r / P.S;
+  int len = static_cast<int>(p_last) + 1;
+  if (p_last < 0 || p_last >= P.L) {
+    report_error(P.err, HM_ERR_BADINDEX);
+    len = 0;
+  }
+  const int per = (len + P.nsplit - 1) / P.nsplit;
+  const int chunk = (per + kTP - 1) / kTP * kTP;
+  const int lo = sp * chunk;
+  const int hi = min(len, lo + chunk);
+  const int ntile = hi > lo ? (hi - lo + kTP - 1) / kTP : 0;
+
+  const __half* kbase = P.kc + ((int64_t)b * P.Hk + kh) * P.L * HD;
+  const __half* vbase = P.vc + ((int64_t)b * P.Hk + kh) * P.L * HD;
+
+  // q of the G heads of this KV head, fp32
+  for (int i = tid; i < G * HD; i += kThreads) {
+    const int gg = i / HD, d = i - gg * HD;
+    sm.q[gg][d] = __half2float(P.q[(int64_t)r * P.Hq * HD + (kh * G + gg) * HD + d]);
+  }
+  if (tid < kMaxG) {
+    sm.m[tid] = -INFINITY;
+    sm.l[tid] = 0.f;
+  }
+  __syncthreads();
+
+  auto issue = [&](int t) {
+    const int st = t & 1;
+    const int p0 = lo + t * kTP;
+    const int nv = min(kTP, hi - p0);
+    const uint32_t bytes = static_cast<uint32_t>(nv) * HD * 2;
+    mbar_arrive_expect_tx(&sm.bar[st], 2 * bytes);
+    bulk_load(&sm.k[st][0][0], kbase + (int64_t)p0 * HD, bytes, &sm.bar[st]);
+    bulk_load(&sm.v[st][0][0], vbase + (int64_t)p0 * HD, bytes, &sm.bar[st]);
+  };
+  if (tid == 0) {
+    if (ntile > 0) issue(0);
+    if (ntile > 1) issue(1);
+  }
+
+  float acc[kMaxG][2 * U];
+#pragma unroll
+  for (int gg = 0; gg < kMaxG; ++gg)
+#pragma unroll
+    for (int u = 0; u < 2 * U; ++u) acc[gg][u] = 0.f;
+
+  const int qp = tid >> 2, qd = tid & 3;   // QK: position qp of the tile, quarter qd of the row
+  const int ph = tid >> 6, dc = tid & 63;  // PV: position parity ph, half2 column group dc
+  bool ok = true;
+  for (int t = 0; t < ntile; ++t) {
+    const int st = t & 1;
+    const int p0 = lo + t * kTP;
+    const int nv = min(kTP, hi - p0);
+    if (!mbar_wait(&sm.bar[st], (t >> 1) & 1, P.err)) {
+      ok = false;
+      break;
+    }
+    // ---- scores s[g][p] = (q_g . k_p) * scale
+    {
+      float part[kMaxG];
+#pragma unroll
+      for (int gg = 0; gg < kMaxG; ++gg) part[gg] = 0.f;
+      if (qp < nv) {
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+          const int c = qd * CPT + (i + qd + (qp & 1)) % CPT;   // rotated chunk order (bank spread)
+          const uint4 kv = *reinterpret_cast<const uint4*>(&sm.k[st][qp][c * 8]);
+          const __half2* kh2 = reinterpret_cast<const __half2*>(&kv);
+          float kf[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(kh2[j]);
+            kf[2 * j] = f.x;
+            kf[2 * j + 1] = f.y;
+          }
+#pragma unroll
+          for (int gg = 0; gg < kMaxG; ++gg) {
+            if (gg < G) {
+              const float4 q0 = *reinterpret_cast<const float4*>(&sm.q[gg][c * 8]);
+              const float4 q1 = *reinterpret_cast<const float4*>(&sm.q[gg][c * 8 + 4]);
+              part[gg] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] +
+                          q1.y * kf[5] + q1.z * kf[6] + q1.w * kf[7];
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int gg = 0; gg < kMaxG; ++gg) {
+        float v = part[gg];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (gg < G && qd == 0) sm.s[gg][qp] = qp < nv ? v * P.scale : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // ---- online softmax update per head (lane = position)
+    for (int gg = warp; gg < G; gg += kThreads / 32) {
+      const float sc = sm.s[gg][lane];
+      const float m_old = sm.m[gg];
+      const float m_new = fmaxf(m_old, warp_max(sc));
+      float pe = 0.f, alpha = 1.f;
+      if (m_new != -INFINITY) {
+        pe = sc == -INFINITY ? 0.f : expf(sc - m_new);
+        alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+      }
+      const float tot = warp_sum(pe);
+      sm.s[gg][lane] = __half2float(__float2half_rn(pe));
+      if (lane == 0) {
+        sm.alpha[gg] = alpha;
+        sm.m[gg] = m_new;
+        sm.l[gg] = sm.l[gg] * alpha + tot;
+      }
+    }
+    __syncthreads();
+    // ---- acc = acc*alpha + P V
+#pragma unroll
+    for (int gg = 0; gg < kMaxG; ++gg) {
+      if (gg < G) {
+        const float a = sm.alpha[gg];
+#pragma unroll
+        for (int u = 0; u < 2 * U; ++u) acc[gg][u] *= a;
+      }
+    }
+    for (int p = ph; p < nv; p += 2) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(&sm.v[st][p][2 * (dc + 64 * u)]));
+#pragma unroll
+        for (int gg = 0; gg < kMaxG; ++gg) {
+          if (gg < G) {
+            const float pr = sm.s[gg][p];
+            acc[gg][2 * u] += pr * vf.x;
+            acc[gg][2 * u + 1] += pr * vf.y;
+          }
+        }
+      }
+    }
+    __syncthreads();  // stage st and s[][] are free again
+    if (tid == 0 && t + 2 < ntile) issue(t + 2);
+  }
+  if (!ok) {
+    mbar_wait(&sm.bar[0], 0, nullptr);
+    mbar_wait(&sm.bar[1], 0, nullptr);
+    return;
+  }
+
+  // ---- merge the two position parities into red[g][d]
+  if (ph == 1) {
+#pragma unroll
+    for (int gg = 0; gg < kMaxG; ++gg)
+      if (gg < G)
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          sm.red[gg][2 * (dc + 64 * u)] = acc[gg][2 * u];
+          sm.red[gg][2 * (dc + 64 * u) + 1] = acc[gg][2 * u + 1];
+        }
+  }
+  __syncthreads();
+  if (ph == 0) {
+#pragma unroll
+    for (int gg = 0; gg < kMaxG; ++gg)
+      if (gg < G)
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          sm.red[gg][2 * (dc + 64 * u)] += acc[gg][2 * u];
+          sm.red[gg][2 * (dc + 64 * u) + 1] += acc[gg][2 * u + 1];
+        }
+  }
+  __syncthreads();
+
+  const int64_t head0 = (int64_t)r * P.Hq + kh * G;
+  if (P.nsplit == 1) {
+    for (int i = tid; i < G * HD; i += kThreads) {
+      const int gg = i / HD, d = i - gg * HD;
+      const float l = sm.l[gg];
+      P.o[(head0 + gg) * HD + d] = __float2half_rn(l > 0.f ? sm.red[gg][d] / l : 0.f);
+    }
+    return;
+  }
+  const int64_t nh = (int64_t)P.R * P.Hq * P.nsplit;
+  float* wm = P.ws;
+  float* wl = P.ws + nh;
+  float* wa = P.ws + 2 * nh;
+  for (int i = tid; i < G * HD; i += kThreads) {
+    const int gg = i / HD, d = i - gg * HD;
+    wa[((head0 + gg) * P.nsplit + sp) * HD + d] = sm.red[gg][d];
+  }
+  if (tid < G) {
+    wm[(head0 + tid) * P.nsplit + sp] = sm.m[tid];
+    wl[(head0 + tid) * P.nsplit + sp] = sm.l[tid];
+  }
+  __threadfence();
+  __syncthreads();
+  int* ticket = &P.counters[r * P.Hk + kh];
+  if (tid == 0) sm.flag = (atomicAdd(ticket, 1) == P.nsplit - 1);
+  __syncthreads();
+  if (!sm.flag) return;
+  __threadfence();
+  for (int i = tid; i < G * HD; i += kThreads) {
+    const int gg = i / HD, d = i - gg * HD;
+    const int64_t h = head0 + gg;
+    float mx = -INFINITY;
+    for (int s2 = 0; s2 < P.nsplit; ++s2) mx = fmaxf(mx, __ldcg(wm + h * P.nsplit + s2));
+    float num = 0.f, den = 0.f;
+    for (int s2 = 0; s2 < P.nsplit; ++s2) {
+      const float ms = __ldcg(wm + h * P.nsplit + s2);
+      const float w = ms > -INFINITY ? expf(ms - mx) : 0.f;
+      num += __ldcg(wa + (h * P.nsplit + s2) * HD + d) * w;
+      den += __ldcg(wl + h * P.nsplit + s2) * w;
+    }
+    P.o[h * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+  }
+  if (tid == 0) *ticket = 0;
+}
+
+template <int HD>
+cudaError_t launch_attn(const AttnParams& p, int pdl, cudaStream_t st) {
+  const size_t smem = sizeof(AttnSmem<HD>);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return hm_launch(decode_attn_kernel<HD>, dim3(p.nsplit, p.Hk, p.R), dim3(kThreads), smem, st, pdl, p);
+}
+
+}  // namespace
+
+extern "C" size_t hm_decode_attn_workspace_bytes(int R, int Hq, int hd, int nsplit) {
+  if (nsplit <= 1) return 0;
+  return static_cast<size_t>(R) * Hq * nsplit * (hd + 2) * sizeof(float);
+}
+
+extern "C" int hm_decode_attn(const void* q, const void* kc, const void* vc, const int64_t* pos, void* o, int R,
+                              int S, int Hq, int Hk, int hd, int L, float scale, int nsplit, void* ws,
+                              size_t ws_bytes, int* counters, int n_counters, int* err, int pdl,
+                              hm_stream_t stream) {
+  if (!q || !kc || !vc || !pos || !o || R < 1 || S < 1 || R % S || Hk < 1 || Hq % Hk || Hq / Hk > kMaxG || L < 1 ||
+      nsplit < 1 || nsplit > 1024)
+    return HM_EARG;
+  if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15u) return HM_EARG;
+  if (nsplit > 1 && (!ws || !counters || n_counters < R * Hk || ws_bytes < hm_decode_attn_workspace_bytes(R, Hq, hd, nsplit)))
+    return HM_EARG;
+  AttnParams p;
+  p.q = reinterpret_cast<const __half*>(q);
+  p.kc = reinterpret_cast<const __half*>(kc);
+  p.vc = reinterpret_cast<const __half*>(vc);
+  p.pos = pos;
+  p.o = reinterpret_cast<__half*>(o);
+  p.R = R;
+  p.S = S;
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.L = L;
+  p.nsplit = nsplit;
+  p.scale = scale;
+  p.ws = reinterpret_cast<float*>(ws);
+  p.counters = counters;
+  p.err = err;
+  cudaError_t e;
+  switch (hd) {
+    case 128: e = launch_attn<128>(p, pdl, stream); break;
+    case 256: e = launch_attn<256>(p, pdl, stream); break;
+    case 384: e = launch_attn<384>(p, pdl, stream); break;
+    default: return HM_EARG;
+  }
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}

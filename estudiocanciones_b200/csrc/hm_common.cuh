@@ -1,0 +1,171 @@
+// Shared device helpers for the HeartMuLa sm_100a decode kernels.
+//
+// Everything here is plain inline PTX for features the kernels rely on:
+// programmatic dependent launch (griddepcontrol), mbarriers with bounded waits,
+// TMA tile loads (cp.async.bulk.tensor) and 1-D bulk copies (cp.async.bulk),
+// the fp16 tensor-core MMA, and an exact int8 -> fp16 conversion.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <utility>
+
+#include "heartmula_b200.h"
+
+// Upper bound for any wait inside a kernel (mbarrier, split-K fixup). A healthy
+// wait ends in microseconds; after this the kernel records HM_ERR_TIMEOUT in the
+// caller's error word and returns instead of spinning on.
+#ifndef HM_WAIT_NS
+#define HM_WAIT_NS 2000000000ull
+#endif
+
+#define HM_DEV __device__ __forceinline__
+
+HM_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// wait: block until every grid this launch depends on has completed and its
+// memory is visible.  Code before it may only read data no earlier kernel writes.
+HM_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// trigger: let the next launch in the stream start its prologue early.
+HM_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+HM_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+HM_DEV void report_error(int* err, int code) {
+  if (err) atomicOr(err, code);
+}
+
+// ---------------------------------------------------------------- mbarrier
+HM_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// make barrier initialisation visible to the async (TMA) proxy
+HM_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+HM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+HM_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+HM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on phase `parity`.  Returns false (and records HM_ERR_TIMEOUT)
+// when the phase does not complete within HM_WAIT_NS or 2^28 polls.
+HM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 28); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > HM_WAIT_NS) break;
+  }
+  report_error(err, HM_ERR_TIMEOUT);
+  return false;
+}
+
+// ---------------------------------------------------------------- TMA
+// 2-D tiled load global -> shared, completion counted on `bar` (bytes).
+// x is the innermost coordinate (elements); callers keep x*elem_size % 16 == 0.
+HM_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
+HM_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+HM_DEV uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+HM_DEV uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+HM_DEV void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- math helpers
+// Exact int8 -> fp16 for four packed bytes: (b0,b1) -> lo, (b2,b3) -> hi.
+// Each byte is biased to 0..255, placed in the mantissa of 1024.0 and the
+// bias 1024+128 is subtracted; every int8 value is exactly representable.
+HM_DEV void i8x4_to_h2x2(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = v ^ 0x80808080u;
+  lo = __byte_perm(u, 0x64646464u, 0x5140);
+  hi = __byte_perm(u, 0x64646464u, 0x5342);
+  const uint32_t bias = 0x64806480u;  // 1152.0 in both halves
+  asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(lo) : "r"(bias));
+  asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(hi) : "r"(bias));
+}
+
+// D(16x8,f32) += A(16x16,f16,row) * B(16x8,f16,col)
+HM_DEV void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+HM_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+HM_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// fp16(a) * fp16(b) rounded once to fp16 (the product of two fp16 values is
+// exact in fp32, so this equals an IEEE fp16 multiply).
+HM_DEV __half hmul_rn(__half a, __half b) { return __float2half_rn(__half2float(a) * __half2float(b)); }
+HM_DEV __half hadd_rn(__half a, __half b) { return __hadd(a, b); }
+
+// Launch helper: every kernel is launched with the programmatic-stream-
+// serialisation attribute when `pdl` is set, so it may overlap the previous
+// kernel's tail (its own griddepcontrol.wait keeps the data dependency).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t hm_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t stream, int pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

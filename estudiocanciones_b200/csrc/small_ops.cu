@@ -1,0 +1,211 @@
+// Small per-row kernels of the HeartMuLa decode path (sm_100a).
+//
+// These back the reference's standalone entry points (`rms`, `_rope_cache`,
+// `_silu_mul` in app/kernels.py, `Emb.__call__` and the frame's embedding sum
+// in app/engine.py).  The fused decode path folds RMSNorm, RoPE and SiLU into
+// the GEMV (gemv_i8.cu); what remains per frame here is the embedding sum that
+// starts the backbone and the frame-commit bookkeeping at the end.
+#include "hm_common.cuh"
+
+namespace {
+
+// ------------------------------------------------------------------ RMSNorm
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
+                                                      __half* __restrict__ y, int D, float eps) {
+  __shared__ float red[8];
+  __shared__ float inv_s;
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const __half* xr = x + (int64_t)r * D;
+  float a = 0.f;
+  for (int k = tid; k < D; k += 256) {
+    const float v = __half2float(xr[k]);
+    a += v * v;
+  }
+  a = warp_sum(a);
+  if ((tid & 31) == 0) red[tid >> 5] = a;
+  __syncthreads();
+  if (tid == 0) {
+    float s = 0.f;
+    for (int i = 0; i < 8; ++i) s += red[i];
+    inv_s = 1.0f / sqrtf(s / static_cast<float>(D) + eps);
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  for (int k = tid; k < D; k += 256)
+    y[(int64_t)r * D + k] = hmul_rn(__float2half_rn(__half2float(xr[k]) * inv), w[k]);
+}
+
+// ------------------------------------------------------------------ RoPE + KV-cache write
+__global__ void rope_kv_kernel(const __half* __restrict__ qkv, const float* __restrict__ rope, int rope_rows,
+                               const int64_t* __restrict__ pos, __half* __restrict__ q_out, __half* __restrict__ kc,
+                               __half* __restrict__ vc, int S, int Hq, int Hk, int hd, int L, int* err) {
+  const int r = blockIdx.x, h = blockIdx.y, i = threadIdx.x;  // pair (2i, 2i+1)
+  if (2 * i >= hd) return;
+  const int64_t p = pos[r];
+  if (p < 0 || p >= L || p >= rope_rows) {
+    if (i == 0) report_error(err, HM_ERR_BADINDEX);
+    return;
+  }
+  const int b = r / S;
+  const int W = (Hq + 2 * Hk) * hd;
+  const float c = rope[(p * (hd / 2) + i) * 2], sn = rope[(p * (hd / 2) + i) * 2 + 1];
+  if (h < Hq) {
+    const __half* src = qkv + (int64_t)r * W + h * hd + 2 * i;
+    const float x0 = __half2float(src[0]), x1 = __half2float(src[1]);
+    __half* dst = q_out + (int64_t)r * Hq * hd + h * hd + 2 * i;
+    dst[0] = __float2half_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    dst[1] = __float2half_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+  } else {
+    const int kh = h - Hq;
+    const __half* src = qkv + (int64_t)r * W + (Hq + kh) * hd + 2 * i;
+    const float x0 = __half2float(src[0]), x1 = __half2float(src[1]);
+    const int64_t dst = (((int64_t)b * Hk + kh) * L + p) * hd + 2 * i;
+    kc[dst] = __float2half_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    kc[dst + 1] = __float2half_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+    const __half* vs = qkv + (int64_t)r * W + (Hq + Hk + kh) * hd + 2 * i;
+    vc[dst] = vs[0];
+    vc[dst + 1] = vs[1];
+  }
+}
+
+// ------------------------------------------------------------------ SiLU * mul
+__global__ void silu_mul_kernel(const __half* __restrict__ a, __half* __restrict__ y, int F) {
+  const int r = blockIdx.x;
+  const int c = blockIdx.y * 256 + threadIdx.x;
+  if (c >= F) return;
+  const float af = __half2float(a[(int64_t)r * 2 * F + c]);
+  const __half s = __float2half_rn(__fdiv_rn(af, __fadd_rn(1.0f, expf(-af))));
+  y[(int64_t)r * F + c] = hmul_rn(s, a[(int64_t)r * 2 * F + F + c]);
+}
+
+// ------------------------------------------------------------------ int8 embedding gather
+__global__ void emb_gather_kernel(const int64_t* __restrict__ idx, const int8_t* __restrict__ tab,
+                                  const __half* __restrict__ scale, int64_t rows, int D, __half* __restrict__ out,
+                                  int* err) {
+  const int i = blockIdx.x;
+  const int64_t id = idx[i];
+  if (id < 0 || id >= rows) {
+    if (threadIdx.x == 0) report_error(err, HM_ERR_BADINDEX);
+    for (int k = threadIdx.x; k < D; k += blockDim.x) out[(int64_t)i * D + k] = __float2half_rn(0.f);
+    return;
+  }
+  const float s = __half2float(scale[id]);
+  for (int k = threadIdx.x; k < D; k += blockDim.x)
+    out[(int64_t)i * D + k] = __float2half_rn(static_cast<float>(tab[id * D + k]) * s);
+}
+
+// Sum of the n_cb codebook embeddings of each row (fp32 accumulation, one
+// rounding) and per-64-column sums of squares of the fp16 result.
+__global__ void __launch_bounds__(256) emb_sum_kernel(const int64_t* __restrict__ tok, int64_t tok_ld, int ncb,
+                                                      int64_t vocab, const int8_t* __restrict__ tab,
+                                                      const __half* __restrict__ scale, int64_t rows, int D,
+                                                      __half* __restrict__ x, float* __restrict__ ss, int64_t ss_ld,
+                                                      int* err) {
+  __shared__ float red[8];
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.y, tid = threadIdx.x;
+  const int k = blockIdx.x * 256 + tid;
+  float a = 0.f;
+  if (k < D) {
+    for (int c = 0; c < ncb; ++c) {
+      const int64_t id = tok[(int64_t)r * tok_ld + c] + c * vocab;
+      if (id < 0 || id >= rows) {
+        report_error(err, HM_ERR_BADINDEX);
+        continue;
+      }
+      a += __half2float(__float2half_rn(static_cast<float>(tab[id * D + k]) * __half2float(scale[id])));
+    }
+  }
+  const __half v = __float2half_rn(a);
+  if (k < D) x[(int64_t)r * D + k] = v;
+  if (ss) {
+    const float vf = k < D ? __half2float(v) : 0.f;
+    const float q = warp_sum(vf * vf);
+    if ((tid & 31) == 0) red[tid >> 5] = q;
+    __syncthreads();
+    if (tid < 4) {
+      const int t = blockIdx.x * 4 + tid;
+      if (t * 64 < D) ss[(int64_t)t * ss_ld + r] = red[2 * tid] + red[2 * tid + 1];
+    }
+  }
+}
+
+// ------------------------------------------------------------------ frame commit
+// End of one decode frame: tok_in <- tok_out (next frame's input), stream[f] <-
+// tok_out[:n_keep], pos += 1 for every row, frame counter += 1.
+__global__ void frame_commit_kernel(const int64_t* __restrict__ tok_out, int64_t* __restrict__ tok_in, int B, int ncb,
+                                    int64_t* __restrict__ pos, int n_keep, int64_t* __restrict__ stream,
+                                    int64_t* __restrict__ frame, int64_t max_frames) {
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x;
+  const int64_t f = *frame;
+  for (int i = tid; i < B * ncb; i += blockDim.x) {
+    const int64_t v = tok_out[i];
+    tok_in[i] = v;
+    const int b = i / ncb;
+    if (stream && b < n_keep && f >= 0 && f < max_frames) stream[f * n_keep * ncb + i] = v;
+  }
+  __syncthreads();
+  if (tid < B) pos[tid] += 1;
+  if (tid == 0) *frame = f + 1;
+}
+
+}  // namespace
+
+extern "C" int hm_rmsnorm(const void* x, const void* w, void* y, int R, int D, float eps, hm_stream_t stream) {
+  if (!x || !w || !y || R < 1 || D < 1) return HM_EARG;
+  rmsnorm_kernel<<<R, 256, 0, stream>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(w),
+                                        reinterpret_cast<__half*>(y), D, eps);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+extern "C" int hm_rope_kv_write(const void* qkv, const float* rope, int rope_rows, const int64_t* pos, void* q_out,
+                                void* kc, void* vc, int R, int S, int Hq, int Hk, int hd, int L, int* err,
+                                hm_stream_t stream) {
+  if (!qkv || !rope || !pos || !q_out || !kc || !vc || R < 1 || S < 1 || hd < 2 || hd % 2 || hd > 2048 || Hq < 1 ||
+      Hk < 1)
+    return HM_EARG;
+  rope_kv_kernel<<<dim3(R, Hq + Hk), hd / 2, 0, stream>>>(
+      reinterpret_cast<const __half*>(qkv), rope, rope_rows, pos, reinterpret_cast<__half*>(q_out),
+      reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), S, Hq, Hk, hd, L, err);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+extern "C" int hm_silu_mul(const void* a, void* y, int R, int F, hm_stream_t stream) {
+  if (!a || !y || R < 1 || F < 1) return HM_EARG;
+  silu_mul_kernel<<<dim3(R, (F + 255) / 256), 256, 0, stream>>>(reinterpret_cast<const __half*>(a),
+                                                               reinterpret_cast<__half*>(y), F);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+extern "C" int hm_emb_gather_i8(const int64_t* idx, int n, const int8_t* tab, const void* scale, int64_t rows, int D,
+                                void* out, int* err, hm_stream_t stream) {
+  if (!idx || !tab || !scale || !out || n < 1 || D < 1) return HM_EARG;
+  emb_gather_kernel<<<n, 256, 0, stream>>>(idx, tab, reinterpret_cast<const __half*>(scale), rows, D,
+                                           reinterpret_cast<__half*>(out), err);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+extern "C" int hm_emb_sum_i8(const int64_t* tok, int64_t tok_ld, int R, int ncb, int64_t vocab, const int8_t* tab,
+                             const void* scale, int64_t rows, int D, void* x_out, float* ss_out, int64_t ss_ld,
+                             int* err, int pdl, hm_stream_t stream) {
+  if (!tok || !tab || !scale || !x_out || R < 1 || ncb < 1 || D < 1 || (ss_out && D % 64)) return HM_EARG;
+  const cudaError_t e = hm_launch(emb_sum_kernel, dim3((D + 255) / 256, R), dim3(256), 0, stream, pdl, tok, tok_ld,
+                                  ncb, vocab, tab, reinterpret_cast<const __half*>(scale), rows, D,
+                                  reinterpret_cast<__half*>(x_out), ss_out, ss_ld, err);
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+extern "C" int hm_frame_commit(const int64_t* tok_out, int64_t* tok_in, int B, int ncb, int64_t* pos, int n_keep,
+                               int64_t* stream_out, int64_t* frame, int64_t max_frames, int pdl, hm_stream_t stream) {
+  if (!tok_out || !tok_in || !pos || !frame || B < 1 || B > 1024 || ncb < 1) return HM_EARG;
+  const cudaError_t e = hm_launch(frame_commit_kernel, dim3(1), dim3(256), 0, stream, pdl, tok_out, tok_in, B, ncb,
+                                  pos, n_keep, stream_out, frame, max_frames);
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}

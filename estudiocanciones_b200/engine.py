@@ -1,0 +1,676 @@
+"""HeartMuLa decode engine on B200: the drop-in for ``app/engine.py``'s hot path.
+
+Keeps the reference engine's call surface (``HeartMuLaLite(weights, device,
+dtype)``, ``generate``, ``_step``, ``_frame_fast``, ``Stack.decode``,
+``Linear``/``Emb``/``fuse``, ``release``, ``vram_weights``), its static KV-cache
+layout (``kc/vc [B, Hk, L, hd]`` fp16 per layer, ``app/engine.py:119-121``)
+and its int8 checkpoint format (``app/convert_final.py:32-47``).
+
+What changes underneath: one frame (3B backbone step, 7 local-decoder passes,
+8 codebook heads, CFG sampling) is a fixed list of launches of the sm_100a
+library — per transformer layer two RMSNorm-fused GEMVs, a RoPE+KV-writing
+GEMV, split-K decode attention and a residual GEMV — built once per batch size
+as a :class:`FramePlan` over static buffers, and captured as ONE CUDA graph.
+Positions live on the device, so the same graph serves the whole song; the
+frame's tokens, the output stream and the position advance are committed on
+the device, so the host loop only replays the graph (plus the reference's
+every-25-frames EOS check).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from pathlib import Path
+
+import torch
+
+from . import _lib, kernels
+from ._lib import GemvDesc, RowSrc, check, HM_EPI_STORE, HM_EPI_ROPE_KV, HM_EPI_SILU, HM_SRC_F16, HM_SRC_RMS, HM_SRC_EMB
+from .checkpoint import (AUDIO_EOS, AUDIO_VOCAB, FRAME_MS, N_CB, TEXT_BOS, TEXT_EOS, load_tensors,
+                         shape_from_tensors)
+from .prefill import prefill_backbone
+from .rope import rope_table
+
+EPS = 1e-5
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+# ----------------------------------------------------------------------------- layers
+class Linear:
+    """int8 per-output-channel weight (``app/engine.py:62-79``): ``q8 [N, K]`` int8, ``s8 [N]`` fp16."""
+
+    def __init__(self, q8: torch.Tensor, s8: torch.Tensor):
+        self.q8 = q8.contiguous()
+        self.s8 = s8.to(torch.float16).contiguous()
+
+    @property
+    def N(self):
+        return self.q8.shape[0]
+
+    @property
+    def K(self):
+        return self.q8.shape[1]
+
+    def __call__(self, x, res=None):
+        return kernels.int8_mm(x, self.q8, self.s8, res)
+
+    @property
+    def nbytes(self):
+        return self.q8.numel() + self.s8.numel() * 2
+
+
+def fuse(parts):
+    """Concatenate layers that read the same input (q|k|v, w1|w3) along N (``app/engine.py:82-86``)."""
+    return Linear(torch.cat([p.q8 for p in parts]), torch.cat([p.s8 for p in parts]))
+
+
+class Emb:
+    """int8 per-row embedding table (``app/engine.py:89-104``)."""
+
+    def __init__(self, q8, s8):
+        self.q8 = q8.contiguous()
+        self.s8 = s8.to(torch.float16).contiguous()
+
+    def __call__(self, idx):
+        return kernels.emb_i8(idx, self.q8, self.s8)
+
+    @property
+    def nbytes(self):
+        return self.q8.numel() + self.s8.numel() * 2
+
+
+class Block:
+    def __init__(self, get, pre, heads):
+        self.qkv = fuse([get(pre + f"attn.{n}_proj.weight") for n in ("q", "k", "v")])
+        self.o = get(pre + "attn.output_proj.weight")
+        self.w13 = fuse([get(pre + "mlp.w1.weight"), get(pre + "mlp.w3.weight")])
+        self.w2 = get(pre + "mlp.w2.weight")
+        self.n1 = get(pre + "sa_norm.scale", norm=True)
+        self.n2 = get(pre + "mlp_norm.scale", norm=True)
+        self.dim = self.n1.numel()
+        self.h = heads
+        self.hd = self.dim // heads
+        self.kvh = (self.qkv.N - heads * self.hd) // (2 * self.hd)
+        self.ffn = self.w13.N // 2
+        self.kc = self.vc = None
+
+    def alloc(self, B, L, dev):
+        self.kc = torch.zeros(B, self.kvh, L, self.hd, device=dev, dtype=torch.float16)
+        self.vc = torch.zeros_like(self.kc)
+
+
+class Stack:
+    def __init__(self, get, prefix, heads, tensors):
+        n = 0
+        while f"{prefix}.layers.{n}.sa_norm.scale" in tensors:
+            n += 1
+        self.blocks = [Block(get, f"{prefix}.layers.{i}.", heads) for i in range(n)]
+        self.norm = get(f"{prefix}.norm.scale", norm=True)
+        self.dim = self.norm.numel()
+        self.hd = self.blocks[0].hd
+        self.rope = None
+
+    def alloc(self, B, L, dev):
+        self.rope = rope_table(self.hd, max(L, 16)).to(dev)
+        for b in self.blocks:
+            b.alloc(B, L, dev)
+
+    def free(self):
+        for b in self.blocks:
+            b.kc = b.vc = None
+
+    @property
+    def L(self):
+        return self.blocks[0].kc.shape[2]
+
+    def decode(self, x, pos, S, nsplit=None):
+        """``Stack.decode`` (``app/engine.py:180-211``): x ``[R, D]`` fp16, row r -> batch r // S,
+        pos ``[R]`` int64 on the device.  Returns ``rms(x_out, norm)``; caches are updated in place."""
+        R = x.shape[0]
+        ns = nsplit or default_nsplit(R, self.blocks[0].kvh, self.L)
+        L = _lib.lib()
+        g = max(max(L.hm_gemv_workspace_bytes(R, b.qkv.N, b.qkv.K, HM_EPI_ROPE_KV, 0),
+                    L.hm_gemv_workspace_bytes(R, b.o.N, b.o.K, HM_EPI_STORE, 0),
+                    L.hm_gemv_workspace_bytes(R, b.w13.N, b.w13.K, HM_EPI_SILU, 0),
+                    L.hm_gemv_workspace_bytes(R, b.w2.N, b.w2.K, HM_EPI_STORE, 0)) for b in self.blocks)
+        ctx = _Ctx(x.device, g, L.hm_decode_attn_workspace_bytes(R, self.blocks[0].h, self.hd, ns))
+        bufs = StackBuffers(self, R, x.device)
+        bufs.x.copy_(x)
+        plan = FramePlan(ctx)
+        plan.sumsq(bufs.x, bufs.ss, R)
+        plan.stack(self, bufs, pos, S, R, ns)
+        plan.run()
+        return kernels.rms(bufs.x, self.norm)
+
+
+# ----------------------------------------------------------------------------- buffers and plan
+def default_nsplit(R, Hk, L, sms=None):
+    """Split count for decode attention: about two CTAs per SM, at most one split per 32 positions."""
+    if sms is None:
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return int(max(1, min(math.ceil(2 * sms / max(1, R * Hk)), max(1, L // 32), 64)))
+
+
+class _Ctx:
+    """Per-device scratch shared by every launch of a plan (launches are stream-ordered)."""
+
+    def __init__(self, device, ws_bytes=1 << 20, attn_ws_bytes=1 << 20):
+        self.dev = torch.device(device)
+        self.tickets = kernels.tickets(self.dev)
+        self.err = kernels.error_word(self.dev)
+        self.ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=self.dev)
+        self.attn_ws = torch.empty(max(attn_ws_bytes, 16), dtype=torch.uint8, device=self.dev)
+        # GEMV tickets [0, 32768); attention tickets [32768, 65536)
+        self.gemv_tk = self.tickets.data_ptr()
+        self.attn_tk = self.tickets[32768:].data_ptr()
+
+    def need(self, gemv_bytes, attn_bytes):
+        """Descriptors capture the scratch pointers, so scratch never grows after
+        the first launch is planned: size it with :meth:`reserve` first."""
+        if gemv_bytes > self.ws.numel() or attn_bytes > self.attn_ws.numel():
+            raise _lib.HMError(f"scratch too small ({gemv_bytes}, {attn_bytes}); call _Ctx.reserve first")
+
+    def reserve(self, model, B, nsplit):
+        """Size the scratch for every launch of a frame with B rows (2B in decoder pass 0)."""
+        L = _lib.lib()
+        g = 0
+        for st, rows in ((model.backbone, (B,)), (model.decoder, (B, 2 * B))):
+            for M in rows:
+                for b in st.blocks:
+                    g = max(g, L.hm_gemv_workspace_bytes(M, b.qkv.N, b.qkv.K, HM_EPI_ROPE_KV, 0),
+                            L.hm_gemv_workspace_bytes(M, b.o.N, b.o.K, HM_EPI_STORE, 0),
+                            L.hm_gemv_workspace_bytes(M, b.w13.N, b.w13.K, HM_EPI_SILU, 0),
+                            L.hm_gemv_workspace_bytes(M, b.w2.N, b.w2.K, HM_EPI_STORE, 0))
+        for lin, M in [(model.c0_head, B), (model.projection, B), (model.projection, 2 * B)] + \
+                [(h, B) for h in model.audio_head]:
+            g = max(g, L.hm_gemv_workspace_bytes(M, lin.N, lin.K, HM_EPI_STORE, 0))
+        b0 = model.backbone.blocks[0]
+        a = L.hm_decode_attn_workspace_bytes(B, b0.h, b0.hd, nsplit)
+        if g > self.ws.numel():
+            self.ws = torch.empty(g, dtype=torch.uint8, device=self.dev)
+        if a > self.attn_ws.numel():
+            self.attn_ws = torch.empty(a, dtype=torch.uint8, device=self.dev)
+
+
+class StackBuffers:
+    """Residual stream, its per-64-column sums of squares, and per-layer scratch of one stack."""
+
+    def __init__(self, stack: Stack, rows: int, dev):
+        b0 = stack.blocks[0]
+        D = stack.dim
+        self.rows = rows
+        self.x = torch.zeros(rows, D, device=dev, dtype=torch.float16)
+        self.ss = torch.zeros(D // 64, rows, device=dev, dtype=torch.float32)
+        self.q = torch.empty(rows, b0.h * b0.hd, device=dev, dtype=torch.float16)
+        self.o = torch.empty_like(self.q)
+        self.mm = torch.empty(rows, b0.ffn, device=dev, dtype=torch.float16)
+
+
+class FramePlan:
+    """An ordered list of launches on fixed buffers.  ``run()`` issues them on the
+    current stream; running it inside ``torch.cuda.graph`` captures the frame."""
+
+    def __init__(self, ctx: _Ctx, pdl: bool = True):
+        self.ctx = ctx
+        self.ops = []
+        self.pdl = int(pdl)
+        self._keep = []
+        self.n_kernels = 0
+
+    def run(self):
+        st = torch.cuda.current_stream().cuda_stream
+        for op in self.ops:
+            op(st)
+
+    # ------------------------------------------------------------------ primitives
+    def _gemv(self, lin: Linear, M, src0, src1=None, epi=HM_EPI_STORE, y=None, res=None, ss_out=None,
+              rope=None, pos=None, S=1, blk: Block | None = None, q_out=None, kspan=0):
+        L = _lib.lib()
+        d = GemvDesc()
+        d.w, d.s, d.N, d.K, d.M = lin.q8.data_ptr(), lin.s8.data_ptr(), lin.N, lin.K, M
+        d.src[0] = src0
+        if src1 is not None:
+            d.src[1] = src1
+            d.interleave = 1
+        d.epi = epi
+        if y is not None:
+            d.y, d.ldy = y.data_ptr(), y.stride(0)
+        if res is not None:
+            d.res, d.ldres = res.data_ptr(), res.stride(0)
+        if ss_out is not None:
+            d.ss_out, d.ss_out_ld = ss_out.data_ptr(), ss_out.stride(0)
+        if epi == HM_EPI_ROPE_KV:
+            d.rope, d.rope_rows, d.pos = rope.data_ptr(), rope.shape[0], pos.data_ptr()
+            d.S, d.Hq, d.Hk, d.hd, d.L = S, blk.h, blk.kvh, blk.hd, blk.kc.shape[2]
+            d.q_out, d.kc, d.vc = q_out.data_ptr(), blk.kc.data_ptr(), blk.vc.data_ptr()
+        wsb = L.hm_gemv_workspace_bytes(M, lin.N, lin.K, epi, kspan)
+        self.ctx.need(wsb, 0)
+        d.ws, d.ws_bytes = self.ctx.ws.data_ptr(), self.ctx.ws.numel()
+        d.counters, d.n_counters = self.ctx.gemv_tk, 32768
+        d.err, d.kspan, d.pdl = self.ctx.err.data_ptr(), kspan, self.pdl
+        self._keep.append(d)
+        ref = C.byref(d)
+        fn = L.hm_gemv_i8_fused
+        self.ops.append(lambda st: check(fn(ref, st), "hm_gemv_i8_fused"))
+        self.n_kernels += 1
+
+    @staticmethod
+    def src_f16(x, row_mul=1, row_add=0):
+        s = RowSrc()
+        s.mode, s.row_mul, s.row_add, s.x, s.ldx = HM_SRC_F16, row_mul, row_add, x.data_ptr(), x.stride(0)
+        return s
+
+    @staticmethod
+    def src_rms(x, ss, gamma, row_mul=1, row_add=0):
+        s = RowSrc()
+        s.mode, s.row_mul, s.row_add, s.x, s.ldx = HM_SRC_RMS, row_mul, row_add, x.data_ptr(), x.stride(0)
+        s.ss, s.ss_tiles, s.ss_ld = ss.data_ptr(), ss.shape[0], ss.stride(0)
+        s.gamma, s.eps, s.dim = gamma.data_ptr(), EPS, x.shape[1]
+        return s
+
+    @staticmethod
+    def src_emb(emb: Emb, tok, col, off, row_mul=1, row_add=0):
+        s = RowSrc()
+        s.mode, s.row_mul, s.row_add = HM_SRC_EMB, row_mul, row_add
+        s.etab, s.escale, s.erows = emb.q8.data_ptr(), emb.s8.data_ptr(), emb.q8.shape[0]
+        s.tok, s.tok_ld, s.tok_col, s.tok_off = tok.data_ptr(), tok.stride(0), col, off
+        return s
+
+    def sumsq(self, x, ss, R):
+        """ss partials of an fp16 matrix that no fused producer wrote (API entry points)."""
+        def op(st, x=x, ss=ss, R=R):
+            D = x.shape[1]
+            part = (x[:R].float() ** 2).reshape(R, D // 64, 64).sum(-1)
+            ss[:, :R].copy_(part.t())
+        self.ops.append(op)
+
+    def attn(self, blk: Block, q, o, pos, S, R, nsplit):
+        L = _lib.lib()
+        wsb = L.hm_decode_attn_workspace_bytes(R, blk.h, blk.hd, nsplit)
+        self.ctx.need(0, wsb)
+        args = (q.data_ptr(), blk.kc.data_ptr(), blk.vc.data_ptr(), pos.data_ptr(), o.data_ptr(), R, S, blk.h,
+                blk.kvh, blk.hd, blk.kc.shape[2], 1.0 / math.sqrt(blk.hd), nsplit, self.ctx.attn_ws.data_ptr(),
+                self.ctx.attn_ws.numel(), self.ctx.attn_tk, 32768, self.ctx.err.data_ptr(), self.pdl)
+        fn = L.hm_decode_attn
+        self.ops.append(lambda st: check(fn(*args, st), "hm_decode_attn"))
+        self.n_kernels += 1
+
+    # ------------------------------------------------------------------ composites
+    def stack(self, stack: Stack, bufs: StackBuffers, pos, S, R, nsplit):
+        """The per-layer loop of ``Stack.decode`` with everything fused into 5 launches per layer.
+        Expects ``bufs.x`` and its ss partials in ``bufs.ss``; leaves the (un-normalised)
+        output in ``bufs.x`` with fresh ss partials."""
+        for b in stack.blocks:
+            self._gemv(b.qkv, R, self.src_rms(bufs.x, bufs.ss, b.n1), epi=HM_EPI_ROPE_KV, rope=stack.rope,
+                       pos=pos, S=S, blk=b, q_out=bufs.q)
+            self.attn(b, bufs.q, bufs.o, pos, S, R, nsplit)
+            self._gemv(b.o, R, self.src_f16(bufs.o), y=bufs.x, res=bufs.x, ss_out=bufs.ss)
+            self._gemv(b.w13, R, self.src_rms(bufs.x, bufs.ss, b.n2), epi=HM_EPI_SILU, y=bufs.mm)
+            self._gemv(b.w2, R, self.src_f16(bufs.mm), y=bufs.x, res=bufs.x, ss_out=bufs.ss)
+
+    def emb_sum(self, emb: Emb, tok, R, ncb, vocab, x, ss):
+        L = _lib.lib()
+        args = (tok.data_ptr(), tok.stride(0), R, ncb, vocab, emb.q8.data_ptr(), emb.s8.data_ptr(), emb.q8.shape[0],
+                x.shape[1], x.data_ptr(), ss.data_ptr(), ss.stride(0), self.ctx.err.data_ptr(), self.pdl)
+        fn = L.hm_emb_sum_i8
+        self.ops.append(lambda st: check(fn(*args, st), "hm_emb_sum_i8"))
+        self.n_kernels += 1
+
+    def sample(self, logits, n_takes, cfg, topk, temp, noise, out, col):
+        L = _lib.lib()
+        B, V = logits.shape
+        args = (logits.data_ptr(), logits.stride(0), B, n_takes, V, noise.data_ptr(), noise.stride(0), float(cfg),
+                int(topk), float(temp), out.data_ptr(), out.stride(0), col, self.ctx.err.data_ptr(), self.pdl)
+        fn = L.hm_cfg_topk_sample
+        self.ops.append(lambda st: check(fn(*args, st), "hm_cfg_topk_sample"))
+        self.n_kernels += 1
+
+    def commit(self, tok_out, tok_in, pos, n_keep, stream, frame):
+        L = _lib.lib()
+        B, ncb = tok_out.shape
+        args = (tok_out.data_ptr(), tok_in.data_ptr(), B, ncb, pos.data_ptr(), n_keep, _p(stream), frame.data_ptr(),
+                0 if stream is None else stream.shape[0], self.pdl)
+        fn = L.hm_frame_commit
+        self.ops.append(lambda st: check(fn(*args, st), "hm_frame_commit"))
+        self.n_kernels += 1
+
+    def torch_op(self, f):
+        self.ops.append(lambda st: f())
+
+
+# ----------------------------------------------------------------------------- model
+class HeartMuLaLite:
+    """B200 engine with the reference's interface (``app/engine.py:215-477``)."""
+
+    def __init__(self, weights, device="cuda", dtype=None, bb_heads: int = 24, dec_heads: int = 8):
+        self.dev = torch.device(device)
+        if self.dev.type != "cuda":
+            raise _lib.HMError("the B200 engine runs on CUDA devices only")
+        if dtype not in (None, torch.float16):
+            raise _lib.HMError("the decode kernels compute in fp16 (the reference's GPU dtype)")
+        self.dt = torch.float16
+        self.fast = True
+        _lib.lib()
+        t = load_tensors(weights, device=self.dev)
+        self.shape = shape_from_tensors(t, bb_heads, dec_heads)
+
+        def get(name, norm=False):
+            if norm:
+                return t[name].to(torch.float16).contiguous()
+            return Linear(t[name + ".q8"], t[name + ".s8"])
+
+        self.backbone = Stack(get, "backbone", bb_heads, t)
+        self.decoder = Stack(get, "decoder", dec_heads, t)
+        self.text_emb = Emb(t["text_embeddings.weight.q8"], t["text_embeddings.weight.s8"])
+        self.audio_emb = Emb(t["audio_embeddings.weight.q8"], t["audio_embeddings.weight.s8"])
+        self.uncond = t["unconditional_text_embedding.weight"].to(torch.float16)
+        self.projection = get("projection.weight")
+        self.c0_head = get("codebook0_head.weight")
+        self.audio_head = [get(f"audio_head.{i}") for i in range(self.shape.n_cb - 1)]
+        self.muq_b = t["muq_linear.bias"].to(torch.float16)
+        self.vocab = self.c0_head.N
+        self.n_cb = self.shape.n_cb
+        self.cb_off = torch.arange(self.n_cb, device=self.dev) * self.vocab
+        self.graphs = {}
+        self._rt = None
+        del t
+
+    # ------------------------------------------------------------------ runtime state
+    def alloc(self, n_takes, B, L):
+        """Caches (``app/engine.py:386-388``), frame buffers and the frame plan."""
+        self.N, self.B = n_takes, B
+        self.backbone.alloc(B, L, self.dev)
+        self.decoder.alloc(B, self.n_cb, self.dev)
+        self._rt = _Runtime(self, n_takes, B)
+
+    def release(self):
+        """Free caches, graphs and buffers (``app/engine.py:463-469``)."""
+        self.graphs.clear()
+        self._rt = None
+        self.backbone.free()
+        self.decoder.free()
+        torch.cuda.empty_cache()
+
+    def vram_weights(self):
+        tot = 0
+        for st in (self.backbone, self.decoder):
+            for b in st.blocks:
+                tot += sum(l.nbytes for l in (b.qkv, b.o, b.w13, b.w2))
+        tot += self.audio_emb.nbytes + sum(l.nbytes for l in self.audio_head) + self.c0_head.nbytes
+        return tot + self.projection.nbytes
+
+    # ------------------------------------------------------------------ reference-shaped entry points
+    def _step(self, tok, pos, bucket=None, cfg=1.5, topk=50, temp=1.0):
+        """One frame from the previous frame's tokens ``tok [B, 8]`` at ``pos [B, 1]``
+        (``app/engine.py:345-349``).  Returns ``[B, 8]`` int64 (a static buffer)."""
+        rt = self._rt
+        rt.tok_in.copy_(tok)
+        rt.pos.copy_(pos.reshape(-1))
+        rt.plan_for(cfg, topk, temp, with_backbone=True, commit=False).run()
+        return rt.tok_out
+
+    def _frame_fast(self, last_h, cfg=1.5, topk=50, temp=1.0):
+        """Codebook heads + local decoder from the backbone's normalised state ``last_h [B, D]``
+        (``app/engine.py:328-343``)."""
+        rt = self._rt
+        rt.x_bb.copy_(last_h)
+        rt.plan_for(cfg, topk, temp, with_backbone=False, commit=False, normed_input=True).run()
+        return rt.tok_out
+
+    # ------------------------------------------------------------------ teacher forcing (parity harness)
+    @torch.inference_mode()
+    def prefill_ids(self, text, muq_idx, n_takes, B, L):
+        """Allocate for ``B`` rows and a ``L``-slot cache, then run the prompt prefill
+        (``app/engine.py:383-398``); the last position's hidden state stays in the runtime."""
+        self.alloc(n_takes, B, L)
+        text_d = text.to(self.dev).long()
+        h = self.text_emb(text_d).unsqueeze(0).repeat(B, 1, 1)
+        h[:n_takes, muq_idx] = self.muq_b
+        if B == 2 * n_takes:
+            h[n_takes:] = self.uncond[0]
+        prefill_backbone(self, h)
+        self._rt.pos.fill_(int(text.numel()))
+
+    @torch.inference_mode()
+    def teacher_frame(self, force, with_backbone, tok=None, pos=None, cfg=1.5, topk=50, temp=1.0, graph=False):
+        """One frame with the sampled ids replaced by ``force [B, n_cb]``; returns the raw
+        fp16 logits of every codebook head ``[n_cb, B, V]``.  Without the backbone the
+        frame starts from the prefill's last hidden state."""
+        rt = self._rt
+        rt.force.copy_(force)
+        if tok is not None:
+            rt.tok_in.copy_(tok)
+        if pos is not None:
+            rt.pos.copy_(pos.reshape(-1))
+        plan = rt.plan_for(cfg, topk, temp, with_backbone=with_backbone, commit=False, teacher=True)
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream(device=self.dev)
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                with torch.cuda.graph(g, stream=st):
+                    plan.run()
+            torch.cuda.current_stream().wait_stream(st)
+            g.replay()
+        else:
+            plan.run()
+        return rt.rec.clone()
+
+    # ------------------------------------------------------------------ prompt (app/engine.py:357-372)
+    @staticmethod
+    def _prompt(lyrics, tags, tokenizer):
+        tags = tags.lower()
+        if not tags.startswith("<tag>"):
+            tags = "<tag>" + tags
+        if not tags.endswith("</tag>"):
+            tags = tags + "</tag>"
+        t_ids = tokenizer.encode(tags).ids
+        l_ids = tokenizer.encode(lyrics.lower()).ids
+        for ids in (t_ids, l_ids):
+            if ids[0] != TEXT_BOS:
+                ids.insert(0, TEXT_BOS)
+            if ids[-1] != TEXT_EOS:
+                ids.append(TEXT_EOS)
+        return torch.tensor(t_ids + [0] + l_ids), len(t_ids)
+
+    @torch.inference_mode()
+    def generate(self, lyrics, tags, tokenizer, *, max_ms=60_000, temperature=1.0, topk=50, cfg_scale=1.5,
+                 seed=None, use_graphs=True, progress=None, abort=None, n=1):
+        """Reference ``generate`` (``app/engine.py:374-448``): ``[8, T]`` per take."""
+        text, muq_idx = self._prompt(lyrics, tags, tokenizer)
+        return self.generate_ids(text, muq_idx, max_ms=max_ms, temperature=temperature, topk=topk,
+                                 cfg_scale=cfg_scale, seed=seed, use_graphs=use_graphs, progress=progress,
+                                 abort=abort, n=n)
+
+    @torch.inference_mode()
+    def generate_ids(self, text, muq_idx, *, max_ms=60_000, temperature=1.0, topk=50, cfg_scale=1.5, seed=None,
+                     use_graphs=True, progress=None, abort=None, n=1, check_every=25, stop_at_eos=True,
+                     fixed_noise=False):
+        """``generate`` from prompt token ids (host or device int64 ``[P]``).
+        ``fixed_noise`` replaces the exponential noise by ones (greedy within top-k),
+        which makes runs independent of the random stream (tests)."""
+        if seed is not None and seed >= 0:
+            torch.manual_seed(seed)
+        N = n
+        B = 2 * N if cfg_scale != 1.0 else N
+        P = int(text.numel())
+        n_frames = max_ms // FRAME_MS
+        L = P + n_frames + 2
+        self.alloc(N, B, L + 256)
+        rt = self._rt
+        text_d = text.to(self.dev, non_blocking=True).long()
+        # prompt embeddings: int8 text gather on the GPU, muq bias, unconditional rows
+        te = self.text_emb(text_d)
+        h = te.unsqueeze(0).repeat(B, 1, 1)
+        h[:N, muq_idx] = self.muq_b
+        if B == 2 * N:
+            h[N:] = self.uncond[0]
+        prefill_backbone(self, h)
+        rt.draw_noise = not fixed_noise
+        rt.stream_out.zero_()
+        rt.frame.zero_()
+        rt.pos.fill_(P)
+        plan0 = rt.plan_for(cfg_scale, topk, temperature, with_backbone=False, commit=True)
+        plan0.run()            # first frame from the prompt's last hidden state
+        g = rt.graph_for(cfg_scale, topk, temperature) if use_graphs else None
+        cur = 0
+        ends = [None] * N
+        last = n_frames
+        for i in range(n_frames):
+            if abort and abort():
+                self.release()
+                return None
+            if g is not None:
+                g.replay()
+            else:
+                rt.plan_for(cfg_scale, topk, temperature, with_backbone=True, commit=True).run()
+            cur = i + 1
+            if (i + 1) % check_every == 0 or i == n_frames - 1:
+                a = max(1, i + 2 - check_every)
+                eos = (rt.stream_out[a:i + 2] >= AUDIO_EOS).any(-1).cpu()
+                for c in range(N):
+                    if ends[c] is None and eos[:, c].any():
+                        ends[c] = a + int(eos[:, c].nonzero()[0, 0])
+                if stop_at_eos and all(e is not None for e in ends):
+                    last = i + 1
+                    break
+                if progress:
+                    progress((i + 1) * FRAME_MS / 1000, max_ms / 1000)
+        del cur
+        res = []
+        for c in range(N):
+            T = ends[c] if ends[c] is not None else last + 1
+            res.append(rt.stream_out[:T, c].t().clone())
+        self.release()
+        return res[0] if n == 1 else res
+
+
+class _Runtime:
+    """Static buffers of one (takes, rows) configuration and the plans/graphs over them."""
+
+    def __init__(self, m: HeartMuLaLite, N, B):
+        dev = m.dev
+        self.m, self.N, self.B = m, N, B
+        self.ctx = _Ctx(dev)
+        self.bb = StackBuffers(m.backbone, B, dev)
+        self.dec = StackBuffers(m.decoder, 2 * B, dev)
+        self.x_bb, self.ss_bb = self.bb.x, self.bb.ss
+        self.tok_in = torch.zeros(B, m.n_cb, dtype=torch.long, device=dev)
+        self.tok_out = torch.zeros(B, m.n_cb, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.long, device=dev)
+        self.dpos0 = torch.arange(2, device=dev).repeat(B)
+        self.dpos = [torch.full((B,), i, dtype=torch.long, device=dev) for i in range(m.n_cb)]
+        self.logits = torch.empty(B, m.vocab, dtype=torch.float16, device=dev)
+        self.noise = torch.ones(m.n_cb, N, m.vocab, dtype=torch.float32, device=dev)
+        L = m.backbone.L
+        self.max_frames = L
+        self.stream_out = torch.zeros(L, N, m.n_cb, dtype=torch.long, device=dev)
+        self.frame = torch.zeros(1, dtype=torch.long, device=dev)
+        self.nsplit = default_nsplit(B, m.backbone.blocks[0].kvh, L)
+        self.plans = {}
+        self.graphs = {}
+        self.noise_stream = torch.cuda.Stream(device=dev)
+        self.draw_noise = True
+        self.pdl = True
+        self.force = torch.zeros(B, m.n_cb, dtype=torch.long, device=dev)
+        self.rec = torch.zeros(m.n_cb, B, m.vocab, dtype=torch.float16, device=dev)
+        self.ctx.reserve(m, B, self.nsplit)
+
+    def _noise_ops(self, plan: FramePlan):
+        """Exponential noise of the 8 samplers, drawn from torch's generator in the
+        reference's order (``app/engine.py:297``) on a side stream."""
+        noise, ns = self.noise, self.noise_stream
+
+        def fork():
+            ns.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(ns):
+                if self.draw_noise:
+                    for c in range(noise.shape[0]):
+                        noise[c].exponential_(1)
+
+        def join():
+            torch.cuda.current_stream().wait_stream(ns)
+        plan.torch_op(fork)
+        return join
+
+    def plan_for(self, cfg, topk, temp, with_backbone=True, commit=True, normed_input=False, teacher=False):
+        key = (float(cfg), int(topk), float(temp), with_backbone, commit, normed_input, teacher)
+        p = self.plans.get(key)
+        if p is None:
+            p = self._build(cfg, topk, temp, with_backbone, commit, normed_input, teacher)
+            self.plans[key] = p
+        return p
+
+    def graph_for(self, cfg, topk, temp):
+        key = (float(cfg), int(topk), float(temp))
+        g = self.graphs.get(key)
+        if g is None:
+            plan = self.plan_for(cfg, topk, temp, with_backbone=True, commit=True)
+            # one eager warm-up frame (as the reference's _capture does, app/engine.py:450-456);
+            # it writes the cache slot at the current position, which the replay rewrites
+            saved = (self.tok_in.clone(), self.pos.clone(), self.frame.clone())
+            plan.run()
+            self.tok_in.copy_(saved[0])
+            self.pos.copy_(saved[1])
+            self.frame.copy_(saved[2])
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(device=self.m.dev)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    plan.run()
+            torch.cuda.current_stream().wait_stream(s)
+            self.tok_in.copy_(saved[0])
+            self.pos.copy_(saved[1])
+            self.frame.copy_(saved[2])
+            self.graphs[key] = g
+        return g
+
+    def _build(self, cfg, topk, temp, with_backbone, commit, normed_input, teacher=False):
+        m = self.m
+        B, N = self.B, self.N
+        V = m.vocab
+        plan = FramePlan(self.ctx, pdl=self.pdl)
+        join = self._noise_ops(plan)
+        if teacher:
+            # teacher forcing: record every head's logits and take the forced ids
+            # instead of sampling (the parity harness of the tests)
+            def pick(c, *_):
+                def op(c=c):
+                    self.rec[c].copy_(self.logits)
+                    self.tok_out[:, c].copy_(self.force[:, c])
+                plan.torch_op(op)
+            sample = pick
+        else:
+            def sample(c, noise):
+                plan.sample(self.logits, N, cfg, topk, temp, noise, self.tok_out, c)
+        bb, dec = self.bb, self.dec
+        if with_backbone:
+            plan.emb_sum(m.audio_emb, self.tok_in, B, m.n_cb, V, bb.x, bb.ss)
+            plan.stack(m.backbone, bb, self.pos, 1, B, self.nsplit)
+        # last_h = rms(x_bb, backbone.norm), fused into the consumers' prologue; an
+        # already-normalised last_h (the _frame_fast entry point) is read as is
+        last_h = plan.src_f16(bb.x) if normed_input else plan.src_rms(bb.x, bb.ss, m.backbone.norm)
+        plan._gemv(m.c0_head, B, last_h, y=self.logits)
+        plan.torch_op(join)
+        sample(0, self.noise[0])
+        # decoder pass 0: rows (2b, 2b+1) = (last_h[b], emb(0, c0[b])) at positions (0, 1)
+        last_h = plan.src_f16(bb.x) if normed_input else plan.src_rms(bb.x, bb.ss, m.backbone.norm)
+        plan._gemv(m.projection, 2 * B, last_h,
+                   plan.src_emb(m.audio_emb, self.tok_out, 0, 0), y=dec.x, ss_out=dec.ss)
+        plan.stack(m.decoder, dec, self.dpos0, 2, 2 * B, 1)
+        plan._gemv(m.audio_head[0], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm, row_mul=2, row_add=1),
+                   y=self.logits)
+        sample(1, self.noise[1])
+        for c in range(2, m.n_cb):
+            plan._gemv(m.projection, B, plan.src_emb(m.audio_emb, self.tok_out, c - 1, (c - 1) * V),
+                       y=dec.x, ss_out=dec.ss)
+            plan.stack(m.decoder, dec, self.dpos[c], 1, B, 1)
+            plan._gemv(m.audio_head[c - 1], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm), y=self.logits)
+            sample(c, self.noise[c])
+        if commit:
+            plan.commit(self.tok_out, self.tok_in, self.pos, N, self.stream_out, self.frame)
+        return plan

@@ -1,0 +1,176 @@
+/*
+ * heartmula_b200.h — C ABI of the B200 (sm_100a) HeartMuLa decode-path library.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as `hm_stream_t`), launches on that stream, never allocates and
+ * never synchronises, so all of them can be captured into a CUDA graph.
+ * Each returns 0 on success, a cudaError_t value (> 0) when the launch failed,
+ * or HM_EARG (< 0) when an argument is out of the supported range.
+ *
+ * Device-side faults are not used for error reporting: kernels that can meet a
+ * bad index or a wait that never ends OR a bit (HM_ERR_*) into the caller's
+ * `err` word (a device int, may be NULL) and skip the access / return.
+ *
+ * Activations are fp16 (IEEE half stored as uint16), weights int8 row-major
+ * [N, K] with one fp16 scale per row, matching the reference checkpoint after
+ * its loader (app/engine.py:235-242 casts the bf16 scales to fp16).
+ */
+#ifndef HEARTMULA_B200_H
+#define HEARTMULA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* hm_stream_t; /* == cudaStream_t */
+
+/* host return codes */
+#define HM_OK 0
+#define HM_EARG (-1)
+
+/* device error-word bits */
+#define HM_ERR_TIMEOUT 1   /* a bounded wait gave up */
+#define HM_ERR_BADINDEX 2  /* token id / position outside its table; access skipped */
+
+/* ------------------------------------------------------------------ int8 GEMV
+ * y[m, n] = fp16( sum_k x[m,k] * w[n,k] * s[n] ) (+ res[m, n] in fp16),  M <= 32, K % 16 == 0.
+ * Replaces int8_mm / _gemv8 (app/kernels.py:20-54; M <= 16 branch, extended to 32).
+ * `ws`/`counters`: split-K scratch, sized by hm_gemv_workspace_bytes /
+ * hm_gemv_counters; counters must be zero before the first call and are left
+ * zero by every call.  kspan = 0 picks the split automatically. */
+int hm_gemv_i8(const void* x, int64_t ldx, const int8_t* w, const void* s, const void* res, int64_t ldres, void* y,
+               int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, int* counters, int n_counters, int* err,
+               int kspan, int pdl, hm_stream_t stream);
+
+/* Where the GEMV input rows come from (fused prologue). */
+#define HM_SRC_F16 0 /* x row as is */
+#define HM_SRC_RMS 1 /* RMSNorm of the x row: fp16(fp16(x*inv)*gamma), inv from ss partials (app/kernels.py:58-67) */
+#define HM_SRC_EMB 2 /* int8 embedding row fp16(q8[id]*s8[id]) with id = tok[...] + tok_off (app/engine.py:95-98) */
+
+typedef struct {
+  int mode;
+  int row_mul, row_add;         /* source row of output row m: m*row_mul + row_add */
+  const void* x;                /* F16/RMS: fp16 rows */
+  int64_t ldx;
+  const float* ss;              /* RMS: sum-of-squares partials ss[t*ss_ld + row], t < ss_tiles */
+  int ss_tiles;
+  int64_t ss_ld;
+  const void* gamma;            /* RMS: fp16 [K] */
+  float eps;
+  int dim;                      /* RMS: row width D (divisor of the mean) */
+  const int8_t* etab;           /* EMB: int8 table [erows, K] */
+  const void* escale;           /* EMB: fp16 [erows] */
+  int64_t erows;
+  const int64_t* tok;           /* EMB: id = tok[row*tok_ld + tok_col] + tok_off */
+  int64_t tok_ld;
+  int tok_col;
+  int64_t tok_off;
+} hm_row_src;
+
+#define HM_EPI_STORE 0   /* y = fp16(acc*s) (+res); optional per-64-column sum of squares */
+#define HM_EPI_ROPE_KV 1 /* fused qkv: RoPE q -> q_out, RoPE k / copy v -> cache slot pos (app/kernels.py:79-107) */
+#define HM_EPI_SILU 2    /* fused w1|w3: y[m,j] = fp16(silu(a)) * b (app/kernels.py:172-180) */
+
+typedef struct {
+  const int8_t* w;
+  const void* s;
+  int N, K, M;
+  hm_row_src src[2];
+  int interleave;               /* 1: row m takes src[m & 1] with local row m >> 1 */
+  int epi;
+  void* y;                      /* STORE/SILU output */
+  int64_t ldy;
+  const void* res;              /* STORE: optional residual (may alias y) */
+  int64_t ldres;
+  float* ss_out;                /* STORE: optional ss partials ss_out[tile*ss_out_ld + m] (N % 64 == 0) */
+  int64_t ss_out_ld;
+  const float* rope;            /* ROPE_KV: fp32 [rope_rows, hd/2, 2] */
+  int rope_rows;
+  const int64_t* pos;           /* ROPE_KV: absolute position of each row */
+  int S, Hq, Hk, hd, L;         /* ROPE_KV: rows per batch entry, heads, head dim, cache length */
+  void* q_out;                  /* ROPE_KV: fp16 [M, Hq*hd] */
+  void* kc;                     /* ROPE_KV: fp16 [B, Hk, L, hd] */
+  void* vc;
+  void* ws;                     /* split-K scratch */
+  size_t ws_bytes;
+  int* counters;
+  int n_counters;
+  int* err;
+  int kspan;                    /* 0 = automatic */
+  int pdl;                      /* launch with programmatic dependent launch */
+} hm_gemv_desc;
+
+/* The fused GEMV: prologue rows from `src`, epilogue per `epi`.  The per-layer
+ * decode path of Stack.decode (app/engine.py:180-211) is five of these plus
+ * hm_decode_attn. */
+int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream);
+
+/* Scratch needed by a GEMV of this shape (kspan = 0: the automatic choice). */
+size_t hm_gemv_workspace_bytes(int M, int N, int K, int epi, int kspan);
+int hm_gemv_counters(int N, int epi);
+/* The split actually used for a shape (for reporting). */
+int hm_gemv_pick_kspan(int M, int N, int K, int epi, int kspan);
+
+/* ------------------------------------------------------------------ small kernels */
+/* rms(x, w, eps) (app/kernels.py:58-74). x, y fp16 [R, D]; w fp16 [D]. */
+int hm_rmsnorm(const void* x, const void* w, void* y, int R, int D, float eps, hm_stream_t stream);
+
+/* _rope_cache (app/kernels.py:79-107): qkv [R, (Hq+2Hk)*hd] -> q_out [R, Hq*hd],
+ * kc/vc [B, Hk, L, hd] written at pos[r] for batch r / S. */
+int hm_rope_kv_write(const void* qkv, const float* rope, int rope_rows, const int64_t* pos, void* q_out, void* kc,
+                     void* vc, int R, int S, int Hq, int Hk, int hd, int L, int* err, hm_stream_t stream);
+
+/* _silu_mul (app/kernels.py:172-180): a [R, 2F] -> y [R, F]. */
+int hm_silu_mul(const void* a, void* y, int R, int F, hm_stream_t stream);
+
+/* Emb.__call__ int8 branch (app/engine.py:95-98): out[i] = fp16(q8[idx[i]] * s8[idx[i]]). */
+int hm_emb_gather_i8(const int64_t* idx, int n, const int8_t* tab, const void* scale, int64_t rows, int D, void* out,
+                     int* err, hm_stream_t stream);
+
+/* Backbone input of a frame (app/engine.py:348): x[r] = fp16(sum_c emb(tok[r,c] + c*vocab)),
+ * plus optional ss partials per 64 columns for the next fused RMSNorm. */
+int hm_emb_sum_i8(const int64_t* tok, int64_t tok_ld, int R, int ncb, int64_t vocab, const int8_t* tab,
+                  const void* scale, int64_t rows, int D, void* x_out, float* ss_out, int64_t ss_ld, int* err, int pdl,
+                  hm_stream_t stream);
+
+/* End of one decode frame (the bookkeeping of generate's loop, app/engine.py:419-431,
+ * kept on the device): tok_in <- tok_out, stream[frame] <- tok_out[:n_keep],
+ * pos[b] += 1, frame += 1.  tok_* are int64 [B, ncb]; stream int64 [max_frames, n_keep, ncb]. */
+int hm_frame_commit(const int64_t* tok_out, int64_t* tok_in, int B, int ncb, int64_t* pos, int n_keep,
+                    int64_t* stream_out, int64_t* frame, int64_t max_frames, int pdl, hm_stream_t stream);
+
+/* ------------------------------------------------------------------ decode attention
+ * _attn + _attn_combine (app/kernels.py:112-167): row r of batch r/S attends
+ * cache positions [0, pos[r]] with GQA (no KV copy); split over `nsplit`
+ * position ranges, the last CTA of each (row, kv head) merges the partials.
+ * q, o fp16 [R, Hq*hd]; kc, vc fp16 [B, Hk, L, hd]; hd in {64, 128, 256, 384}. */
+int hm_decode_attn(const void* q, const void* kc, const void* vc, const int64_t* pos, void* o, int R, int S, int Hq,
+                   int Hk, int hd, int L, float scale, int nsplit, void* ws, size_t ws_bytes, int* counters,
+                   int n_counters, int* err, int pdl, hm_stream_t stream);
+size_t hm_decode_attn_workspace_bytes(int R, int Hq, int hd, int nsplit);
+
+/* ------------------------------------------------------------------ sampler
+ * _guided + _sample (app/engine.py:291-305) for one codebook: optional CFG mix
+ * (rows [0,N) conditional, [N,2N) unconditional, fp16 arithmetic), /temp,
+ * top-k mask, softmax(log_softmax), argmax(p / noise).  The id is written to
+ * out[b*out_ld + out_col] for b = n and, with CFG, b = n + N. */
+int hm_cfg_topk_sample(const void* logits, int64_t ld_logits, int B, int N, int V, const float* noise,
+                       int64_t ld_noise, float cfg, int topk, float temp, int64_t* out, int64_t out_ld, int out_col,
+                       int* err, int pdl, hm_stream_t stream);
+
+/* ------------------------------------------------------------------ info */
+int hm_device_sm_count(int device);
+/* sizeof / offsetof of the descriptor structs, for bindings to verify their layout:
+ * 0 sizeof(hm_row_src), 1 sizeof(hm_gemv_desc), 2 offsetof(hm_gemv_desc, src),
+ * 3 offsetof(hm_gemv_desc, ws), 4 offsetof(hm_gemv_desc, pdl). */
+size_t hm_abi_layout(int which);
+const char* hm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HEARTMULA_B200_H */

@@ -1,0 +1,320 @@
+"""Kernel-level parity of the sm_100a library against the CPU oracle and the
+reference's golden vectors.  Every call goes through the C ABI."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import heartmula_oracle as O
+from estudiocanciones_b200._lib import HM_EPI_ROPE_KV, HM_EPI_SILU
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    from estudiocanciones_b200 import build, kernels
+    build.build()
+    kernels.read_errors(DEV)
+    yield
+    assert kernels.read_errors(DEV) == 0, "a kernel reported an error bit"
+
+
+def g(a):
+    return torch.from_numpy(np.array(a))
+
+
+def close16(out, ref, ulps=2, frac_exact=0.95):
+    """fp16 results equal up to `ulps` fp16 ulps (of the reference value), most of them exactly."""
+    o, r = out.float().cpu(), ref.float().cpu()
+    ulp = torch.clamp(2.0 ** (torch.floor(torch.log2(r.abs().clamp_min(2.0 ** -14))) - 10), min=2.0 ** -24)
+    bad = (o - r).abs() > ulps * ulp
+    assert int(bad.sum()) == 0, f"{int(bad.sum())} values off by > {ulps} ulp; max abs {float((o - r).abs().max())}"
+    assert (o == r).float().mean().item() >= frac_exact
+
+
+def rand_lin(N, K, gen):
+    w = torch.randint(-127, 128, (N, K), generator=gen, dtype=torch.int8)
+    s = (torch.randn(N, generator=gen).abs() * 0.02 / 127).half()
+    return w, s
+
+
+# ----------------------------------------------------------------------------- GEMV
+@pytest.mark.parametrize("i", range(5))
+def test_gemv_golden(golden, i):
+    from estudiocanciones_b200 import kernels
+    z = golden("kernels")
+    x, w, s, y = g(z[f"gemv{i}_x"]), g(z[f"gemv{i}_w"]), g(z[f"gemv{i}_s"]), g(z[f"gemv{i}_y"])
+    r = g(z[f"gemv{i}_r"]).to(DEV) if f"gemv{i}_r" in z else None
+    out = kernels.int8_mm(x.to(DEV), w.to(DEV), s.to(DEV), r)
+    close16(out, y, ulps=2, frac_exact=0.9)
+
+
+@pytest.mark.parametrize("M,N,K,kspan,res", [
+    (1, 64, 128, 0, False), (3, 200, 512, 128, True), (8, 5120, 3072, 0, False), (8, 3072, 8192, 1024, True),
+    (9, 1536, 1024, 256, False), (16, 8197, 3072, 0, False), (20, 1024, 3072, 512, True), (32, 3072, 1024, 0, True),
+    (8, 8197, 1024, 0, False), (1, 16384, 3072, 1024, False)])
+def test_gemv_matches_oracle(M, N, K, kspan, res):
+    from estudiocanciones_b200 import kernels
+    gen = torch.Generator().manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, generator=gen).half()
+    w, s = rand_lin(N, K, gen)
+    r = torch.randn(M, N, generator=gen).half() if res else None
+    out = kernels.int8_mm(x.to(DEV), w.to(DEV), s.to(DEV), r.to(DEV) if res else None, kspan=kspan)
+    # the oracle's M > 16 branch rounds w*s to fp16 first (the reference's cuBLAS path);
+    # the kernel keeps the exact int8 x fp16 product for every M, so compare with that
+    acc = x.float() @ w.float().t()
+    ref = (acc * s.float()).half()
+    if res:
+        ref = (ref.float() + r.float()).half()
+    close16(out, ref, ulps=2, frac_exact=0.9)
+    if M <= 16:
+        close16(out, O.gemv_i8(x, w, s, r), ulps=2, frac_exact=0.9)
+
+
+def test_gemv_is_deterministic():
+    from estudiocanciones_b200 import kernels
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(8, 3072, generator=gen).half().to(DEV)
+    w, s = rand_lin(3072, 3072, gen)
+    w, s = w.to(DEV), s.to(DEV)
+    a = kernels.int8_mm(x, w, s, kspan=128)
+    b = kernels.int8_mm(x, w, s, kspan=128)
+    assert torch.equal(a, b)
+
+
+# ----------------------------------------------------------------------------- fused GEMV prologues/epilogues
+def _plan():
+    from estudiocanciones_b200.engine import FramePlan, _Ctx
+    return FramePlan(_Ctx(DEV, 64 << 20, 1 << 20), pdl=False)
+
+
+def _ss(x):
+    R, D = x.shape
+    return (x.float() ** 2).reshape(R, D // 64, 64).sum(-1).t().contiguous()
+
+
+def test_gemv_rms_prologue_and_residual_ss():
+    from estudiocanciones_b200.engine import Linear
+    gen = torch.Generator().manual_seed(11)
+    M, D, N = 8, 3072, 3072
+    x = (torch.randn(M, D, generator=gen) * 2).half()
+    gamma = (1 + 0.1 * torch.randn(D, generator=gen)).half()
+    w, s = rand_lin(N, D, gen)
+    res = torch.randn(M, N, generator=gen).half()
+    lin = Linear(w.to(DEV), s.to(DEV))
+    xd, yd = x.to(DEV), res.to(DEV).clone()
+    ss_in = _ss(xd)
+    ss_out = torch.zeros(N // 64, M, device=DEV)
+    p = _plan()
+    p._gemv(lin, M, p.src_rms(xd, ss_in, gamma.to(DEV)), y=yd, res=yd, ss_out=ss_out)
+    p.run()
+    ref = O.gemv_i8(O.rmsnorm(x, gamma), w, s, res)
+    close16(yd, ref, ulps=2, frac_exact=0.9)
+    torch.testing.assert_close(ss_out.cpu(), _ss(yd).cpu(), rtol=1e-5, atol=1e-4)
+
+
+def test_gemv_emb_interleave_prologue():
+    """Decoder pass 0 input: rows (2b, 2b+1) = (rms(x_b), emb(c0_b))."""
+    from estudiocanciones_b200.engine import Emb, Linear
+    gen = torch.Generator().manual_seed(12)
+    B, D, N, V = 4, 3072, 1024, 8197
+    x = torch.randn(B, D, generator=gen).half()
+    gamma = torch.ones(D).half()
+    tq = torch.randint(-127, 128, (8 * V, D), generator=gen, dtype=torch.int8)
+    ts = (torch.rand(8 * V, generator=gen) * 0.01).half()
+    tok = torch.randint(0, V, (B, 8), generator=gen)
+    w, s = rand_lin(N, D, gen)
+    lin, emb = Linear(w.to(DEV), s.to(DEV)), Emb(tq.to(DEV), ts.to(DEV))
+    xd, tokd = x.to(DEV), tok.to(DEV)
+    y = torch.empty(2 * B, N, dtype=torch.float16, device=DEV)
+    p = _plan()
+    p._gemv(lin, 2 * B, p.src_rms(xd, _ss(xd), gamma.to(DEV)), p.src_emb(emb, tokd, 0, 0), y=y)
+    p._gemv(lin, B, p.src_emb(emb, tokd, 3, 3 * V), y=y[:B])  # codebook 3 rows -> y[:B]
+    p.run()
+    e0 = O.emb_i8(tok[:, 0], tq, ts)
+    xin = torch.stack([O.rmsnorm(x, gamma), e0], 1).reshape(2 * B, D)
+    ref = O.gemv_i8(xin, w, s)
+    close16(y[B:], ref[B:], ulps=2, frac_exact=0.9)
+    close16(y[:B], O.gemv_i8(O.emb_i8(tok[:, 3] + 3 * V, tq, ts), w, s), ulps=2, frac_exact=0.9)
+
+
+@pytest.mark.parametrize("S,Hq,Hk", [(1, 24, 8), (2, 8, 2)])
+def test_gemv_rope_kv_epilogue(S, Hq, Hk):
+    from estudiocanciones_b200.engine import Block, Linear
+    gen = torch.Generator().manual_seed(13)
+    hd, D, L = 128, 1024, 64
+    R = 4
+    B = R // S
+    x = torch.randn(R, D, generator=gen).half()
+    gamma = torch.ones(D).half()
+    N = (Hq + 2 * Hk) * hd
+    w, s = rand_lin(N, D, gen)
+    pos = torch.tensor([5, 63, 0, 17][:R]) if S == 1 else torch.tensor([0, 1, 0, 1])
+    rope = O.rope_table(hd, L)
+    kc0 = torch.randn(B, Hk, L, hd, generator=gen).half()
+    vc0 = torch.randn(B, Hk, L, hd, generator=gen).half()
+    blk = Block.__new__(Block)
+    blk.h, blk.kvh, blk.hd = Hq, Hk, hd
+    blk.kc, blk.vc = kc0.clone().to(DEV), vc0.clone().to(DEV)
+    lin = Linear(w.to(DEV), s.to(DEV))
+    xd = x.to(DEV)
+    q = torch.empty(R, Hq * hd, dtype=torch.float16, device=DEV)
+    p = _plan()
+    p._gemv(lin, R, p.src_rms(xd, _ss(xd), gamma.to(DEV)), epi=HM_EPI_ROPE_KV, rope=rope.to(DEV), pos=pos.to(DEV), S=S,
+            blk=blk, q_out=q)
+    p.run()
+    qkv = O.gemv_i8(O.rmsnorm(x, gamma), w, s)
+    kc, vc = kc0.clone(), vc0.clone()
+    qr = O.rope_kv_write(qkv, rope, pos, kc, vc, S, Hq, Hk)
+    close16(q, qr, ulps=2, frac_exact=0.9)
+    close16(blk.kc, kc, ulps=2, frac_exact=0.95)
+    close16(blk.vc, vc, ulps=2, frac_exact=0.95)
+    # slots other than the written positions are untouched (bit-exact)
+    mask = torch.ones(B, L, dtype=torch.bool)
+    for r in range(R):
+        mask[r // S, int(pos[r])] = False
+    assert torch.equal(blk.kc.cpu()[mask.nonzero(as_tuple=True)], kc0[mask.nonzero(as_tuple=True)])
+
+
+def test_gemv_silu_epilogue():
+    from estudiocanciones_b200.engine import Linear
+    gen = torch.Generator().manual_seed(14)
+    M, D, F = 8, 1024, 8192
+    x = torch.randn(M, D, generator=gen).half()
+    gamma = (1 + 0.1 * torch.randn(D, generator=gen)).half()
+    w, s = rand_lin(2 * F, D, gen)
+    lin = Linear(w.to(DEV), s.to(DEV))
+    xd = x.to(DEV)
+    y = torch.empty(M, F, dtype=torch.float16, device=DEV)
+    p = _plan()
+    p._gemv(lin, M, p.src_rms(xd, _ss(xd), gamma.to(DEV)), epi=HM_EPI_SILU, y=y)
+    p.run()
+    ref = O.silu_mul(O.gemv_i8(O.rmsnorm(x, gamma), w, s))
+    close16(y, ref, ulps=3, frac_exact=0.9)
+
+
+# ----------------------------------------------------------------------------- small kernels
+@pytest.mark.parametrize("i", range(2))
+def test_rms_golden(golden, i):
+    from estudiocanciones_b200 import kernels
+    z = golden("kernels")
+    out = kernels.rms(g(z[f"rms{i}_x"]).to(DEV), g(z[f"rms{i}_w"]).to(DEV))
+    close16(out, g(z[f"rms{i}_y"]), ulps=1, frac_exact=0.99)
+
+
+@pytest.mark.parametrize("i", range(2))
+def test_rope_cache_golden(golden, i):
+    from estudiocanciones_b200 import kernels
+    z = golden("kernels")
+    R, S, Hq, Hk, L = (int(v) for v in z[f"rope{i}_cfg"])
+    kc, vc = g(z[f"rope{i}_kc0"]).to(DEV), g(z[f"rope{i}_vc0"]).to(DEV)
+    q = torch.empty(R, Hq * 128, dtype=torch.float16, device=DEV)
+    kernels.rope_cache(g(z[f"rope{i}_qkv"]).to(DEV), g(z[f"rope{i}_table"]).to(DEV), g(z[f"rope{i}_pos"]).to(DEV), q,
+                       kc, vc, S, Hq, Hk, L)
+    close16(q, g(z[f"rope{i}_q"]), ulps=1, frac_exact=0.98)
+    close16(kc, g(z[f"rope{i}_kc"]), ulps=1, frac_exact=0.98)
+    assert torch.equal(vc.cpu(), g(z[f"rope{i}_vc"]))
+
+
+@pytest.mark.parametrize("i", range(2))
+def test_silu_golden(golden, i):
+    from estudiocanciones_b200 import kernels
+    z = golden("kernels")
+    out = kernels.silu_mul(g(z[f"silu{i}_a"]).to(DEV))
+    close16(out, g(z[f"silu{i}_y"]), ulps=1, frac_exact=0.99)
+
+
+def test_emb_gather_and_sum():
+    from estudiocanciones_b200 import kernels
+    from estudiocanciones_b200.engine import Emb, FramePlan
+    gen = torch.Generator().manual_seed(15)
+    V, D, B = 8197, 3072, 8
+    tq = torch.randint(-127, 128, (8 * V, D), generator=gen, dtype=torch.int8)
+    ts = (torch.rand(8 * V, generator=gen) * 0.01).half()
+    tok = torch.randint(0, V, (B, 8), generator=gen)
+    out = kernels.emb_i8(tok[:, 2].to(DEV) + 2 * V, tq.to(DEV), ts.to(DEV))
+    assert torch.equal(out.cpu(), O.emb_i8(tok[:, 2] + 2 * V, tq, ts))
+    x = torch.empty(B, D, dtype=torch.float16, device=DEV)
+    ss = torch.empty(D // 64, B, device=DEV)
+    p = _plan()
+    p.emb_sum(Emb(tq.to(DEV), ts.to(DEV)), tok.to(DEV), B, 8, V, x, ss)
+    p.run()
+    assert torch.equal(x.cpu(), O.emb_sum(tok, tq, ts, V))
+    torch.testing.assert_close(ss.cpu(), _ss(x).cpu(), rtol=1e-5, atol=1e-4)
+
+
+def test_bad_token_sets_error_bit_without_fault():
+    from estudiocanciones_b200 import kernels
+    tq = torch.zeros(10, 64, dtype=torch.int8, device=DEV)
+    ts = torch.ones(10, dtype=torch.float16, device=DEV)
+    out = kernels.emb_i8(torch.tensor([3, 12], device=DEV), tq, ts)
+    assert kernels.read_errors(DEV) == 2
+    assert torch.all(out[1] == 0)
+
+
+# ----------------------------------------------------------------------------- attention
+@pytest.mark.parametrize("i", range(3))
+def test_attn_golden(golden, i):
+    from estudiocanciones_b200 import kernels
+    z = golden("kernels")
+    R, S, Hq, Hk, L, ns = (int(v) for v in z[f"attn{i}_cfg"])
+    o = torch.empty(R, Hq * 128, dtype=torch.float16, device=DEV)
+    kernels.attn(g(z[f"attn{i}_q"]).to(DEV), g(z[f"attn{i}_kc"]).to(DEV), g(z[f"attn{i}_vc"]).to(DEV),
+                 g(z[f"attn{i}_pos"]).to(DEV), o, S, Hq, Hk, L, nsplit=ns)
+    torch.testing.assert_close(o.cpu().float(), g(z[f"attn{i}_o"]).float(), atol=2e-3, rtol=5e-3)
+
+
+@pytest.mark.parametrize("R,S,Hq,Hk,hd,L,pos,ns", [
+    (8, 1, 24, 8, 128, 1350, [0, 1, 31, 32, 599, 975, 1348, 1349], 5),
+    (1, 1, 24, 8, 128, 512, [511], 37),
+    (16, 2, 8, 2, 128, 8, [0, 1] * 8, 1),
+    (4, 1, 8, 2, 128, 8, [7, 6, 5, 2], 1),
+    (4, 1, 8, 4, 384, 40, [3, 39, 0, 20], 3),
+    (2, 1, 24, 8, 128, 4282, [4281, 4023], 16)])
+def test_attn_matches_oracle(R, S, Hq, Hk, hd, L, pos, ns):
+    from estudiocanciones_b200 import kernels
+    gen = torch.Generator().manual_seed(R + L + ns)
+    B = R // S
+    q = torch.randn(R, Hq * hd, generator=gen).half()
+    kc = torch.randn(B, Hk, L, hd, generator=gen).half()
+    vc = torch.randn(B, Hk, L, hd, generator=gen).half()
+    pos_t = torch.tensor(pos)
+    o = torch.empty(R, Hq * hd, dtype=torch.float16, device=DEV)
+    kernels.attn(q.to(DEV), kc.to(DEV), vc.to(DEV), pos_t.to(DEV), o, S, Hq, Hk, L, nsplit=ns)
+    ref = O.decode_attn(q, kc, vc, pos_t, S, Hq, Hk)
+    torch.testing.assert_close(o.cpu().float(), ref.float(), atol=2e-3, rtol=5e-3)
+
+
+# ----------------------------------------------------------------------------- sampler
+@pytest.mark.parametrize("i", range(5))
+def test_sampler_golden(golden, i):
+    from estudiocanciones_b200 import kernels
+    z = golden("sampler")
+    rows, n_takes, topk, temp, cfg = z[f"s{i}_cfg"]
+    rows, n_takes, topk = int(rows), int(n_takes), int(topk)
+    out = torch.full((rows, 8), -1, dtype=torch.long, device=DEV)
+    kernels.sample(g(z[f"s{i}_logits"]).to(DEV), n_takes, float(cfg), topk, float(temp),
+                   g(z[f"s{i}_noise"]).to(DEV), out, 3)
+    assert torch.equal(out[:, 3:4].cpu(), g(z[f"s{i}_ids"]))
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_sampler_matches_oracle(seed):
+    from estudiocanciones_b200 import kernels
+    gen = torch.Generator().manual_seed(100 + seed)
+    N, V = 4, 8197
+    cfg, topk, temp = [(1.5, 50, 1.0), (1.0, 50, 1.0), (3.0, 5, 0.5), (1.5, 1, 1.0), (1.5, 8197, 1.2),
+                       (1.5, 50, 1.0)][seed]
+    B = 2 * N if cfg != 1.0 else N
+    logits = (torch.randn(B, V, generator=gen) * 4).half()
+    if seed == 5:
+        logits[:, 200:260] = 0.5   # a plateau of equal values straddling the top-k boundary
+    noise = torch.empty(N, V).exponential_(1, generator=gen)
+    out = torch.full((B, 8), -1, dtype=torch.long, device=DEV)
+    kernels.sample(logits.to(DEV), N, cfg, topk, temp, noise.to(DEV), out, 0)
+    ref = O.guided_sample(logits, N, cfg, topk, temp, noise)
+    assert torch.equal(out[:, :1].cpu(), ref)
