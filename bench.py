@@ -50,6 +50,10 @@ def args_():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn"],
+                    help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures")
+    ap.add_argument("--layers", type=int, default=4, help="backbone layers of the small cases")
+    ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
 
@@ -382,8 +386,71 @@ def run_ours(a, world, rank, local):
         print(json.dumps(out), flush=True)
 
 
+def run_case(a):
+    """Small single-kernel cases for profiling: the GEMV launches of a few backbone
+    layers (weights > L2 but well under a GB) or one decode-attention launch at the
+    benchmark's shapes.  Eager launches without PDL; prints one JSON line."""
+    from dataclasses import replace
+    from estudiocanciones_b200.checkpoint import BASELINE_SHAPE, synthetic_tensors
+    from estudiocanciones_b200.engine import FramePlan, HeartMuLaLite
+    dev = torch.device("cuda", 0)
+    shape = replace(BASELINE_SHAPE, bb_layers=a.layers, dec_layers=1, text_vocab=1024)
+    t = synthetic_tensors(shape, seed=0, device=dev)
+    m = HeartMuLaLite(t, device=dev)
+    del t
+    N, B, P = a.takes, 2 * a.takes, a.prompt
+    L = P + a.frames + 2 + 256
+    m.alloc(N, B, L)
+    rt = m._rt
+    rt.pos.fill_(P + a.frames // 2)
+    g = torch.Generator(device=dev).manual_seed(0)
+    for blk in m.backbone.blocks:
+        blk.kc.normal_(generator=g)
+        blk.vc.normal_(generator=g)
+    p = FramePlan(rt.ctx, pdl=False)
+    if a.case == "gemv":
+        from estudiocanciones_b200._lib import HM_EPI_ROPE_KV, HM_EPI_SILU
+        bb = rt.bb
+        for b in m.backbone.blocks:
+            p._gemv(b.qkv, B, p.src_rms(bb.x, bb.ss, b.n1), epi=HM_EPI_ROPE_KV, rope=m.backbone.rope, pos=rt.pos,
+                    S=1, blk=b, q_out=bb.q)
+            p._gemv(b.o, B, p.src_f16(bb.o), y=bb.x, res=bb.x, ss_out=bb.ss)
+            p._gemv(b.w13, B, p.src_rms(bb.x, bb.ss, b.n2), epi=HM_EPI_SILU, y=bb.mm)
+            p._gemv(b.w2, B, p.src_f16(bb.mm), y=bb.x, res=bb.x, ss_out=bb.ss)
+    else:
+        b = m.backbone.blocks[0]
+        p.attn(b, rt.bb.q, rt.bb.o, rt.pos, 1, B, rt.nsplit)
+    p.run()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(graph, stream=st):
+            p.run()
+    torch.cuda.current_stream().wait_stream(st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph.replay()
+    e0.record()
+    for _ in range(a.reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000 * e0.elapsed_time(e1) / (a.reps * p.n_kernels)
+    out = {"case": a.case, "launches": p.n_kernels, "us_per_launch": round(us, 3), "rows": B,
+           "pos": P + a.frames // 2, "nsplit": rt.nsplit,
+           "env": {k: v for k, v in os.environ.items() if k.startswith("HM_")}}
+    if a.case == "gemv":
+        wb = sum(l.nbytes for b in m.backbone.blocks for l in (b.qkv, b.o, b.w13, b.w2))
+        out["weight_GBps"] = round(wb / (us * 1e-6 * p.n_kernels) / 1e9, 1)
+    print(json.dumps(out), flush=True)
+
+
 def main():
     a = args_()
+    if a.case != "frame":
+        run_case(a)
+        return
     world, rank, local = dist_setup()
     try:
         if a.impl == "reference":

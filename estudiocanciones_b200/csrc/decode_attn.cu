@@ -36,16 +36,27 @@ struct AttnParams {
   int* err;
 };
 
+constexpr int kMaxSplit = 64;
+
+template <int HD>
+struct AttnCfg {
+  static constexpr int NST = HD <= 128 ? 4 : 2;  // K/V ring stages (16 KB each at hd 128)
+};
+
 template <int HD>
 struct AttnSmem {
-  __half k[2][kTP][HD];
-  __half v[2][kTP][HD];
+  __half k[AttnCfg<HD>::NST][kTP][HD];
+  __half v[AttnCfg<HD>::NST][kTP][HD];
   float q[kMaxG][HD];
   float s[kMaxG][kTP];
   float red[kMaxG][HD];
   float alpha[kMaxG], m[kMaxG], l[kMaxG];
-  uint64_t bar[2];
+  float cw[kMaxG][kMaxSplit];  // combine weights of the split partials
+  float cl[kMaxG][kMaxSplit];  // their softmax denominators
+  float cden[kMaxG];
+  uint64_t bar[AttnCfg<HD>::NST];
   int flag;
+  int abort_flag;
 };
 
 template <int HD>
@@ -56,36 +67,53 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   AttnSmem<HD>& sm = *reinterpret_cast<AttnSmem<HD>*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sp = blockIdx.x, kh = blockIdx.y, r = blockIdx.z;
-  const int G = P.Hq / P.Hk;
+  // parameters in registers: the waits and barriers below clobber memory, which would
+  // otherwise re-read every field from the parameter block inside the loops
+  const int Hq = P.Hq, Hk = P.Hk, S = P.S, L = P.L, nsplit = P.nsplit, R = P.R;
+  const float scale = P.scale;
+  int* const err = P.err;
+  const __half* const qg = P.q;
+  __half* const og = P.o;
+  float* const wsg = P.ws;
+  int* const counters = P.counters;
+  const int G = Hq / Hk;
 
+  constexpr int NST = AttnCfg<HD>::NST;
   if (tid == 0) {
-    mbar_init(&sm.bar[0], 1);
-    mbar_init(&sm.bar[1], 1);
+    sm.abort_flag = 0;
+    for (int i = 0; i < NST; ++i) mbar_init(&sm.bar[i], 1);
     fence_barrier_init();
   }
   pdl_trigger();
   pdl_wait();
 
   const int64_t p_last = P.pos[r];
-  const int b = r / P.S;
+  const int b = r / S;
   int len = static_cast<int>(p_last) + 1;
-  if (p_last < 0 || p_last >= P.L) {
-    report_error(P.err, HM_ERR_BADINDEX);
+  if (p_last < 0 || p_last >= L) {
+    report_error(err, HM_ERR_BADINDEX);
     len = 0;
   }
-  const int per = (len + P.nsplit - 1) / P.nsplit;
+  const int per = (len + nsplit - 1) / nsplit;
   const int chunk = (per + kTP - 1) / kTP * kTP;
   const int lo = sp * chunk;
   const int hi = min(len, lo + chunk);
   const int ntile = hi > lo ? (hi - lo + kTP - 1) / kTP : 0;
 
-  const __half* kbase = P.kc + ((int64_t)b * P.Hk + kh) * P.L * HD;
-  const __half* vbase = P.vc + ((int64_t)b * P.Hk + kh) * P.L * HD;
+  const __half* kbase = P.kc + ((int64_t)b * Hk + kh) * L * HD;
+  const __half* vbase = P.vc + ((int64_t)b * Hk + kh) * L * HD;
 
-  // q of the G heads of this KV head, fp32
-  for (int i = tid; i < G * HD; i += kThreads) {
-    const int gg = i / HD, d = i - gg * HD;
-    sm.q[gg][d] = __half2float(P.q[(int64_t)r * P.Hq * HD + (kh * G + gg) * HD + d]);
+  // q of the G heads of this KV head, fp32 (16-byte loads, all in flight together)
+  for (int i = tid; i < G * HD / 8; i += kThreads) {
+    const int gg = (8 * i) / HD, d = 8 * i - gg * HD;
+    const uint4 v = *reinterpret_cast<const uint4*>(qg + (int64_t)r * Hq * HD + (kh * G + gg) * HD + d);
+    const __half2* h2 = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h2[j]);
+      sm.q[gg][d + 2 * j] = f.x;
+      sm.q[gg][d + 2 * j + 1] = f.y;
+    }
   }
   if (tid < kMaxG) {
     sm.m[tid] = -INFINITY;
@@ -94,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   __syncthreads();
 
   auto issue = [&](int t) {
-    const int st = t & 1;
+    const int st = t % NST;
     const int p0 = lo + t * kTP;
     const int nv = min(kTP, hi - p0);
     const uint32_t bytes = static_cast<uint32_t>(nv) * HD * 2;
@@ -102,10 +130,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     bulk_load(&sm.k[st][0][0], kbase + (int64_t)p0 * HD, bytes, &sm.bar[st]);
     bulk_load(&sm.v[st][0][0], vbase + (int64_t)p0 * HD, bytes, &sm.bar[st]);
   };
-  if (tid == 0) {
-    if (ntile > 0) issue(0);
-    if (ntile > 1) issue(1);
-  }
+  if (tid == 0)
+    for (int t = 0; t < NST && t < ntile; ++t) issue(t);
 
   float acc[kMaxG][2 * U];
 #pragma unroll
@@ -115,15 +141,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
 
   const int qp = tid >> 2, qd = tid & 3;   // QK: position qp of the tile, quarter qd of the row
   const int ph = tid >> 6, dc = tid & 63;  // PV: position parity ph, half2 column group dc
-  bool ok = true;
   for (int t = 0; t < ntile; ++t) {
-    const int st = t & 1;
+    const int st = t % NST;
     const int p0 = lo + t * kTP;
     const int nv = min(kTP, hi - p0);
-    if (!mbar_wait(&sm.bar[st], (t >> 1) & 1, P.err)) {
-      ok = false;
-      break;
-    }
+    mbar_wait_ab(&sm.bar[st], (t / NST) & 1, err, &sm.abort_flag);  // on timeout: carry on, error flagged
     // ---- scores s[g][p] = (q_g . k_p) * scale
     {
       float part[kMaxG];
@@ -158,7 +180,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         float v = part[gg];
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (gg < G && qd == 0) sm.s[gg][qp] = qp < nv ? v * P.scale : -INFINITY;
+        if (gg < G && qd == 0) sm.s[gg][qp] = qp < nv ? v * scale : -INFINITY;
       }
     }
     __syncthreads();
@@ -205,12 +227,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       }
     }
     __syncthreads();  // stage st and s[][] are free again
-    if (tid == 0 && t + 2 < ntile) issue(t + 2);
-  }
-  if (!ok) {
-    mbar_wait(&sm.bar[0], 0, nullptr);
-    mbar_wait(&sm.bar[1], 0, nullptr);
-    return;
+    if (tid == 0 && t + NST < ntile) issue(t + NST);
   }
 
   // ---- merge the two position parities into red[g][d]
@@ -237,47 +254,70 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
   __syncthreads();
 
-  const int64_t head0 = (int64_t)r * P.Hq + kh * G;
-  if (P.nsplit == 1) {
+  const int64_t head0 = (int64_t)r * Hq + kh * G;
+  if (nsplit == 1) {
     for (int i = tid; i < G * HD; i += kThreads) {
       const int gg = i / HD, d = i - gg * HD;
       const float l = sm.l[gg];
-      P.o[(head0 + gg) * HD + d] = __float2half_rn(l > 0.f ? sm.red[gg][d] / l : 0.f);
+      og[(head0 + gg) * HD + d] = __float2half_rn(l > 0.f ? sm.red[gg][d] / l : 0.f);
     }
     return;
   }
-  const int64_t nh = (int64_t)P.R * P.Hq * P.nsplit;
-  float* wm = P.ws;
-  float* wl = P.ws + nh;
-  float* wa = P.ws + 2 * nh;
+  const int64_t nh = (int64_t)R * Hq * nsplit;
+  float* wm = wsg;
+  float* wl = wsg + nh;
+  float* wa = wsg + 2 * nh;
   for (int i = tid; i < G * HD; i += kThreads) {
     const int gg = i / HD, d = i - gg * HD;
-    wa[((head0 + gg) * P.nsplit + sp) * HD + d] = sm.red[gg][d];
+    wa[((head0 + gg) * nsplit + sp) * HD + d] = sm.red[gg][d];
   }
   if (tid < G) {
-    wm[(head0 + tid) * P.nsplit + sp] = sm.m[tid];
-    wl[(head0 + tid) * P.nsplit + sp] = sm.l[tid];
+    wm[(head0 + tid) * nsplit + sp] = sm.m[tid];
+    wl[(head0 + tid) * nsplit + sp] = sm.l[tid];
   }
   __threadfence();
   __syncthreads();
-  int* ticket = &P.counters[r * P.Hk + kh];
-  if (tid == 0) sm.flag = (atomicAdd(ticket, 1) == P.nsplit - 1);
+  int* ticket = &counters[r * Hk + kh];
+  if (tid == 0) sm.flag = (atomicAdd(ticket, 1) == nsplit - 1);
   __syncthreads();
   if (!sm.flag) return;
   __threadfence();
+  // merge the nsplit partials of the G heads: weights exp(m_s - max) staged first (one
+  // load per thread), then every output sums its column over the splits in order
+  for (int i = tid; i < G * nsplit; i += kThreads) {
+    const int gg = i / nsplit, s2 = i - gg * nsplit;
+    sm.cw[gg][s2] = __ldcg(wm + (head0 + gg) * nsplit + s2);
+    sm.cl[gg][s2] = __ldcg(wl + (head0 + gg) * nsplit + s2);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float mx = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) mx = fmaxf(mx, sm.cw[tid][s2]);
+    float den = 0.f;
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+      const float ms = sm.cw[tid][s2];
+      const float w = ms > -INFINITY ? expf(ms - mx) : 0.f;
+      sm.cw[tid][s2] = w;
+      den += sm.cl[tid][s2] * w;
+    }
+    sm.cden[tid] = den;
+  }
+  __syncthreads();
   for (int i = tid; i < G * HD; i += kThreads) {
     const int gg = i / HD, d = i - gg * HD;
     const int64_t h = head0 + gg;
-    float mx = -INFINITY;
-    for (int s2 = 0; s2 < P.nsplit; ++s2) mx = fmaxf(mx, __ldcg(wm + h * P.nsplit + s2));
-    float num = 0.f, den = 0.f;
-    for (int s2 = 0; s2 < P.nsplit; ++s2) {
-      const float ms = __ldcg(wm + h * P.nsplit + s2);
-      const float w = ms > -INFINITY ? expf(ms - mx) : 0.f;
-      num += __ldcg(wa + (h * P.nsplit + s2) * HD + d) * w;
-      den += __ldcg(wl + h * P.nsplit + s2) * w;
+    float part[8];
+    float num = 0.f;
+    for (int s0 = 0; s0 < nsplit; s0 += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        part[j] = s0 + j < nsplit ? __ldcg(wa + (h * nsplit + s0 + j) * HD + d) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < nsplit) num += part[j] * sm.cw[gg][s0 + j];
     }
-    P.o[h * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+    const float den = sm.cden[gg];
+    og[h * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
   }
   if (tid == 0) *ticket = 0;
 }
@@ -307,7 +347,7 @@ extern "C" int hm_decode_attn(const void* q, const void* kc, const void* vc, con
                               size_t ws_bytes, int* counters, int n_counters, int* err, int pdl,
                               hm_stream_t stream) {
   if (!q || !kc || !vc || !pos || !o || R < 1 || S < 1 || R % S || Hk < 1 || Hq % Hk || Hq / Hk > kMaxG || L < 1 ||
-      nsplit < 1 || nsplit > 1024)
+      nsplit < 1 || nsplit > kMaxSplit)
     return HM_EARG;
   if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15u) return HM_EARG;
   if (nsplit > 1 && (!ws || !counters || n_counters < R * Hk || ws_bytes < hm_decode_attn_workspace_bytes(R, Hq, hd, nsplit)))

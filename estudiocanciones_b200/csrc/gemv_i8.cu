@@ -6,21 +6,28 @@
 // prologue; residual add, RoPE + KV-cache write, or SiLU*mul in the epilogue.
 //
 // Design (HBM-bound: every weight byte is read exactly once per frame):
-//  * CTA tile = 64 weight rows x `kspan` columns (kspan <= 1024, split-K over
-//    the grid's y dimension).  One thread issues TMA tile loads for the whole
-//    tile at CTA start, before griddepcontrol.wait, so weight streaming of
-//    this launch overlaps the tail of the previous one.  Tiles land 128B-
-//    swizzled so the fragment reads below are bank-conflict free.
-//  * Tensor-core MMA m16n8k16 with the weights as the 16-row A operand and up
-//    to 8*MT activation rows as the n dimension ("swap AB"): at R = 8 rows the
-//    MMA n = 8 carries no padding.  The int8 -> fp16 conversion is exact, the
-//    accumulation is fp32, and the per-row scale is applied afterwards in fp32,
-//    exactly where _gemv8 applies it.
-//  * K inside a 128-column block is permuted consistently for A and B so every
+//  * Tiles of 16 weight rows (16 w1 + 16 w3 rows for the SiLU epilogue) over a
+//    k-range that is the whole K whenever the activations fit in shared memory
+//    (every decode shape at up to 8 rows), so no cross-CTA reduction is needed.
+//    One wave of persistent CTAs strides over the tiles.
+//  * A producer warp streams each tile through a 6-stage ring of 8 KB stages
+//    (four 16x128-byte TMA boxes, 128B swizzle, L2 evict-first), running ahead
+//    across tile boundaries and starting before griddepcontrol.wait, so the
+//    weight stream of a launch overlaps the tail of the previous launch.
+//  * Four consumer warps stage the activation k-range once per CTA (all loads
+//    in flight together: cp.async for fp16 rows, ids then int8 rows for
+//    embedding gathers, RMSNorm applied in place); each warp takes one of the
+//    stage's four boxes (a 128-column slice) and runs tensor-core MMA m16n8k16
+//    with the weights as the 16-row A operand and up to 8*MT activation rows as
+//    the n dimension ("swap AB": at R = 8 rows there is no padding).  int8 ->
+//    fp16 is exact, accumulation is fp32, and the per-row scale is applied
+//    afterwards in fp32, where _gemv8 applies it.  The four warps' partial sums
+//    are added in a fixed order (deterministic).
+//  * K inside a 128-column box is permuted consistently for A and B so every
 //    lane reads 32 contiguous weight bytes and 64 contiguous activation bytes.
-//  * Split-K partials go to a scratch buffer; the last CTA of a tile (atomic
-//    ticket) sums them in split order (deterministic) and runs the epilogue,
-//    then re-arms the ticket to zero.
+//  * Only when the activations do not fit (many rows x long K) the k-range is
+//    split over CTAs; partials then go to scratch and the last CTA of a tile
+//    (atomic ticket) sums them in split order and runs the epilogue.
 #include <cudaTypedefs.h>
 
 #include <cstddef>
@@ -34,39 +41,45 @@
 
 namespace {
 
-constexpr int kRows = 64;     // weight rows per CTA tile
-constexpr int kBlkK = 128;    // k columns (bytes) per TMA box / mbarrier
-constexpr int kBoxRows = 32;  // rows per TMA box (two boxes per block)
-constexpr int kThreads = 128;
-constexpr int kMaxKspan = 1024;
-constexpr int kMaxBlocks = kMaxKspan / kBlkK;
+constexpr int kTileRows = 16;   // rows of one MMA row block
+constexpr int kBox = 128;       // k columns (bytes) per TMA box
+constexpr int kBoxBytes = kTileRows * kBox;
+constexpr int kStage = 4 * kBoxBytes;  // four boxes per stage
+constexpr int kNST = 6;         // ring stages
+constexpr int kCons = 128;      // consumer threads (4 MMA warps)
+constexpr int kThreads = kCons + 32;
 constexpr int kMaxM = 32;
+constexpr int kXBudget = 128 * 1024;  // bytes of staged activations per CTA
+constexpr int kBarCons = 1;     // named barrier of the consumer warps
 
 struct GemvParams {
   hm_gemv_desc d;
-  int kspan, nsplit, ntiles;
+  int kspan, nsplit, ntiles, has_gamma;
 };
 
 struct SmemLayout {
-  int w_off, x_off, acc_off, sq_off, scale_off, inv_off, flag_off, bar_off, total;
-  int xp;  // x row pitch in bytes
+  int ring, x, gam, red, inv, esc, rowp, rmode, flag, bars, total;  // flag: [0] tile owner, [1] abort
+  int xp;  // activation row pitch in bytes
 };
 
 __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
+__host__ __device__ inline int rt_of(int epi) { return epi == HM_EPI_SILU ? 2 : 1; }
+__host__ __device__ inline int ks_of(int epi) { return 4 * kBox / rt_of(epi); }  // k bytes per stage
 
-__host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows) {
+__host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_gamma) {
   SmemLayout L;
-  const int nblk = kspan / kBlkK;
-  L.w_off = 0;
+  L.ring = 0;
   L.xp = kspan * 2 + 16;
-  L.x_off = nblk * kBlkK * kRows;                      // multiple of 8192 -> 1024-aligned
-  L.acc_off = align_up(L.x_off + mrows * L.xp, 16);
-  L.sq_off = L.acc_off + kRows * (mrows + 1) * 4;
-  L.scale_off = L.sq_off + kRows * mrows * 4;
-  L.inv_off = L.scale_off + kRows * 4;
-  L.flag_off = L.inv_off + kMaxM * 4;
-  L.bar_off = align_up(L.flag_off + 16, 8);
-  L.total = L.bar_off + kMaxBlocks * 8;
+  L.x = kNST * kStage;
+  L.gam = align_up(L.x + mrows * L.xp, 16);
+  L.red = L.gam + (has_gamma ? 2 * kspan * 2 : 0);
+  L.inv = L.red + 4 * kTileRows * (mrows + 1) * 4;
+  L.esc = L.inv + kMaxM * 4;
+  L.rowp = align_up(L.esc + kMaxM * 4, 8);
+  L.rmode = L.rowp + kMaxM * 8;
+  L.flag = L.rmode + 2 * kMaxM * 4;
+  L.bars = align_up(L.flag + 16, 8);
+  L.total = L.bars + 2 * kNST * 8;
   return L;
 }
 
@@ -74,292 +87,419 @@ __host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows) {
 // free for the B-fragment reads: lanes t and t+2 land in different banks).
 __device__ __forceinline__ int xchunk(int c) { return c ^ (((c >> 3) & 1) << 1); }
 
-struct RowRef {
-  const hm_row_src* s;
-  int row;
-};
-
-__device__ __forceinline__ RowRef row_of(const hm_gemv_desc& d, int m) {
-  const int sel = d.interleave ? (m & 1) : 0;
+__device__ __forceinline__ const hm_row_src& src_of(const hm_gemv_desc& d, int m, int& row, int& sel) {
+  sel = d.interleave ? (m & 1) : 0;
   const int local = d.interleave ? (m >> 1) : m;
-  RowRef r;
-  r.s = &d.src[sel];
-  r.row = local * r.s->row_mul + r.s->row_add;
-  return r;
+  const hm_row_src& s = d.src[sel];
+  row = local * s.row_mul + s.row_add;
+  return s;
 }
 
-// 8 consecutive activations of row m starting at column k, after the prologue transform.
-__device__ __forceinline__ uint4 load_x8(const hm_gemv_desc& d, int m, int k, float inv, int* err) {
-  if (k >= d.K) return make_uint4(0, 0, 0, 0);  // column tail of a K that is not a multiple of 128
-  const RowRef rr = row_of(d, m);
-  const hm_row_src& s = *rr.s;
-  if (s.mode == HM_SRC_EMB) {
-    int64_t id = s.tok[(int64_t)rr.row * s.tok_ld + s.tok_col] + s.tok_off;
-    if (id < 0 || id >= s.erows) {
-      report_error(err, HM_ERR_BADINDEX);
-      return make_uint4(0, 0, 0, 0);
-    }
-    const uint2 q = *reinterpret_cast<const uint2*>(s.etab + id * (int64_t)d.K + k);
-    const float sc = __half2float(reinterpret_cast<const __half*>(s.escale)[id]);
-    const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
-    uint4 out;
-    __half* oh = reinterpret_cast<__half*>(&out);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) oh[j] = __float2half_rn(static_cast<float>(qb[j]) * sc);
-    return out;
-  }
-  const __half* xr = reinterpret_cast<const __half*>(s.x) + (int64_t)rr.row * s.ldx + k;
-  uint4 v = *reinterpret_cast<const uint4*>(xr);
-  if (s.mode == HM_SRC_RMS) {
-    const __half* g = reinterpret_cast<const __half*>(s.gamma) + k;
-    const uint4 gv = *reinterpret_cast<const uint4*>(g);
-    __half* vh = reinterpret_cast<__half*>(&v);
-    const __half* gh = reinterpret_cast<const __half*>(&gv);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) vh[j] = hmul_rn(__float2half_rn(__half2float(vh[j]) * inv), gh[j]);
-  }
-  return v;
+// first weight row of row block rb (0: w1 / the only block, 1: w3) of tile `tile`
+__device__ __forceinline__ int block_row(const hm_gemv_desc& d, int epi, int tile, int rb) {
+  return (epi == HM_EPI_SILU && rb == 1) ? d.N / 2 + tile * kTileRows : tile * kTileRows;
 }
 
 template <int MT, int EPI>
 __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant__ CUtensorMap wmap,
                                                            const __grid_constant__ GemvParams P) {
+  constexpr int RT = EPI == HM_EPI_SILU ? 2 : 1;
+  constexpr int KS = 4 * kBox / RT;
   constexpr int MROWS = 8 * MT;
   constexpr int MP = MROWS + 1;
   extern __shared__ __align__(1024) uint8_t smem[];
   const hm_gemv_desc& d = P.d;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
-  const int kspan = P.kspan, nblk = kspan / kBlkK;
+  const int split = blockIdx.y;
+  const int kspan = P.kspan;
   const int k0 = split * kspan;
   const int M = d.M;
-  const SmemLayout L = smem_layout(kspan, MROWS);
-  uint8_t* wsm = smem + L.w_off;
-  uint8_t* xsm = smem + L.x_off;
-  float* acc_s = reinterpret_cast<float*>(smem + L.acc_off);
-  float* sq_s = reinterpret_cast<float*>(smem + L.sq_off);
-  float* scale_s = reinterpret_cast<float*>(smem + L.scale_off);
-  float* inv_s = reinterpret_cast<float*>(smem + L.inv_off);
-  int* flag_s = reinterpret_cast<int*>(smem + L.flag_off);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  const int per_tile = kspan / KS;  // stages per tile
+  const int my_tiles = (P.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nstages = my_tiles * per_tile;
+  const SmemLayout L = smem_layout(kspan, MROWS, P.has_gamma);
+  uint8_t* ring = smem + L.ring;
+  uint8_t* xsm = smem + L.x;
+  __half* gam_s = reinterpret_cast<__half*>(smem + L.gam);
+  float* red_s = reinterpret_cast<float*>(smem + L.red);
+  float* inv_s = reinterpret_cast<float*>(smem + L.inv);
+  float* esc_s = reinterpret_cast<float*>(smem + L.esc);
+  const uint8_t** rowp_s = reinterpret_cast<const uint8_t**>(smem + L.rowp);
+  int* rmode_s = reinterpret_cast<int*>(smem + L.rmode);
+  int* rsel_s = rmode_s + kMaxM;
+  int* flag_s = reinterpret_cast<int*>(smem + L.flag);
+  volatile int* abort_s = flag_s + 1;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + kNST;
 
-  // weight rows of this tile: [r0a, r0a+32) and [r0b, r0b+32)
-  int r0a, r0b;
-  if (EPI == HM_EPI_SILU) {
-    r0a = tile * kBoxRows;
-    r0b = d.N / 2 + tile * kBoxRows;
-  } else {
-    r0a = tile * kRows;
-    r0b = r0a + kBoxRows;
-  }
-
-  // 128B-swizzled TMA destinations must be 1024-byte aligned
-  if (smem_u32(wsm) & 1023u) {
+  if (smem_u32(ring) & 1023u) {  // 128B-swizzled TMA destinations must be 1024-byte aligned
     if (tid == 0) report_error(d.err, HM_ERR_TIMEOUT);
     return;
   }
-  // ---- prologue that touches only immutable data (weights, scales)
   if (tid == 0) {
-    prefetch_tensormap(&wmap);
-    for (int b = 0; b < nblk; ++b) mbar_init(&bars[b], 1);
+    *abort_s = 0;
+    for (int i = 0; i < kNST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kCons / 32);
+    }
     fence_barrier_init();
   }
   __syncthreads();
-  if (tid == 0) {
-    const uint64_t pol = policy_evict_first();
-    for (int b = 0; b < nblk; ++b) {
-      mbar_arrive_expect_tx(&bars[b], kRows * kBlkK);
-      tma_load_2d(wsm + b * (kRows * kBlkK), &wmap, k0 + b * kBlkK, r0a, &bars[b], pol);
-      tma_load_2d(wsm + b * (kRows * kBlkK) + kBoxRows * kBlkK, &wmap, k0 + b * kBlkK, r0b, &bars[b], pol);
-    }
-  }
-  if (tid < kRows) {
-    const int n = tid < kBoxRows ? r0a + tid : r0b + (tid - kBoxRows);
-    scale_s[tid] = n < d.N ? __half2float(reinterpret_cast<const __half*>(d.s)[n]) : 0.f;
-  }
-  pdl_trigger();
-  // ---- everything below reads data produced by earlier launches
-  pdl_wait();
 
-  // RMSNorm inverse scales: sum of the producer's per-64-column partials in a fixed order
-  for (int m = warp; m < M; m += kThreads / 32) {
-    const RowRef rr = row_of(d, m);
-    float inv = 0.f;
-    if (rr.s->mode == HM_SRC_RMS) {
-      float a = 0.f;
-      for (int t = lane; t < rr.s->ss_tiles; t += 32) a += rr.s->ss[(int64_t)t * rr.s->ss_ld + rr.row];
-      a = warp_sum(a);
-      inv = 1.0f / sqrtf(a / static_cast<float>(rr.s->dim) + rr.s->eps);
-    }
-    if (lane == 0) inv_s[m] = inv;
-  }
-  __syncthreads();
-
-  // activation tile [MROWS][kspan] fp16, swizzled 16-byte chunks, zero rows >= M
-  {
-    const int cpr = kspan / 8;
-    for (int i = tid; i < MROWS * cpr; i += kThreads) {
-      const int m = i / cpr, c = i - m * cpr;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (m < M) v = load_x8(d, m, k0 + 8 * c, inv_s[m], d.err);
-      *reinterpret_cast<uint4*>(xsm + m * L.xp + xchunk(c) * 16) = v;
-    }
-  }
-  __syncthreads();
-
-  // ---- main loop: warp w owns tile rows [16w, 16w+16)
-  float acc[MT][4];
+  // ================================================================ producer warp
+  if (warp == kCons / 32) {
+    pdl_trigger();
+    if (lane == 0) {
+      int* const perr = d.err;
+      const int half_n = d.N / 2;
+      prefetch_tensormap(&wmap);
+      const uint64_t pol = policy_evict_first();
+      for (int it = 0; it < nstages; ++it) {
+        const int slot = it % kNST;
+        if (it >= kNST) mbar_wait_ab(&empty[slot], ((it / kNST) - 1) & 1, perr, abort_s);
+        const int tile = (int)blockIdx.x + (it / per_tile) * (int)gridDim.x;
+        const int kx = k0 + (it % per_tile) * KS;
+        mbar_arrive_expect_tx(&full[slot], kStage);
 #pragma unroll
-  for (int j = 0; j < MT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const int g = lane >> 2, t = lane & 3;
-  const int r1 = warp * 16 + g;
-  bool ok = true;
-  for (int b = 0; b < nblk; ++b) {
-    if (!mbar_wait(&bars[b], 0, d.err)) {
-      ok = false;
-      break;
-    }
-    const uint8_t* wb = wsm + b * (kRows * kBlkK);
-    const uint4 lo0 = *reinterpret_cast<const uint4*>(wb + r1 * kBlkK + (((2 * t) ^ g) << 4));
-    const uint4 lo1 = *reinterpret_cast<const uint4*>(wb + r1 * kBlkK + (((2 * t + 1) ^ g) << 4));
-    const uint4 hi0 = *reinterpret_cast<const uint4*>(wb + (r1 + 8) * kBlkK + (((2 * t) ^ g) << 4));
-    const uint4 hi1 = *reinterpret_cast<const uint4*>(wb + (r1 + 8) * kBlkK + (((2 * t + 1) ^ g) << 4));
-    const uint32_t wa[8] = {lo0.x, lo0.y, lo0.z, lo0.w, lo1.x, lo1.y, lo1.z, lo1.w};
-    const uint32_t wc[8] = {hi0.x, hi0.y, hi0.z, hi0.w, hi1.x, hi1.y, hi1.z, hi1.w};
-    uint32_t xw[MT][16];
-#pragma unroll
-    for (int j = 0; j < MT; ++j) {
-      const uint8_t* xr = xsm + (8 * j + g) * L.xp;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + xchunk(16 * b + 4 * t + i) * 16);
-        xw[j][4 * i + 0] = v.x;
-        xw[j][4 * i + 1] = v.y;
-        xw[j][4 * i + 2] = v.z;
-        xw[j][4 * i + 3] = v.w;
+        for (int b = 0; b < 4; ++b)
+          tma_load_2d(ring + slot * kStage + b * kBoxBytes, &wmap, kx + (b / RT) * kBox,
+                      (RT == 2 && (b % RT) == 1 ? half_n : 0) + tile * kTileRows, &full[slot], pol);
       }
     }
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      uint32_t a0, a1, a2, a3;
-      i8x4_to_h2x2(wa[s], a0, a2);
-      i8x4_to_h2x2(wc[s], a1, a3);
-#pragma unroll
-      for (int j = 0; j < MT; ++j) mma_16816(acc[j], a0, a1, a2, a3, xw[j][2 * s], xw[j][2 * s + 1]);
-    }
-  }
-  if (!ok) {
-    // drain: give every outstanding TMA block one more bounded chance, then leave
-    for (int b = 0; b < nblk; ++b) mbar_wait(&bars[b], 0, nullptr);
+    pdl_wait();
     return;
   }
-#pragma unroll
-  for (int j = 0; j < MT; ++j) {
-    const int m = 8 * j + 2 * t;
-    acc_s[r1 * MP + m] = acc[j][0];
-    acc_s[r1 * MP + m + 1] = acc[j][1];
-    acc_s[(r1 + 8) * MP + m] = acc[j][2];
-    acc_s[(r1 + 8) * MP + m + 1] = acc[j][3];
-  }
-  __syncthreads();
 
-  // ---- split-K fixup: last CTA of this tile sums the partials in split order
-  if (P.nsplit > 1) {
-    float* ws = reinterpret_cast<float*>(d.ws);
-    const int per = kRows * M;
-    float* mine = ws + ((int64_t)split * P.ntiles + tile) * per;
-    for (int i = tid; i < per; i += kThreads) mine[i] = acc_s[(i / M) * MP + (i % M)];
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int prev = atomicAdd(&d.counters[tile], 1);
-      flag_s[0] = (prev == P.nsplit - 1);
-    }
-    __syncthreads();
-    if (!flag_s[0]) return;
-    __threadfence();
-    for (int i = tid; i < per; i += kThreads) {
-      float a = 0.f;
-      for (int sp = 0; sp < P.nsplit; ++sp) a += __ldcg(ws + ((int64_t)sp * P.ntiles + tile) * per + i);
-      acc_s[(i / M) * MP + (i % M)] = a;
-    }
-    if (tid == 0) d.counters[tile] = 0;
-    __syncthreads();
-  }
+  // ================================================================ consumer warps
+  pdl_trigger();
+  pdl_wait();  // activations, tokens and sums of squares come from earlier launches
 
-  // ---- epilogues
-  if (EPI == HM_EPI_STORE) {
-    __half* y = reinterpret_cast<__half*>(d.y);
-    const __half* res = reinterpret_cast<const __half*>(d.res);
-    for (int i = tid; i < kRows * M; i += kThreads) {
-      const int r = i & (kRows - 1), m = i >> 6;
-      const int n = r0a + r;
-      float sq = 0.f;
-      if (n < d.N) {
-        __half v = __float2half_rn(acc_s[r * MP + m] * scale_s[r]);
-        if (res) v = hadd_rn(v, res[(int64_t)m * d.ldres + n]);
-        y[(int64_t)m * d.ldy + n] = v;
-        const float vf = __half2float(v);
-        sq = vf * vf;
-      }
-      sq_s[m * kRows + r] = sq;
-    }
-    if (d.ss_out) {
-      __syncthreads();
-      for (int m = warp; m < M; m += kThreads / 32) {
-        const float a = warp_sum(sq_s[m * kRows + lane] + sq_s[m * kRows + lane + 32]);
-        if (lane == 0) d.ss_out[(int64_t)tile * d.ss_out_ld + m] = a;
-      }
-    }
-  } else if (EPI == HM_EPI_ROPE_KV) {
-    const int hd = d.hd, qw = d.Hq * hd, kw = d.Hk * hd;
-    __half* qo = reinterpret_cast<__half*>(d.q_out);
-    __half* kc = reinterpret_cast<__half*>(d.kc);
-    __half* vc = reinterpret_cast<__half*>(d.vc);
-    for (int i = tid; i < (kRows / 2) * M; i += kThreads) {
-      const int r = 2 * (i & 31), m = i >> 5;
-      const int n = r0a + r;
-      if (n >= d.N) continue;
-      const float x0 = __half2float(__float2half_rn(acc_s[r * MP + m] * scale_s[r]));
-      const float x1 = __half2float(__float2half_rn(acc_s[(r + 1) * MP + m] * scale_s[r + 1]));
-      const int64_t p = d.pos[m];
-      const int bb = m / d.S;
-      if (p < 0 || p >= d.L || p >= d.rope_rows) {
-        report_error(d.err, HM_ERR_BADINDEX);
-        continue;
-      }
-      const int dh = n % hd;
-      if (n < qw + kw) {
-        const float* cs = d.rope + (p * (hd / 2) + dh / 2) * 2;
-        const float c = cs[0], sn = cs[1];
-        const __half y0 = __float2half_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-        const __half y1 = __float2half_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
-        __half* dst;
-        if (n < qw) {
-          dst = qo + (int64_t)m * qw + n;
+  // Parameter fields are copied to registers / shared memory once: the inline-asm
+  // copies and barriers below clobber memory, which would otherwise force a reload
+  // of every field through the parameter block on each loop iteration.
+  const int K = d.K, N = d.N;
+  int* const err = d.err;
+
+  // ---- per-row sources resolved once: row pointer, mode, source index, embedding scale
+  if (tid < MROWS) {
+    const int m = tid;
+    int mode = -1;  // -1: padding row or rejected id -> zeros
+    int sel = 0;
+    const uint8_t* base = nullptr;
+    float esc = 0.f;
+    if (m < M) {
+      int row;
+      const hm_row_src& s = src_of(d, m, row, sel);
+      mode = s.mode;
+      if (mode == HM_SRC_EMB) {
+        const int64_t id = s.tok[(int64_t)row * s.tok_ld + s.tok_col] + s.tok_off;
+        if (id < 0 || id >= s.erows) {
+          report_error(err, HM_ERR_BADINDEX);
+          mode = -1;
         } else {
-          const int kh = (n - qw) / hd;
-          dst = kc + (((int64_t)bb * d.Hk + kh) * d.L + p) * hd + dh;
+          base = reinterpret_cast<const uint8_t*>(s.etab + id * (int64_t)K);
+          esc = __half2float(reinterpret_cast<const __half*>(s.escale)[id]);
         }
-        dst[0] = y0;
-        dst[1] = y1;
       } else {
-        const int kh = (n - qw - kw) / hd;
-        __half* dst = vc + (((int64_t)bb * d.Hk + kh) * d.L + p) * hd + dh;
-        dst[0] = __float2half_rn(x0);
-        dst[1] = __float2half_rn(x1);
+        base = reinterpret_cast<const uint8_t*>(reinterpret_cast<const __half*>(s.x) + (int64_t)row * s.ldx);
       }
     }
-  } else {  // HM_EPI_SILU
-    __half* y = reinterpret_cast<__half*>(d.y);
-    for (int i = tid; i < kBoxRows * M; i += kThreads) {
-      const int jj = i & 31, m = i >> 5;
-      const __half a = __float2half_rn(acc_s[jj * MP + m] * scale_s[jj]);
-      const __half bv = __float2half_rn(acc_s[(kBoxRows + jj) * MP + m] * scale_s[kBoxRows + jj]);
-      const float af = __half2float(a);
-      const __half sl = __float2half_rn(__fdiv_rn(af, __fadd_rn(1.0f, expf(-af))));
-      y[(int64_t)m * d.ldy + r0a + jj] = hmul_rn(sl, bv);
+    rmode_s[m] = mode;
+    rsel_s[m] = sel;
+    rowp_s[m] = base;
+    esc_s[m] = esc;
+  }
+  const __half* gam0 = reinterpret_cast<const __half*>(d.src[0].gamma);
+  const __half* gam1 = reinterpret_cast<const __half*>(d.src[1].gamma);
+  const bool g0 = P.has_gamma && d.src[0].mode == HM_SRC_RMS;
+  const bool g1 = P.has_gamma && d.interleave && d.src[1].mode == HM_SRC_RMS;
+  named_bar(kBarCons, kCons);
+
+  // ---- issue every copy of the activation k-range [MROWS][kspan] (swizzled 16-byte chunks):
+  // fp16 rows 16 B per chunk, int8 embedding rows 8 B into the first half of the chunk
+  const int cpr = kspan / 8;
+  const int kend = min(kspan, K - k0);  // valid columns of this k-range (a multiple of 8)
+  for (int m = 0; m < MROWS; ++m) {
+    const int mode = rmode_s[m];
+    const uint8_t* base = rowp_s[m];
+    uint8_t* xr = xsm + m * L.xp;
+    for (int c = tid; c < cpr; c += kCons) {
+      uint8_t* dst = xr + xchunk(c) * 16;
+      if (mode < 0 || 8 * c >= kend)
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      else if (mode == HM_SRC_EMB)
+        cp_async8(dst, base + k0 + 8 * c);
+      else
+        cp_async16(dst, base + 2 * (k0 + 8 * c));
     }
+  }
+  for (int c = tid; c < cpr; c += kCons) {
+    if (8 * c >= kend) continue;
+    if (g0) cp_async16(gam_s + 8 * c, gam0 + k0 + 8 * c);
+    if (g1) cp_async16(gam_s + kspan + 8 * c, gam1 + k0 + 8 * c);
+  }
+  // ---- RMSNorm 1/rms of RMS rows from the producers' ss partials, while the copies fly
+  for (int m = warp; m < M; m += kCons / 32) {
+    int row, sel;
+    const hm_row_src& s = src_of(d, m, row, sel);
+    if (s.mode != HM_SRC_RMS) continue;
+    const float* ss = s.ss;
+    const int tiles = s.ss_tiles;
+    const int64_t ld = s.ss_ld;
+    const float dim = static_cast<float>(s.dim), eps = s.eps;
+    float a = 0.f;
+    for (int t = lane; t < tiles; t += 32) a += ss[(int64_t)t * ld + row];
+    a = warp_sum(a);
+    if (lane == 0) inv_s[m] = 1.0f / sqrtf(a / dim + eps);
+  }
+  cp_async_wait_all();
+  named_bar(kBarCons, kCons);
+
+  // ---- in-place transforms: RMSNorm (fp16(x*inv) * gamma) and int8 -> fp16 embedding rows
+  for (int m = 0; m < M; ++m) {
+    const int mode = rmode_s[m];
+    if (mode != HM_SRC_RMS && mode != HM_SRC_EMB) continue;
+    uint8_t* xr = xsm + m * L.xp;
+    if (mode == HM_SRC_RMS) {
+      const float inv = inv_s[m];
+      const __half* gs = gam_s + rsel_s[m] * kspan;
+      for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
+        uint4* slot = reinterpret_cast<uint4*>(xr + xchunk(c) * 16);
+        uint4 v = *slot;
+        const uint4 gv = *reinterpret_cast<const uint4*>(gs + 8 * c);
+        __half* vh = reinterpret_cast<__half*>(&v);
+        const __half* gh = reinterpret_cast<const __half*>(&gv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vh[j] = hmul_rn(__float2half_rn(__half2float(vh[j]) * inv), gh[j]);
+        *slot = v;
+      }
+    } else {
+      const float sc = esc_s[m];
+      for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
+        uint4* slot = reinterpret_cast<uint4*>(xr + xchunk(c) * 16);
+        const uint2 q = *reinterpret_cast<const uint2*>(slot);
+        const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
+        uint4 v;
+        __half* vh = reinterpret_cast<__half*>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vh[j] = __float2half_rn(static_cast<float>(qb[j]) * sc);
+        *slot = v;
+      }
+    }
+  }
+  named_bar(kBarCons, kCons);
+
+  // epilogue parameters, in registers for the whole tile loop
+  const __half* const scales = reinterpret_cast<const __half*>(d.s);
+  __half* const yout = reinterpret_cast<__half*>(d.y);
+  const int64_t ldy = d.ldy, ldres = d.ldres, ss_ld = d.ss_out_ld;
+  const __half* const resid = reinterpret_cast<const __half*>(d.res);
+  float* const ss_out = d.ss_out;
+  float* const wsp = reinterpret_cast<float*>(d.ws);
+  int* const counters = d.counters;
+  struct RopeP {
+    int hd, qw, kw, S, L, Hk, rope_rows;
+    const int64_t* pos;
+    const float* rope;
+    __half *qo, *kc, *vc;
+  } rp{};
+  if (EPI == HM_EPI_ROPE_KV) {
+    rp.hd = d.hd;
+    rp.qw = d.Hq * d.hd;
+    rp.kw = d.Hk * d.hd;
+    rp.S = d.S;
+    rp.L = d.L;
+    rp.Hk = d.Hk;
+    rp.rope_rows = d.rope_rows;
+    rp.pos = d.pos;
+    rp.rope = d.rope;
+    rp.qo = reinterpret_cast<__half*>(d.q_out);
+    rp.kc = reinterpret_cast<__half*>(d.kc);
+    rp.vc = reinterpret_cast<__half*>(d.vc);
+  }
+
+  // ---- tiles: warp w consumes box w of every stage (row block w % RT, k slice w / RT)
+  const int g = lane >> 2, t = lane & 3;
+  const int rb = warp % RT, ksub = warp / RT;
+  // epilogue ownership: thread -> (row r of the 16, rows m = m0, m0 + 8, ...)
+  const int er = tid & 15, em0 = tid >> 4;
+  int it = 0;
+  for (int ti = 0; ti < my_tiles; ++ti) {
+    const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
+    // scales this thread's epilogue needs (immutable, prefetched while the tile streams)
+    const int n0 = tile * kTileRows + er;
+    const int n1 = (RT == 2 ? N / 2 : 0) + tile * kTileRows + er;
+    const float sc0 = n0 < N ? __half2float(scales[n0]) : 0.f;
+    const float sc1 = (RT == 2 && n1 < N) ? __half2float(scales[n1]) : 0.f;
+    float acc[MT][4];
+#pragma unroll
+    for (int j = 0; j < MT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int st = 0; st < per_tile; ++st, ++it) {
+      const int slot = it % kNST;
+      mbar_wait_ab(&full[slot], (it / kNST) & 1, err, abort_s);  // on timeout: carry on, error flagged
+      const uint8_t* wb = ring + slot * kStage + warp * kBoxBytes;
+      const uint4 lo0 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t) ^ g) << 4));
+      const uint4 lo1 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + 1) ^ g) << 4));
+      const uint4 hi0 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t) ^ g) << 4));
+      const uint4 hi1 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t + 1) ^ g) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);  // this warp's box is in registers now
+      const uint32_t wa[8] = {lo0.x, lo0.y, lo0.z, lo0.w, lo1.x, lo1.y, lo1.z, lo1.w};
+      const uint32_t wc[8] = {hi0.x, hi0.y, hi0.z, hi0.w, hi1.x, hi1.y, hi1.z, hi1.w};
+      const int cb = (st * KS + ksub * kBox) / 8;  // first activation chunk of this box
+      uint32_t xw[MT][16];
+#pragma unroll
+      for (int j = 0; j < MT; ++j) {
+        const uint8_t* xr = xsm + (8 * j + g) * L.xp;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xr + xchunk(cb + 4 * t + i) * 16);
+          xw[j][4 * i + 0] = v.x;
+          xw[j][4 * i + 1] = v.y;
+          xw[j][4 * i + 2] = v.z;
+          xw[j][4 * i + 3] = v.w;
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        uint32_t a0, a1, a2, a3;
+        i8x4_to_h2x2(wa[s], a0, a2);
+        i8x4_to_h2x2(wc[s], a1, a3);
+#pragma unroll
+        for (int j = 0; j < MT; ++j) mma_16816(acc[j], a0, a1, a2, a3, xw[j][2 * s], xw[j][2 * s + 1]);
+      }
+    }
+    // ---- partial sums of the four warps -> red_s[warp][row][m]
+    float* rw = red_s + warp * kTileRows * MP;
+#pragma unroll
+    for (int j = 0; j < MT; ++j) {
+      const int m = 8 * j + 2 * t;
+      rw[g * MP + m] = acc[j][0];
+      rw[g * MP + m + 1] = acc[j][1];
+      rw[(g + 8) * MP + m] = acc[j][2];
+      rw[(g + 8) * MP + m + 1] = acc[j][3];
+    }
+    named_bar(kBarCons, kCons);
+    // value of (row block b, row r, activation row m): warps b, b+RT, ... summed in order
+    auto tile_sum = [&](int b, int r, int m) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = b; w < 4; w += RT) a += red_s[(w * kTileRows + r) * MP + m];
+      return a;
+    };
+
+    // ---- split-K (only when the activations did not fit): last CTA sums partials in split order
+    bool owner = true;
+    if (P.nsplit > 1) {
+      float* ws = wsp;
+      const int per = RT * kTileRows * M;
+      float* mine = ws + ((int64_t)split * P.ntiles + tile) * per;
+      for (int i = tid; i < per; i += kCons) {
+        const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
+        mine[i] = tile_sum(b, r, m);
+      }
+      __threadfence();
+      named_bar(kBarCons, kCons);
+      if (tid == 0) flag_s[0] = (atomicAdd(&counters[tile], 1) == P.nsplit - 1);
+      named_bar(kBarCons, kCons);
+      owner = flag_s[0] != 0;
+      if (owner) {
+        __threadfence();
+        for (int i = tid; i < per; i += kCons) {
+          const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
+          float a = 0.f;
+          for (int sp = 0; sp < P.nsplit; ++sp) a += __ldcg(ws + ((int64_t)sp * P.ntiles + tile) * per + i);
+          red_s[(b * kTileRows + r) * MP + m] = a;  // warp-b slot now holds the full sum
+        }
+        if (tid == 0) counters[tile] = 0;
+        named_bar(kBarCons, kCons);
+      }
+    }
+    auto value = [&](int b, int r, int m) {
+      return P.nsplit > 1 ? red_s[(b * kTileRows + r) * MP + m] : tile_sum(b, r, m);
+    };
+
+    // ---- epilogues (the owner of the tile only)
+    if (owner) {
+      if (EPI == HM_EPI_STORE) {
+        __half* y = yout;
+        const __half* res = resid;
+        const int n = n0;
+#pragma unroll
+        for (int q = 0; q < MT; ++q) {
+          const int m = em0 + 8 * q;
+          float sq = 0.f;
+          if (m < M && n < N) {
+            __half v = __float2half_rn(value(0, er, m) * sc0);
+            if (res) v = hadd_rn(v, res[(int64_t)m * ldres + n]);
+            y[(int64_t)m * ldy + n] = v;
+            const float vf = __half2float(v);
+            sq = vf * vf;
+          }
+          if (ss_out) {  // 16 consecutive lanes share m: sum over the tile's 16 columns
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            if (er == 0 && m < M) ss_out[(int64_t)tile * ss_ld + m] = sq;
+          }
+        }
+      } else if (EPI == HM_EPI_ROPE_KV) {
+        const int hd = rp.hd, qw = rp.qw, kw = rp.kw;
+        __half* qo = rp.qo;
+        __half* kc = rp.kc;
+        __half* vc = rp.vc;
+        // the pair (2i, 2i+1) is handled by the thread of row 2i; its partner row's
+        // scale comes from the neighbouring lane
+        const float sc_next = __shfl_down_sync(0xffffffffu, sc0, 1);
+#pragma unroll
+        for (int q = 0; q < MT; ++q) {
+          const int m = em0 + 8 * q;
+          const int n = n0;
+          if ((er & 1) || m >= M || n >= N) continue;
+          const float x0 = __half2float(__float2half_rn(value(0, er, m) * sc0));
+          const float x1 = __half2float(__float2half_rn(value(0, er + 1, m) * sc_next));
+          const int64_t p = rp.pos[m];
+          const int bb = m / rp.S;
+          if (p < 0 || p >= rp.L || p >= rp.rope_rows) {
+            report_error(err, HM_ERR_BADINDEX);
+            continue;
+          }
+          const int dh = n % hd;
+          if (n < qw + kw) {
+            const float* cs = rp.rope + (p * (hd / 2) + dh / 2) * 2;
+            const float c = cs[0], sn = cs[1];
+            const __half y0 = __float2half_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+            const __half y1 = __float2half_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+            __half* dst;
+            if (n < qw) {
+              dst = qo + (int64_t)m * qw + n;
+            } else {
+              const int kh = (n - qw) / hd;
+              dst = kc + (((int64_t)bb * rp.Hk + kh) * rp.L + p) * hd + dh;
+            }
+            dst[0] = y0;
+            dst[1] = y1;
+          } else {
+            const int kh = (n - qw - kw) / hd;
+            __half* dst = vc + (((int64_t)bb * rp.Hk + kh) * rp.L + p) * hd + dh;
+            dst[0] = __float2half_rn(x0);
+            dst[1] = __float2half_rn(x1);
+          }
+        }
+      } else {  // HM_EPI_SILU: row block 0 = w1 (a), row block 1 = w3 (b)
+        __half* y = yout;
+#pragma unroll
+        for (int q = 0; q < MT; ++q) {
+          const int m = em0 + 8 * q;
+          if (m >= M) continue;
+          const __half a = __float2half_rn(value(0, er, m) * sc0);
+          const __half bv = __float2half_rn(value(1, er, m) * sc1);
+          const float af = __half2float(a);
+          const __half sl = __float2half_rn(__fdiv_rn(af, __fadd_rn(1.0f, expf(-af))));
+          y[(int64_t)m * ldy + n0] = hmul_rn(sl, bv);
+        }
+      }
+    }
+    named_bar(kBarCons, kCons);  // red_s is reused by the next tile
   }
 }
 
@@ -405,7 +545,7 @@ bool weight_map(const int8_t* w, int N, int K, CUtensorMap* out) {
   CUtensorMap m;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
-  cuuint32_t box[2] = {kBlkK, kBoxRows};
+  cuuint32_t box[2] = {kBox, kTileRows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -429,45 +569,53 @@ int sm_count() {
   return n;
 }
 
-int ntiles_of(int N, int epi) { return epi == HM_EPI_SILU ? (N / 2) / kBoxRows : (N + kRows - 1) / kRows; }
-
-double min_ctas_frac() {
-  static double f = -1;
-  if (f < 0) {
-    const char* e = getenv("HM_GEMV_MIN_CTAS");
-    f = e ? atof(e) : 0.6;
-  }
-  return f;
+int ntiles_of(int N, int epi) {
+  return epi == HM_EPI_SILU ? (N / 2) / kTileRows : (N + kTileRows - 1) / kTileRows;
 }
 
-// K rounded up to whole 128-column TMA boxes (the tail is zero-filled)
-int padded_k(int K) { return (K + kBlkK - 1) / kBlkK * kBlkK; }
+double env_or(const char* name, double dflt) {
+  const char* e = getenv(name);
+  return e ? atof(e) : dflt;
+}
 
-int auto_kspan(int M, int N, int K, int epi) {
-  K = padded_k(K);
-  const int nt = ntiles_of(N, epi);
-  const int target = static_cast<int>(min_ctas_frac() * sm_count());
-  int best = 0;
-  for (int ks : {1024, 512, 256, 128}) {
-    if (K % ks) continue;
-    best = ks;
-    if (nt * (K / ks) >= target) return ks;
+int mrows_of(int M) { return M <= 8 ? 8 : (M <= 16 ? 16 : 32); }
+
+// K rounded up to whole stages (the tail is zero-filled by TMA and masked for x)
+int padded_k(int K, int epi) { return (K + ks_of(epi) - 1) / ks_of(epi) * ks_of(epi); }
+
+// The widest k-range (fewest splits) whose staged activations fit the budget.
+int auto_kspan(int M, int K, int epi) {
+  const int ks = ks_of(epi), kp = padded_k(K, epi), mr = mrows_of(M);
+  static const int budget = static_cast<int>(env_or("HM_GEMV_X_BUDGET", 136 * 1024));
+  for (int s = 1; s <= kp / ks; ++s) {
+    if ((kp / ks) % s) continue;
+    const int span = kp / s;
+    if (mr * (span * 2 + 16) <= budget) return span;
   }
-  (void)M;
-  return best;
+  return ks;
 }
 
 template <int MT, int EPI>
 cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p, cudaStream_t st) {
-  const SmemLayout L = smem_layout(p.kspan, 8 * MT);
-  static int configured_max = 0;
-  if (L.total > configured_max) {
+  const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma).total;
+  static int configured = 0;
+  if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smem_layout(kMaxKspan, 8 * MT).total);
+                                         227 * 1024);
     if (e != cudaSuccess) return e;
-    configured_max = smem_layout(kMaxKspan, 8 * MT).total;
+    configured = 227 * 1024;
   }
-  return hm_launch(gemv_i8_kernel<MT, EPI>, dim3(p.ntiles, p.nsplit), dim3(kThreads), L.total, st, p.d.pdl, map, p);
+  // one wave: CTAs per SM from the occupancy calculator (capped), tiles strided over the grid
+  int occ = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<MT, EPI>, kThreads, smem) != cudaSuccess ||
+      occ < 1)
+    occ = 1;
+  static const int cap = static_cast<int>(env_or("HM_GEMV_CTAS_PER_SM", 2));
+  const int per_sm = occ < cap ? occ : cap;
+  int J = per_sm * sm_count() / p.nsplit;
+  if (J < 1) J = 1;
+  if (J > p.ntiles) J = p.ntiles;
+  return hm_launch(gemv_i8_kernel<MT, EPI>, dim3(J, p.nsplit), dim3(kThreads), smem, st, p.d.pdl, map, p);
 }
 
 template <int EPI>
@@ -482,8 +630,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 extern "C" int hm_gemv_pick_kspan(int M, int N, int K, int epi, int kspan) {
+  (void)N;
   if (kspan > 0) return kspan;
-  return auto_kspan(M, N, K, epi);
+  return auto_kspan(M, K, epi);
 }
 
 extern "C" int hm_gemv_counters(int N, int epi) { return ntiles_of(N, epi); }
@@ -491,40 +640,46 @@ extern "C" int hm_gemv_counters(int N, int epi) { return ntiles_of(N, epi); }
 extern "C" size_t hm_gemv_workspace_bytes(int M, int N, int K, int epi, int kspan) {
   const int ks = hm_gemv_pick_kspan(M, N, K, epi, kspan);
   if (ks <= 0) return 0;
-  const int nsplit = padded_k(K) / ks;
+  const int nsplit = padded_k(K, epi) / ks;
   if (nsplit <= 1) return 0;
-  return static_cast<size_t>(nsplit) * ntiles_of(N, epi) * kRows * M * sizeof(float);
+  return static_cast<size_t>(nsplit) * ntiles_of(N, epi) * rt_of(epi) * kTileRows * M * sizeof(float);
 }
 
 extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
   if (!d || !d->w || !d->s || d->M < 1 || d->M > kMaxM || d->N < 1 || d->K < 16 || d->K % 16) return HM_EARG;
   if (!aligned16(d->w)) return HM_EARG;
-  if (d->epi == HM_EPI_SILU && (d->N % (2 * kBoxRows) || !d->y)) return HM_EARG;
+  if (d->epi == HM_EPI_SILU && (d->N % (2 * kTileRows) || !d->y)) return HM_EARG;
   if (d->epi == HM_EPI_STORE && !d->y) return HM_EARG;
-  if (d->epi == HM_EPI_STORE && d->ss_out && d->N % kRows) return HM_EARG;
+  if (d->epi == HM_EPI_STORE && d->ss_out && d->N % kTileRows) return HM_EARG;
   if (d->epi == HM_EPI_ROPE_KV &&
-      (!d->rope || !d->pos || !d->q_out || !d->kc || !d->vc || d->hd % 64 || d->S < 1 ||
+      (!d->rope || !d->pos || !d->q_out || !d->kc || !d->vc || d->hd % kTileRows || d->S < 1 ||
        d->N != (d->Hq + 2 * d->Hk) * d->hd))
     return HM_EARG;
+  int has_gamma = 0;
   for (int i = 0; i < (d->interleave ? 2 : 1); ++i) {
     const hm_row_src& s = d->src[i];
     if (s.mode == HM_SRC_EMB) {
       if (!s.etab || !s.escale || !s.tok || (reinterpret_cast<uintptr_t>(s.etab) & 7u)) return HM_EARG;
     } else {
       if (!s.x || !aligned16(s.x) || (s.ldx % 8)) return HM_EARG;
-      if (s.mode == HM_SRC_RMS && (!s.ss || !s.gamma || !aligned16(s.gamma) || s.dim <= 0)) return HM_EARG;
+      if (s.mode == HM_SRC_RMS) {
+        if (!s.ss || !s.gamma || !aligned16(s.gamma) || s.dim <= 0) return HM_EARG;
+        has_gamma = 1;
+      }
     }
   }
   GemvParams p;
   p.d = *d;
-  const int kpad = padded_k(d->K);
+  p.has_gamma = has_gamma;
+  const int kpad = padded_k(d->K, d->epi);
   p.kspan = hm_gemv_pick_kspan(d->M, d->N, d->K, d->epi, d->kspan);
-  if (p.kspan <= 0 || p.kspan > kMaxKspan || p.kspan % kBlkK || kpad % p.kspan) return HM_EARG;
+  if (p.kspan <= 0 || p.kspan % ks_of(d->epi) || kpad % p.kspan) return HM_EARG;
+  if (smem_layout(p.kspan, mrows_of(d->M), has_gamma).total > 227 * 1024) return HM_EARG;
   p.nsplit = kpad / p.kspan;
   p.ntiles = ntiles_of(d->N, d->epi);
   if (p.nsplit > 1) {
     if (!d->ws || !d->counters || d->n_counters < p.ntiles ||
-        d->ws_bytes < static_cast<size_t>(p.nsplit) * p.ntiles * kRows * d->M * sizeof(float))
+        d->ws_bytes < hm_gemv_workspace_bytes(d->M, d->N, d->K, d->epi, p.kspan))
       return HM_EARG;
   }
   CUtensorMap map;
@@ -585,4 +740,4 @@ extern "C" size_t hm_abi_layout(int which) {
   }
 }
 
-extern "C" const char* hm_version(void) { return "heartmula_b200 0.1 sm_100a"; }
+extern "C" const char* hm_version(void) { return "heartmula_b200 0.2 sm_100a"; }

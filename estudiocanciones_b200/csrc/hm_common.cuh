@@ -55,6 +55,10 @@ HM_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+HM_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 HM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -80,6 +84,27 @@ HM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   return false;
 }
 
+// Bounded wait that never strands a CTA: the first wait to time out sets a
+// CTA-wide abort flag in shared memory and every later wait returns at once.
+// Callers carry on (computing garbage that the error word flags) instead of
+// returning early, so every thread still reaches every barrier and the kernel
+// ends in bounded time.
+HM_DEV bool mbar_wait_ab(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 28); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > HM_WAIT_NS) break;
+    }
+  }
+  *abort_flag = 1;
+  report_error(err, HM_ERR_TIMEOUT);
+  return false;
+}
+
 // ---------------------------------------------------------------- TMA
 // 2-D tiled load global -> shared, completion counted on `bar` (bytes).
 // x is the innermost coordinate (elements); callers keep x*elem_size % 16 == 0.
@@ -98,6 +123,23 @@ HM_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+
+// Ampere-style asynchronous copies (global -> shared), completed with wait_all.
+HM_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+HM_DEV void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+HM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Arrive on `bar` once every cp.async this thread issued so far has landed
+// (the barrier's expected count includes this arrival).
+HM_DEV void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Barrier over the first `n` threads of the CTA (id 0 is __syncthreads').
+HM_DEV void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 HM_DEV uint64_t policy_evict_first() {
   uint64_t p;

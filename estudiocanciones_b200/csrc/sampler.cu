@@ -79,23 +79,32 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
   pdl_trigger();
   pdl_wait();
   const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool mix = P.B == 2 * P.N;
+  // parameters in registers (the block barriers below would force re-reads otherwise)
+  const int V = P.V, Nt = P.N, topk = P.topk;
+  const bool mix = P.B == 2 * Nt;
+  const float cfg = P.cfg, temp = P.temp;
+  const __half* const logits = P.logits;
+  const int64_t ldl = P.ld_logits, ldn = P.ld_noise, out_ld = P.out_ld;
+  const float* const noise = P.noise;
+  int64_t* const outp = P.out;
+  const int out_col = P.out_col;
+  int* const err = P.err;
   float l[kPer];
   uint32_t key[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int v = tid + j * kThreads;
     float val = -INFINITY;
-    if (v < P.V) {
-      const __half c = P.logits[(int64_t)n * P.ld_logits + v];
+    if (v < V) {
+      const __half c = logits[(int64_t)n * ldl + v];
       __half g = c;
       if (mix) {
-        const __half u = P.logits[(int64_t)(n + P.N) * P.ld_logits + v];
+        const __half u = logits[(int64_t)(n + Nt) * ldl + v];
         const __half d = __hsub(c, u);
-        const __half e = __float2half_rn(__half2float(d) * P.cfg);
+        const __half e = __float2half_rn(__half2float(d) * cfg);
         g = __hadd(u, e);
       }
-      val = __fdiv_rn(__half2float(g), P.temp);
+      val = __fdiv_rn(__half2float(g), temp);
     }
     l[j] = val;
     key[j] = f2key(val);
@@ -103,14 +112,14 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
 
   // ---- radix select of the topk-th largest key, 8 bits per pass from the top
   uint32_t prefix = 0, pmask = 0;
-  int kk = P.topk;
+  int kk = topk;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       const int v = tid + j * kThreads;
-      const bool in = v < P.V && (key[j] & pmask) == prefix;
+      const bool in = v < V && (key[j] & pmask) == prefix;
       const uint32_t dig = (key[j] >> shift) & 255u;
       const uint32_t act = __ballot_sync(0xffffffffu, in);
       if (in) {
@@ -193,8 +202,8 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int v = tid + j * kThreads;
-    if (v < P.V) {
-      const float r = __fdiv_rn(__fdiv_rn(l[j], s2), P.noise[(int64_t)n * P.ld_noise + v]);
+    if (v < V) {
+      const float r = __fdiv_rn(__fdiv_rn(l[j], s2), noise[(int64_t)n * ldn + v]);
       if (better(r, v, best, bi)) {
         best = r;
         bi = v;
@@ -228,12 +237,12 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
       }
     }
     if (lane == 0) {
-      if (bi < 0 || bi >= P.V) {
-        report_error(P.err, HM_ERR_BADINDEX);
+      if (bi < 0 || bi >= V) {
+        report_error(err, HM_ERR_BADINDEX);
         bi = 0;
       }
-      P.out[(int64_t)n * P.out_ld + P.out_col] = bi;
-      if (mix) P.out[(int64_t)(n + P.N) * P.out_ld + P.out_col] = bi;
+      outp[(int64_t)n * out_ld + out_col] = bi;
+      if (mix) outp[(int64_t)(n + Nt) * out_ld + out_col] = bi;
     }
   }
 }

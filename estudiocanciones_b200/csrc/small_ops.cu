@@ -95,13 +95,13 @@ __global__ void emb_gather_kernel(const int64_t* __restrict__ idx, const int8_t*
 }
 
 // Sum of the n_cb codebook embeddings of each row (fp32 accumulation, one
-// rounding) and per-64-column sums of squares of the fp16 result.
+// rounding) and per-16-column sums of squares of the fp16 result (the
+// granularity every residual-stream producer writes for the fused RMSNorm).
 __global__ void __launch_bounds__(256) emb_sum_kernel(const int64_t* __restrict__ tok, int64_t tok_ld, int ncb,
                                                       int64_t vocab, const int8_t* __restrict__ tab,
                                                       const __half* __restrict__ scale, int64_t rows, int D,
                                                       __half* __restrict__ x, float* __restrict__ ss, int64_t ss_ld,
                                                       int* err) {
-  __shared__ float red[8];
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.y, tid = threadIdx.x;
@@ -120,14 +120,10 @@ __global__ void __launch_bounds__(256) emb_sum_kernel(const int64_t* __restrict_
   const __half v = __float2half_rn(a);
   if (k < D) x[(int64_t)r * D + k] = v;
   if (ss) {
-    const float vf = k < D ? __half2float(v) : 0.f;
-    const float q = warp_sum(vf * vf);
-    if ((tid & 31) == 0) red[tid >> 5] = q;
-    __syncthreads();
-    if (tid < 4) {
-      const int t = blockIdx.x * 4 + tid;
-      if (t * 64 < D) ss[(int64_t)t * ss_ld + r] = red[2 * tid] + red[2 * tid + 1];
-    }
+    float q = k < D ? __half2float(v) * __half2float(v) : 0.f;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if ((tid & 15) == 0 && k < D) ss[(int64_t)(k / 16) * ss_ld + r] = q;
   }
 }
 
@@ -195,7 +191,7 @@ extern "C" int hm_emb_gather_i8(const int64_t* idx, int n, const int8_t* tab, co
 extern "C" int hm_emb_sum_i8(const int64_t* tok, int64_t tok_ld, int R, int ncb, int64_t vocab, const int8_t* tab,
                              const void* scale, int64_t rows, int D, void* x_out, float* ss_out, int64_t ss_ld,
                              int* err, int pdl, hm_stream_t stream) {
-  if (!tok || !tab || !scale || !x_out || R < 1 || ncb < 1 || D < 1 || (ss_out && D % 64)) return HM_EARG;
+  if (!tok || !tab || !scale || !x_out || R < 1 || ncb < 1 || D < 1 || (ss_out && D % 16)) return HM_EARG;
   const cudaError_t e = hm_launch(emb_sum_kernel, dim3((D + 255) / 256, R), dim3(256), 0, stream, pdl, tok, tok_ld,
                                   ncb, vocab, tab, reinterpret_cast<const __half*>(scale), rows, D,
                                   reinterpret_cast<__half*>(x_out), ss_out, ss_ld, err);

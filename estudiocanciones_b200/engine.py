@@ -32,6 +32,7 @@ from .prefill import prefill_backbone
 from .rope import rope_table
 
 EPS = 1e-5
+SS_COLS = 16   # columns per sum-of-squares partial written by residual-stream producers
 
 
 def _p(t):
@@ -126,6 +127,7 @@ class Stack:
     def L(self):
         return self.blocks[0].kc.shape[2]
 
+    @torch.inference_mode()
     def decode(self, x, pos, S, nsplit=None):
         """``Stack.decode`` (``app/engine.py:180-211``): x ``[R, D]`` fp16, row r -> batch r // S,
         pos ``[R]`` int64 on the device.  Returns ``rms(x_out, norm)``; caches are updated in place."""
@@ -148,10 +150,11 @@ class Stack:
 
 # ----------------------------------------------------------------------------- buffers and plan
 def default_nsplit(R, Hk, L, sms=None):
-    """Split count for decode attention: about two CTAs per SM, at most one split per 32 positions."""
+    """Split count for decode attention: about four CTAs per SM (a short chain of
+    K/V tiles per CTA), at most one split per 64 cache positions."""
     if sms is None:
         sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    return int(max(1, min(math.ceil(2 * sms / max(1, R * Hk)), max(1, L // 32), 64)))
+    return int(max(1, min(math.ceil(4 * sms / max(1, R * Hk)), max(1, L // 64), 64)))
 
 
 class _Ctx:
@@ -196,14 +199,14 @@ class _Ctx:
 
 
 class StackBuffers:
-    """Residual stream, its per-64-column sums of squares, and per-layer scratch of one stack."""
+    """Residual stream, its per-16-column sums of squares, and per-layer scratch of one stack."""
 
     def __init__(self, stack: Stack, rows: int, dev):
         b0 = stack.blocks[0]
         D = stack.dim
         self.rows = rows
         self.x = torch.zeros(rows, D, device=dev, dtype=torch.float16)
-        self.ss = torch.zeros(D // 64, rows, device=dev, dtype=torch.float32)
+        self.ss = torch.zeros(D // SS_COLS, rows, device=dev, dtype=torch.float32)
         self.q = torch.empty(rows, b0.h * b0.hd, device=dev, dtype=torch.float16)
         self.o = torch.empty_like(self.q)
         self.mm = torch.empty(rows, b0.ffn, device=dev, dtype=torch.float16)
@@ -283,7 +286,7 @@ class FramePlan:
         """ss partials of an fp16 matrix that no fused producer wrote (API entry points)."""
         def op(st, x=x, ss=ss, R=R):
             D = x.shape[1]
-            part = (x[:R].float() ** 2).reshape(R, D // 64, 64).sum(-1)
+            part = (x[:R].float() ** 2).reshape(R, D // SS_COLS, SS_COLS).sum(-1)
             ss[:, :R].copy_(part.t())
         self.ops.append(op)
 
@@ -403,6 +406,7 @@ class HeartMuLaLite:
         return tot + self.projection.nbytes
 
     # ------------------------------------------------------------------ reference-shaped entry points
+    @torch.inference_mode()
     def _step(self, tok, pos, bucket=None, cfg=1.5, topk=50, temp=1.0):
         """One frame from the previous frame's tokens ``tok [B, 8]`` at ``pos [B, 1]``
         (``app/engine.py:345-349``).  Returns ``[B, 8]`` int64 (a static buffer)."""
@@ -412,6 +416,7 @@ class HeartMuLaLite:
         rt.plan_for(cfg, topk, temp, with_backbone=True, commit=False).run()
         return rt.tok_out
 
+    @torch.inference_mode()
     def _frame_fast(self, last_h, cfg=1.5, topk=50, temp=1.0):
         """Codebook heads + local decoder from the backbone's normalised state ``last_h [B, D]``
         (``app/engine.py:328-343``)."""

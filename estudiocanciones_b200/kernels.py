@@ -72,7 +72,8 @@ def read_errors(device, clear: bool = True) -> int:
     e = error_word(device)
     v = int(e.item())
     if clear and v:
-        e.zero_()
+        with torch.inference_mode():   # the word may have been created under inference mode
+            e.zero_()
     return v
 
 

@@ -22,7 +22,7 @@ def prefill_backbone(model, h: torch.Tensor) -> None:
     if rt is None:
         raise HMError("alloc() first")
     B, P, D = h.shape
-    from .engine import FramePlan
+    from .engine import SS_COLS, FramePlan
     plan = rt.plans.get("prefill_step")
     if plan is None:
         plan = FramePlan(rt.ctx)
@@ -33,7 +33,7 @@ def prefill_backbone(model, h: torch.Tensor) -> None:
     def load(p):
         x_in.copy_(h[:, p])
         rt.x_bb.copy_(x_in)
-        rt.ss_bb.copy_((x_in.float() ** 2).reshape(B, D // 64, 64).sum(-1).t())
+        rt.ss_bb.copy_((x_in.float() ** 2).reshape(B, D // SS_COLS, SS_COLS).sum(-1).t())
         rt.pos.fill_(p)
 
     if P <= 2:
@@ -50,7 +50,7 @@ def prefill_backbone(model, h: torch.Tensor) -> None:
     with torch.cuda.stream(s):
         with torch.cuda.graph(g, stream=s):
             rt.x_bb.copy_(x_in)
-            rt.ss_bb.copy_((x_in.float() ** 2).reshape(B, D // 64, 64).sum(-1).t())
+            rt.ss_bb.copy_((x_in.float() ** 2).reshape(B, D // SS_COLS, SS_COLS).sum(-1).t())
             plan.run()
     torch.cuda.current_stream().wait_stream(s)
     for p in range(1, P):

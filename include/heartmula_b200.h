@@ -70,7 +70,7 @@ typedef struct {
   int64_t tok_off;
 } hm_row_src;
 
-#define HM_EPI_STORE 0   /* y = fp16(acc*s) (+res); optional per-64-column sum of squares */
+#define HM_EPI_STORE 0   /* y = fp16(acc*s) (+res); optional per-16-column sum of squares */
 #define HM_EPI_ROPE_KV 1 /* fused qkv: RoPE q -> q_out, RoPE k / copy v -> cache slot pos (app/kernels.py:79-107) */
 #define HM_EPI_SILU 2    /* fused w1|w3: y[m,j] = fp16(silu(a)) * b (app/kernels.py:172-180) */
 
@@ -85,7 +85,7 @@ typedef struct {
   int64_t ldy;
   const void* res;              /* STORE: optional residual (may alias y) */
   int64_t ldres;
-  float* ss_out;                /* STORE: optional ss partials ss_out[tile*ss_out_ld + m] (N % 64 == 0) */
+  float* ss_out;                /* STORE: optional ss partials ss_out[t*ss_out_ld + m], t = 16-column tile */
   int64_t ss_out_ld;
   const float* rope;            /* ROPE_KV: fp32 [rope_rows, hd/2, 2] */
   int rope_rows;
@@ -131,7 +131,7 @@ int hm_emb_gather_i8(const int64_t* idx, int n, const int8_t* tab, const void* s
                      int* err, hm_stream_t stream);
 
 /* Backbone input of a frame (app/engine.py:348): x[r] = fp16(sum_c emb(tok[r,c] + c*vocab)),
- * plus optional ss partials per 64 columns for the next fused RMSNorm. */
+ * plus optional ss partials per 16 columns for the next fused RMSNorm. */
 int hm_emb_sum_i8(const int64_t* tok, int64_t tok_ld, int R, int ncb, int64_t vocab, const int8_t* tab,
                   const void* scale, int64_t rows, int D, void* x_out, float* ss_out, int64_t ss_ld, int* err, int pdl,
                   hm_stream_t stream);

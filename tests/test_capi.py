@@ -59,14 +59,15 @@ def test_host_argument_validation_without_gpu(lib):
 
 
 def test_workspace_sizing_is_consistent(lib):
-    # split-K scratch = splits * tiles * 64 rows * M * 4 bytes, zero without a split
-    for (M, N, K) in [(8, 5120, 3072), (1, 3072, 8192), (16, 8197, 3072), (32, 1024, 3072)]:
-        ks = lib.hm_gemv_pick_kspan(M, N, K, 0, 0)
-        assert ks in (128, 256, 512, 1024) and K % ks == 0
-        tiles = lib.hm_gemv_counters(N, 0)
-        assert tiles == (N + 63) // 64
-        want = (K // ks) * tiles * 64 * M * 4 if K // ks > 1 else 0
-        assert lib.hm_gemv_workspace_bytes(M, N, K, 0, 0) == want
-    assert lib.hm_gemv_counters(16384, 2) == 8192 // 32
+    # decode shapes at <= 8 rows stage their whole K: no split, no scratch
+    for (M, N, K) in [(8, 5120, 3072), (1, 3072, 8192), (8, 8197, 3072), (8, 3072, 8192)]:
+        assert lib.hm_gemv_pick_kspan(M, N, K, 0, 0) == K
+        assert lib.hm_gemv_workspace_bytes(M, N, K, 0, 0) == 0
+    # many rows x long K: split, scratch = splits * tiles * 16 rows * M * 4 bytes
+    ks = lib.hm_gemv_pick_kspan(32, 1024, 8192, 0, 0)
+    assert 8192 % ks == 0 and ks < 8192
+    assert lib.hm_gemv_workspace_bytes(32, 1024, 8192, 0, 0) == (8192 // ks) * 64 * 16 * 32 * 4
+    assert lib.hm_gemv_counters(5120, 0) == 320
+    assert lib.hm_gemv_counters(16384, 2) == 8192 // 16
     assert lib.hm_decode_attn_workspace_bytes(8, 24, 128, 1) == 0
     assert lib.hm_decode_attn_workspace_bytes(8, 24, 128, 5) == 8 * 24 * 5 * 130 * 4

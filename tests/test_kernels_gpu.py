@@ -27,13 +27,27 @@ def g(a):
     return torch.from_numpy(np.array(a))
 
 
-def close16(out, ref, ulps=2, frac_exact=0.95):
-    """fp16 results equal up to `ulps` fp16 ulps (of the reference value), most of them exactly."""
+def close16(out, ref, ulps=2, frac_exact=0.95, slack=None):
+    """fp16 results equal up to `ulps` fp16 ulps (of the reference value), most of them exactly.
+    `slack`: extra absolute tolerance per element (fp32 accumulation-order bound)."""
     o, r = out.float().cpu(), ref.float().cpu()
     ulp = torch.clamp(2.0 ** (torch.floor(torch.log2(r.abs().clamp_min(2.0 ** -14))) - 10), min=2.0 ** -24)
-    bad = (o - r).abs() > ulps * ulp
+    tol = ulps * ulp + (0 if slack is None else slack)
+    bad = (o - r).abs() > tol
     assert int(bad.sum()) == 0, f"{int(bad.sum())} values off by > {ulps} ulp; max abs {float((o - r).abs().max())}"
     assert (o == r).float().mean().item() >= frac_exact
+
+
+def acc_slack(x, w, s):
+    """Bound on the difference two fp32 accumulation orders can make in x.w*s:
+    about K*2^-24 relative to sum |x_k w_k|."""
+    return (x.float().abs() @ w.float().abs().t()) * s.float() * (x.shape[-1] * 2.0 ** -24)
+
+
+def rms_slack(xn, w, s, ref):
+    """Accumulation-order slack plus the effect of the normalised input differing by
+    one fp16 ulp in a few places (the 1/rms sum is accumulated in another order)."""
+    return acc_slack(xn, w, s) + 1e-3 * ref.float().abs() + 1e-4
 
 
 def rand_lin(N, K, gen):
@@ -54,9 +68,9 @@ def test_gemv_golden(golden, i):
 
 
 @pytest.mark.parametrize("M,N,K,kspan,res", [
-    (1, 64, 128, 0, False), (3, 200, 512, 128, True), (8, 5120, 3072, 0, False), (8, 3072, 8192, 1024, True),
-    (9, 1536, 1024, 256, False), (16, 8197, 3072, 0, False), (20, 1024, 3072, 512, True), (32, 3072, 1024, 0, True),
-    (8, 8197, 1024, 0, False), (1, 16384, 3072, 1024, False)])
+    (1, 64, 128, 0, False), (3, 200, 512, 0, True), (8, 5120, 3072, 0, False), (8, 3072, 8192, 1024, True),
+    (9, 1536, 1024, 512, False), (16, 8197, 3072, 0, False), (20, 1024, 3072, 512, True), (32, 3072, 1024, 0, True),
+    (8, 8197, 1024, 0, False), (1, 16384, 3072, 1024, False), (32, 1024, 8192, 0, True), (5, 2048, 8192, 0, False)])
 def test_gemv_matches_oracle(M, N, K, kspan, res):
     from estudiocanciones_b200 import kernels
     gen = torch.Generator().manual_seed(M * 7 + N + K)
@@ -70,9 +84,10 @@ def test_gemv_matches_oracle(M, N, K, kspan, res):
     ref = (acc * s.float()).half()
     if res:
         ref = (ref.float() + r.float()).half()
-    close16(out, ref, ulps=2, frac_exact=0.9)
+    slack = acc_slack(x, w, s)
+    close16(out, ref, ulps=2, frac_exact=0.9, slack=slack)
     if M <= 16:
-        close16(out, O.gemv_i8(x, w, s, r), ulps=2, frac_exact=0.9)
+        close16(out, O.gemv_i8(x, w, s, r), ulps=2, frac_exact=0.9, slack=slack)
 
 
 def test_gemv_is_deterministic():
@@ -81,8 +96,8 @@ def test_gemv_is_deterministic():
     x = torch.randn(8, 3072, generator=gen).half().to(DEV)
     w, s = rand_lin(3072, 3072, gen)
     w, s = w.to(DEV), s.to(DEV)
-    a = kernels.int8_mm(x, w, s, kspan=128)
-    b = kernels.int8_mm(x, w, s, kspan=128)
+    a = kernels.int8_mm(x, w, s, kspan=512)
+    b = kernels.int8_mm(x, w, s, kspan=512)
     assert torch.equal(a, b)
 
 
@@ -94,7 +109,7 @@ def _plan():
 
 def _ss(x):
     R, D = x.shape
-    return (x.float() ** 2).reshape(R, D // 64, 64).sum(-1).t().contiguous()
+    return (x.float() ** 2).reshape(R, D // 16, 16).sum(-1).t().contiguous()
 
 
 def test_gemv_rms_prologue_and_residual_ss():
@@ -108,12 +123,13 @@ def test_gemv_rms_prologue_and_residual_ss():
     lin = Linear(w.to(DEV), s.to(DEV))
     xd, yd = x.to(DEV), res.to(DEV).clone()
     ss_in = _ss(xd)
-    ss_out = torch.zeros(N // 64, M, device=DEV)
+    ss_out = torch.zeros(N // 16, M, device=DEV)
     p = _plan()
     p._gemv(lin, M, p.src_rms(xd, ss_in, gamma.to(DEV)), y=yd, res=yd, ss_out=ss_out)
     p.run()
-    ref = O.gemv_i8(O.rmsnorm(x, gamma), w, s, res)
-    close16(yd, ref, ulps=2, frac_exact=0.9)
+    xn = O.rmsnorm(x, gamma)
+    ref = O.gemv_i8(xn, w, s, res)
+    close16(yd, ref, ulps=2, frac_exact=0.9, slack=rms_slack(xn, w, s, ref))
     torch.testing.assert_close(ss_out.cpu(), _ss(yd).cpu(), rtol=1e-5, atol=1e-4)
 
 
@@ -138,7 +154,7 @@ def test_gemv_emb_interleave_prologue():
     e0 = O.emb_i8(tok[:, 0], tq, ts)
     xin = torch.stack([O.rmsnorm(x, gamma), e0], 1).reshape(2 * B, D)
     ref = O.gemv_i8(xin, w, s)
-    close16(y[B:], ref[B:], ulps=2, frac_exact=0.9)
+    close16(y[B:], ref[B:], ulps=2, frac_exact=0.9, slack=rms_slack(xin[B:], w, s, ref[B:]))
     close16(y[:B], O.gemv_i8(O.emb_i8(tok[:, 3] + 3 * V, tq, ts), w, s), ulps=2, frac_exact=0.9)
 
 
@@ -167,17 +183,23 @@ def test_gemv_rope_kv_epilogue(S, Hq, Hk):
     p._gemv(lin, R, p.src_rms(xd, _ss(xd), gamma.to(DEV)), epi=HM_EPI_ROPE_KV, rope=rope.to(DEV), pos=pos.to(DEV), S=S,
             blk=blk, q_out=q)
     p.run()
-    qkv = O.gemv_i8(O.rmsnorm(x, gamma), w, s)
+    xn = O.rmsnorm(x, gamma)
+    qkv = O.gemv_i8(xn, w, s)
     kc, vc = kc0.clone(), vc0.clone()
     qr = O.rope_kv_write(qkv, rope, pos, kc, vc, S, Hq, Hk)
-    close16(q, qr, ulps=2, frac_exact=0.9)
-    close16(blk.kc, kc, ulps=2, frac_exact=0.95)
-    close16(blk.vc, vc, ulps=2, frac_exact=0.95)
+    sl = rms_slack(xn, w, s, qkv).float().abs().reshape(R, -1)
+    qsl = sl[:, : Hq * 128]
+    qsl = torch.maximum(qsl, qsl.reshape(R, Hq, 64, 2).flip(-1).reshape(R, -1))  # rotation mixes pairs
+    close16(q, qr, ulps=2, frac_exact=0.9, slack=qsl)
+    close16(blk.kc, kc, ulps=2, frac_exact=0.95, slack=1e-3 * kc.float().abs() + 2e-4)
+    close16(blk.vc, vc, ulps=2, frac_exact=0.95, slack=1e-3 * vc.float().abs() + 2e-4)
     # slots other than the written positions are untouched (bit-exact)
     mask = torch.ones(B, L, dtype=torch.bool)
     for r in range(R):
         mask[r // S, int(pos[r])] = False
-    assert torch.equal(blk.kc.cpu()[mask.nonzero(as_tuple=True)], kc0[mask.nonzero(as_tuple=True)])
+    idx = mask.nonzero(as_tuple=True)      # (batch, position) pairs nobody wrote
+    assert torch.equal(blk.kc.cpu().permute(0, 2, 1, 3)[idx], kc0.permute(0, 2, 1, 3)[idx])
+    assert torch.equal(blk.vc.cpu().permute(0, 2, 1, 3)[idx], vc0.permute(0, 2, 1, 3)[idx])
 
 
 def test_gemv_silu_epilogue():
@@ -193,8 +215,11 @@ def test_gemv_silu_epilogue():
     p = _plan()
     p._gemv(lin, M, p.src_rms(xd, _ss(xd), gamma.to(DEV)), epi=HM_EPI_SILU, y=y)
     p.run()
-    ref = O.silu_mul(O.gemv_i8(O.rmsnorm(x, gamma), w, s))
-    close16(y, ref, ulps=3, frac_exact=0.9)
+    xn = O.rmsnorm(x, gamma)
+    a = O.gemv_i8(xn, w, s)
+    ref = O.silu_mul(a)
+    sl = rms_slack(xn, w, s, a)
+    close16(y, ref, ulps=3, frac_exact=0.9, slack=2 * (sl[:, :F] * a[:, F:].float().abs() + sl[:, F:]))
 
 
 # ----------------------------------------------------------------------------- small kernels
@@ -225,7 +250,9 @@ def test_silu_golden(golden, i):
     from estudiocanciones_b200 import kernels
     z = golden("kernels")
     out = kernels.silu_mul(g(z[f"silu{i}_a"]).to(DEV))
-    close16(out, g(z[f"silu{i}_y"]), ulps=1, frac_exact=0.99)
+    # CUDA's expf and Triton's tl.exp differ in the last fp32 bits, which can move
+    # the rounded silu by one fp16 ulp and the product by one more
+    close16(out, g(z[f"silu{i}_y"]), ulps=2, frac_exact=0.99)
 
 
 def test_emb_gather_and_sum():
@@ -239,7 +266,7 @@ def test_emb_gather_and_sum():
     out = kernels.emb_i8(tok[:, 2].to(DEV) + 2 * V, tq.to(DEV), ts.to(DEV))
     assert torch.equal(out.cpu(), O.emb_i8(tok[:, 2] + 2 * V, tq, ts))
     x = torch.empty(B, D, dtype=torch.float16, device=DEV)
-    ss = torch.empty(D // 64, B, device=DEV)
+    ss = torch.empty(D // 16, B, device=DEV)
     p = _plan()
     p.emb_sum(Emb(tq.to(DEV), ts.to(DEV)), tok.to(DEV), B, 8, V, x, ss)
     p.run()
