@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libheartmula_b200.so"
 HM_SRC_F16, HM_SRC_RMS, HM_SRC_EMB = 0, 1, 2
 HM_EPI_STORE, HM_EPI_ROPE_KV, HM_EPI_SILU = 0, 1, 2
 HM_ERR_TIMEOUT, HM_ERR_BADINDEX = 1, 2
+HM_ENOSPACE = -2
 
 # Every exported symbol of include/heartmula_b200.h with (restype, argtypes).
 _P, _I, _I64, _F, _SZ = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
@@ -55,6 +56,7 @@ SIGNATURES = {
     "hm_frame_commit": (_I, [_P, _P, _I, _I, _P, _I, _P, _P, _I64, _I, _P]),
     "hm_decode_attn": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P, _I, _P, _I, _P]),
     "hm_decode_attn_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "hm_decode_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "hm_cfg_topk_sample": (_I, [_P, _I64, _I, _I, _I, _P, _I64, _F, _I, _F, _P, _I64, _I, _P, _I, _P]),
     "hm_device_sm_count": (_I, [_I]),
     "hm_abi_layout": (_SZ, [_I]),

@@ -15,6 +15,8 @@
 // and the normaliser keeps the fp32 sum, as in _attn.  With nsplit > 1 the
 // last CTA of each (row, KV head) merges the split partials (log-sum-exp) and
 // re-arms its ticket.
+#include <mutex>
+
 #include "hm_common.cuh"
 
 namespace {
@@ -374,6 +376,88 @@ extern "C" int hm_decode_attn(const void* q, const void* kc, const void* vc, con
     case 256: e = launch_attn<256>(p, pdl, stream); break;
     case 384: e = launch_attn<384>(p, pdl, stream); break;
     default: return HM_EARG;
+  }
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+// ------------------------------------------------------------------ allocation-free variant
+// Some callers cannot allocate device memory when they run this kernel: a host
+// that drives decoding from a real-time audio thread (cudaMalloc/cudaFree may
+// synchronise the device and stall for milliseconds), or an application that
+// hands out all device memory from its own fixed arena and forbids the CUDA
+// allocator.  For them hm_decode_attn_noalloc keeps its scratch -- the split
+// partials and the merge tickets -- in this fixed array instead of taking a
+// workspace.  Every GPU that loads the library holds the array until exit.
+constexpr size_t kNoAllocPartialFloats = size_t(1) << 20;  // 4 MiB of split partials
+constexpr int kNoAllocTickets = 4096;
+static __device__ __align__(256) float hm_attn_scratch[kNoAllocPartialFloats + kNoAllocTickets];
+
+namespace {
+constexpr int kMaxDevices = 128;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  The array's name
+// in host code is only a stand-in, so the address is looked up once per device
+// (on that device's first call) and cached.
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, hm_attn_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" int hm_decode_attn_noalloc(const void* q, const void* kc, const void* vc, const int64_t* pos, void* o,
+                                      int R, int S, int Hq, int Hk, int hd, int L, float scale, int nsplit, int* err,
+                                      hm_stream_t stream) {
+  if (!q || !kc || !vc || !pos || !o || R < 1 || S < 1 || R % S || Hk < 1 || Hq % Hk || Hq / Hk > kMaxG || L < 1 ||
+      nsplit < 1 || nsplit > kMaxSplit)
+    return HM_EARG;
+  if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15u) return HM_EARG;
+  if (hd != 128 && hd != 256 && hd != 384) return HM_EARG;
+  if (nsplit > 1 && (hm_decode_attn_workspace_bytes(R, Hq, hd, nsplit) > kNoAllocPartialFloats * sizeof(float) ||
+                     R * Hk > kNoAllocTickets))
+    return HM_ENOSPACE;
+  void* base = nullptr;
+  cudaError_t e = noalloc_scratch(&base);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  float* partials = reinterpret_cast<float*>(base);
+  int* tickets = reinterpret_cast<int*>(partials + kNoAllocPartialFloats);
+  if (nsplit > 1) {
+    // the array keeps whatever the previous call left: start from zero tickets
+    e = cudaMemsetAsync(tickets, 0, sizeof(int) * R * Hk, stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  AttnParams p;
+  p.q = reinterpret_cast<const __half*>(q);
+  p.kc = reinterpret_cast<const __half*>(kc);
+  p.vc = reinterpret_cast<const __half*>(vc);
+  p.pos = pos;
+  p.o = reinterpret_cast<__half*>(o);
+  p.R = R;
+  p.S = S;
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.L = L;
+  p.nsplit = nsplit;
+  p.scale = scale;
+  p.ws = partials;
+  p.counters = tickets;
+  p.err = err;
+  switch (hd) {
+    case 128: e = launch_attn<128>(p, 0, stream); break;
+    case 256: e = launch_attn<256>(p, 0, stream); break;
+    default: e = launch_attn<384>(p, 0, stream); break;
   }
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }

@@ -30,6 +30,7 @@ typedef struct CUstream_st* hm_stream_t; /* == cudaStream_t */
 /* host return codes */
 #define HM_OK 0
 #define HM_EARG (-1)
+#define HM_ENOSPACE (-2) /* the request needs more scratch than hm_decode_attn_noalloc's fixed array holds */
 
 /* device error-word bits */
 #define HM_ERR_TIMEOUT 1   /* a bounded wait gave up */
@@ -151,6 +152,21 @@ int hm_decode_attn(const void* q, const void* kc, const void* vc, const int64_t*
                    int Hk, int hd, int L, float scale, int nsplit, void* ws, size_t ws_bytes, int* counters,
                    int n_counters, int* err, int pdl, hm_stream_t stream);
 size_t hm_decode_attn_workspace_bytes(int R, int Hq, int hd, int nsplit);
+
+/* Decode attention that allocates nothing (no counterpart in the reference, which
+ * always takes its scratch from the torch allocator).  For callers that cannot
+ * allocate device memory while they decode -- a real-time audio thread, where
+ * cudaMalloc may synchronise the device and stall, or an application that serves
+ * every buffer from its own fixed arena.  Same arguments and results as
+ * hm_decode_attn without the workspace: the split partials and merge tickets live
+ * in a fixed array inside the library (4 MiB of partials: R*Hq*nsplit*(hd+2) floats
+ * <= 1048576, and R*Hk <= 4096 tickets); larger requests return HM_ENOSPACE.  Every
+ * GPU that loads the library holds the array until the process exits.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress), so
+ * make that first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (other streams, other threads) race on it. */
+int hm_decode_attn_noalloc(const void* q, const void* kc, const void* vc, const int64_t* pos, void* o, int R, int S,
+                           int Hq, int Hk, int hd, int L, float scale, int nsplit, int* err, hm_stream_t stream);
 
 /* ------------------------------------------------------------------ sampler
  * _guided + _sample (app/engine.py:291-305) for one codebook: optional CFG mix
