@@ -15,7 +15,10 @@
 // and the normaliser keeps the fp32 sum, as in _attn.  With nsplit > 1 the
 // last CTA of each (row, KV head) merges the split partials (log-sum-exp) and
 // re-arms its ticket.
+#include <cstdlib>
 #include <mutex>
+#include <unordered_map>
+#include <utility>
 
 #include "hm_common.cuh"
 
@@ -324,6 +327,311 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   if (tid == 0) *ticket = 0;
 }
 
+// ------------------------------------------------------------------ tensor-core path (hd = 128)
+// Same contract as decode_attn_kernel for head_dim 128, with QK^T and PV on the
+// tensor cores (FA2-style): the G query heads of the KV head are the rows of a
+// 16-row MMA tile (rows >= G are zero), each warp owns 16 positions of every
+// 64-position stage, scores stay in registers, probabilities are rounded to fp16
+// and fed straight back as the A operand of the PV MMA.  K and V tiles arrive by
+// 2-D TMA (box 64 dims x 64 positions, 128B swizzle) through a 3-stage ring.
+constexpr int kTcPos = 64;   // positions per stage (4 warps x 16)
+constexpr int kTcNst = 3;
+constexpr int kTcBox = kTcPos * 128;  // bytes of one 64x64 fp16 box
+
+struct TcSmem {
+  uint8_t k[kTcNst][2][kTcBox];  // [stage][dims 0-63 | 64-127][64 positions x 128 B]
+  uint8_t v[kTcNst][2][kTcBox];
+  float mw[4][kMaxG], lw[4][kMaxG];
+  float cw[kMaxG][kMaxSplit], cl[kMaxG][kMaxSplit], cden[kMaxG];
+  uint64_t bar[kTcNst];
+  int flag, abort_flag;
+};
+
+__device__ __forceinline__ uint32_t swz(const uint8_t* box, int row, int chunk) {
+  return smem_u32(box + row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                  const __grid_constant__ CUtensorMap vmap,
+                                                                  const __grid_constant__ AttnParams P) {
+  constexpr int HD = 128;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  TcSmem& sm = *reinterpret_cast<TcSmem*>(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int sp = blockIdx.x, kh = blockIdx.y, r = blockIdx.z;
+  const int Hq = P.Hq, Hk = P.Hk, S = P.S, L = P.L, nsplit = P.nsplit, R = P.R;
+  const float scale = P.scale;
+  int* const err = P.err;
+  __half* const og = P.o;
+  float* const wsg = P.ws;
+  int* const counters = P.counters;
+  const int G = Hq / Hk;
+
+  if (smem_u32(smem_raw) & 1023u) {
+    if (tid == 0) report_error(err, HM_ERR_TIMEOUT);
+    return;
+  }
+  if (tid == 0) {
+    sm.abort_flag = 0;
+    for (int i = 0; i < kTcNst; ++i) mbar_init(&sm.bar[i], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
+  pdl_trigger();
+  pdl_wait();
+
+  const int64_t p_last = P.pos[r];
+  const int b = r / S;
+  int len = static_cast<int>(p_last) + 1;
+  if (p_last < 0 || p_last >= L) {
+    report_error(err, HM_ERR_BADINDEX);
+    len = 0;
+  }
+  const int per = (len + nsplit - 1) / nsplit;
+  const int chunk = (per + kTcPos - 1) / kTcPos * kTcPos;
+  const int lo = sp * chunk;
+  const int hi = min(len, lo + chunk);
+  const int ntile = hi > lo ? (hi - lo + kTcPos - 1) / kTcPos : 0;
+  const int row0 = ((b * Hk + kh) * L) + lo;
+
+  auto issue = [&](int tt) {
+    const int st = tt % kTcNst;
+    const int y = row0 + tt * kTcPos;
+    mbar_arrive_expect_tx(&sm.bar[st], 4 * kTcBox);
+    tma_load_2d_plain(sm.k[st][0], &kmap, 0, y, &sm.bar[st]);
+    tma_load_2d_plain(sm.k[st][1], &kmap, 64, y, &sm.bar[st]);
+    tma_load_2d_plain(sm.v[st][0], &vmap, 0, y, &sm.bar[st]);
+    tma_load_2d_plain(sm.v[st][1], &vmap, 64, y, &sm.bar[st]);
+  };
+  if (tid == 0)
+    for (int tt = 0; tt < kTcNst && tt < ntile; ++tt) issue(tt);
+
+  // q of this lane's head (row g of the MMA tile), as A fragments for 8 k-steps
+  uint32_t qa[8][2];
+  {
+    const __half* qh = P.q + ((int64_t)r * Hq + kh * G + g) * HD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qh + 16 * ks + 2 * t) : 0u;
+      qa[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qh + 16 * ks + 8 + 2 * t) : 0u;
+    }
+  }
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const int mi = lane >> 3, ri = lane & 7;
+
+  for (int tt = 0; tt < ntile; ++tt) {
+    const int st = tt % kTcNst;
+    mbar_wait_ab(&sm.bar[st], (tt / kTcNst) & 1, err, &sm.abort_flag);  // on timeout: carry on, error flagged
+    const int nvalid = min(16, hi - (lo + tt * kTcPos + warp * 16));
+    if (nvalid > 0) {
+      // ---- S = Q K^T over this warp's 16 positions (two n-tiles of 8)
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const int kp = warp * 16 + (mi >= 2 ? 8 : 0) + ri;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int c = 2 * ks + (mi & 1);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(b00, b01, b10, b11, swz(sm.k[st][c >> 3], kp, c & 7));
+        mma_16816(s[0], qa[ks][0], 0u, qa[ks][1], 0u, b00, b01);
+        mma_16816(s[1], qa[ks][0], 0u, qa[ks][1], 0u, b10, b11);
+      }
+      // ---- online softmax for head g (the quad t = 0..3 holds its 16 scores)
+      float v4[4];
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int pl = 8 * n + 2 * t + e;
+          const float val = pl < nvalid ? s[n][e] * scale : -INFINITY;
+          v4[2 * n + e] = val;
+          tmax = fmaxf(tmax, val);
+        }
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+      const float m_new = fmaxf(m_run, tmax);
+      float alpha = 1.f, psum = 0.f;
+      float pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        pv[i] = (m_new == -INFINITY || v4[i] == -INFINITY) ? 0.f : expf(v4[i] - m_new);
+        psum += pv[i];
+      }
+      if (m_new != -INFINITY) alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+      psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+      psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+      l_run = l_run * alpha + psum;
+      m_run = m_new;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        acc[i][0] *= alpha;
+        acc[i][1] *= alpha;
+      }
+      // ---- acc += fp16(P) V
+      const uint32_t pa0 = pack_h2(pv[0], pv[1]), pa2 = pack_h2(pv[2], pv[3]);
+      const int vp = warp * 16 + (mi & 1) * 8 + ri;
+#pragma unroll
+      for (int nd = 0; nd < 8; ++nd) {
+        const int c = 2 * nd + (mi >> 1);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(v0, v1, v2, v3, swz(sm.v[st][c >> 3], vp, c & 7));
+        mma_16816(acc[2 * nd], pa0, 0u, pa2, 0u, v0, v1);
+        mma_16816(acc[2 * nd + 1], pa0, 0u, pa2, 0u, v2, v3);
+      }
+    }
+    __syncthreads();  // every warp is done with stage st
+    if (tid == 0 && tt + kTcNst < ntile) issue(tt + kTcNst);
+  }
+
+  // ---- merge the four warps (red aliases the now idle stage-0 K buffers)
+  float* red = reinterpret_cast<float*>(&sm.k[0][0][0]);  // [4][kMaxG][128]
+  if (g < G) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      red[(warp * kMaxG + g) * HD + 8 * i + 2 * t] = acc[i][0];
+      red[(warp * kMaxG + g) * HD + 8 * i + 2 * t + 1] = acc[i][1];
+    }
+    if (t == 0) {
+      sm.mw[warp][g] = m_run;
+      sm.lw[warp][g] = l_run;
+    }
+  }
+  __syncthreads();
+  const int64_t head0 = (int64_t)r * Hq + kh * G;
+  const int64_t nh = (int64_t)R * Hq * nsplit;
+  float* wm = wsg;
+  float* wl = wsg + nh;
+  float* wa = wsg + 2 * nh;
+  for (int i = tid; i < G * HD; i += kThreads) {
+    const int gg = i / HD, d = i - gg * HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm.mw[w][gg]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sm.mw[w][gg];
+      const float f = mw > -INFINITY ? expf(mw - M) : 0.f;
+      num += red[(w * kMaxG + gg) * HD + d] * f;
+      den += sm.lw[w][gg] * f;
+    }
+    if (nsplit == 1) {
+      og[(head0 + gg) * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+    } else {
+      wa[((head0 + gg) * nsplit + sp) * HD + d] = num;
+      if (d == 0) {
+        wm[(head0 + gg) * nsplit + sp] = M;
+        wl[(head0 + gg) * nsplit + sp] = den;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  int* ticket = &counters[r * Hk + kh];
+  if (tid == 0) sm.flag = (atomicAdd(ticket, 1) == nsplit - 1);
+  __syncthreads();
+  if (!sm.flag) return;
+  __threadfence();
+  for (int i = tid; i < G * nsplit; i += kThreads) {
+    const int gg = i / nsplit, s2 = i - gg * nsplit;
+    sm.cw[gg][s2] = __ldcg(wm + (head0 + gg) * nsplit + s2);
+    sm.cl[gg][s2] = __ldcg(wl + (head0 + gg) * nsplit + s2);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float mx = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) mx = fmaxf(mx, sm.cw[tid][s2]);
+    float den = 0.f;
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+      const float ms = sm.cw[tid][s2];
+      const float w = ms > -INFINITY ? expf(ms - mx) : 0.f;
+      sm.cw[tid][s2] = w;
+      den += sm.cl[tid][s2] * w;
+    }
+    sm.cden[tid] = den;
+  }
+  __syncthreads();
+  for (int i = tid; i < G * HD; i += kThreads) {
+    const int gg = i / HD, d = i - gg * HD;
+    const int64_t h = head0 + gg;
+    float part[8];
+    float num = 0.f;
+    for (int s0 = 0; s0 < nsplit; s0 += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) part[j] = s0 + j < nsplit ? __ldcg(wa + (h * nsplit + s0 + j) * HD + d) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < nsplit) num += part[j] * sm.cw[gg][s0 + j];
+    }
+    const float den = sm.cden[gg];
+    og[h * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+  }
+  if (tid == 0) *ticket = 0;
+}
+
+// 2-D view [rows = B*Hk*L, 128] of an fp16 cache for the TMA (cached by pointer)
+bool cache_map(const void* base, int64_t rows, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, std::pair<int64_t, CUtensorMap>> cache;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(base);
+    if (it != cache.end() && it->second.first == rows) {
+      *out = it->second.second;
+      return true;
+    }
+  }
+  auto enc = hm_encode_fn();
+  if (!enc) return false;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTcPos)};
+  cuuint32_t es[2] = {1, 1};
+  if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache[base] = {rows, m};
+  *out = m;
+  return true;
+}
+
+// HM_ATTN_TC=0 selects the CUDA-core kernel for head_dim 128 (comparison runs)
+bool attn_tc_enabled() {
+  static const int on = [] {
+    const char* e = getenv("HM_ATTN_TC");
+    return e ? atoi(e) : 1;
+  }();
+  return on != 0;
+}
+
+cudaError_t launch_attn_tc(const AttnParams& p, int B, int pdl, cudaStream_t st) {
+  const int64_t rows = (int64_t)B * p.Hk * p.L;
+  CUtensorMap km, vm;
+  if (!cache_map(p.kc, rows, &km) || !cache_map(p.vc, rows, &vm)) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(TcSmem) + 1024;  // + slack to align the base to 1024
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return hm_launch(decode_attn_tc_kernel, dim3(p.nsplit, p.Hk, p.R), dim3(kThreads), smem, st, pdl, km, vm, p);
+}
+
 template <int HD>
 cudaError_t launch_attn(const AttnParams& p, int pdl, cudaStream_t st) {
   const size_t smem = sizeof(AttnSmem<HD>);
@@ -372,7 +680,7 @@ extern "C" int hm_decode_attn(const void* q, const void* kc, const void* vc, con
   p.err = err;
   cudaError_t e;
   switch (hd) {
-    case 128: e = launch_attn<128>(p, pdl, stream); break;
+    case 128: e = attn_tc_enabled() ? launch_attn_tc(p, R / S, pdl, stream) : launch_attn<128>(p, pdl, stream); break;
     case 256: e = launch_attn<256>(p, pdl, stream); break;
     case 384: e = launch_attn<384>(p, pdl, stream); break;
     default: return HM_EARG;

@@ -7,10 +7,12 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <utility>
 
 #include "heartmula_b200.h"
@@ -116,6 +118,15 @@ HM_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_
       : "memory");
 }
 
+// Same without an L2 cache hint.
+HM_DEV void tma_load_2d_plain(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
 HM_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -177,6 +188,23 @@ HM_DEV void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// ldmatrix: four 8x8 b16 matrices; lanes 8i..8i+7 give the row addresses of matrix i
+HM_DEV void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+HM_DEV void ldsm_x4_t(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// two floats -> fp16x2 (first in the low half), round to nearest even
+HM_DEV uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 HM_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -192,6 +220,20 @@ HM_DEV float warp_max(float v) {
 // exact in fp32, so this equals an IEEE fp16 multiply).
 HM_DEV __half hmul_rn(__half a, __half b) { return __float2half_rn(__half2float(a) * __half2float(b)); }
 HM_DEV __half hadd_rn(__half a, __half b) { return __hadd(a, b); }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static inline PFN_cuTensorMapEncodeTiled_v12000 hm_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
 
 // Launch helper: every kernel is launched with the programmatic-stream-
 // serialisation attribute when `pdl` is set, so it may overlap the previous

@@ -150,11 +150,11 @@ class Stack:
 
 # ----------------------------------------------------------------------------- buffers and plan
 def default_nsplit(R, Hk, L, sms=None):
-    """Split count for decode attention: about four CTAs per SM (a short chain of
-    K/V tiles per CTA), at most one split per 64 cache positions."""
+    """Split count for decode attention: one wave of two CTAs per SM, at most one
+    split per 64 cache positions (one K/V stage)."""
     if sms is None:
         sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    return int(max(1, min(math.ceil(4 * sms / max(1, R * Hk)), max(1, L // 64), 64)))
+    return int(max(1, min(2 * sms // max(1, R * Hk), max(1, L // 64), 64)))
 
 
 class _Ctx:

@@ -51,7 +51,7 @@ def test_prompt_assembly_matches_reference_rules():
 
 def test_default_attention_split():
     from estudiocanciones_b200.engine import default_nsplit
-    assert default_nsplit(8, 8, 1608, sms=148) == 10
+    assert default_nsplit(8, 8, 1608, sms=148) == 4
     assert default_nsplit(1, 8, 768, sms=148) == 12
-    assert default_nsplit(1, 8, 8192, sms=148) == 64
+    assert default_nsplit(1, 8, 8192, sms=148) == 37
     assert default_nsplit(8, 2, 8, sms=148) == 1
