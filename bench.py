@@ -50,7 +50,7 @@ def args_():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn"],
+    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn", "sampler"],
                     help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures")
     ap.add_argument("--layers", type=int, default=4, help="backbone layers of the small cases")
     ap.add_argument("--reps", type=int, default=3)
@@ -388,8 +388,8 @@ def run_ours(a, world, rank, local):
 
 def run_case(a):
     """Small single-kernel cases for profiling: the GEMV launches of a few backbone
-    layers (weights > L2 but well under a GB) or one decode-attention launch at the
-    benchmark's shapes.  Eager launches without PDL; prints one JSON line."""
+    layers (weights > L2 but well under a GB), one decode-attention launch at the
+    benchmark's shapes, or the 8 samplers of a frame.  Graph replays; prints one JSON line."""
     from dataclasses import replace
     from estudiocanciones_b200.checkpoint import BASELINE_SHAPE, synthetic_tensors
     from estudiocanciones_b200.engine import FramePlan, HeartMuLaLite
@@ -407,8 +407,11 @@ def run_case(a):
     for blk in m.backbone.blocks:
         blk.kc.normal_(generator=g)
         blk.vc.normal_(generator=g)
-    p = FramePlan(rt.ctx, pdl=False)
-    if a.case == "gemv":
+    p = FramePlan(rt.ctx, pdl=not a.no_pdl)
+    if a.case == "sampler":
+        for c in range(8):
+            p.sample(rt.logits, N, 1.5, 50, 1.0, rt.noise[c], rt.tok_out, c)
+    elif a.case == "gemv":
         from estudiocanciones_b200._lib import HM_EPI_ROPE_KV, HM_EPI_SILU
         bb = rt.bb
         for b in m.backbone.blocks:

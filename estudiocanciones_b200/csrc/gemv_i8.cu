@@ -79,13 +79,15 @@ __host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_
   L.rmode = L.rowp + kMaxM * 8;
   L.flag = L.rmode + 2 * kMaxM * 4;
   L.bars = align_up(L.flag + 16, 8);
-  L.total = L.bars + 2 * kNST * 8;
+  L.total = L.bars + (2 * kNST + 1) * 8;
   return L;
 }
 
-// Swizzled position of 16-byte chunk c inside an activation row (bank-conflict
-// free for the B-fragment reads: lanes t and t+2 land in different banks).
-__device__ __forceinline__ int xchunk(int c) { return c ^ (((c >> 3) & 1) << 1); }
+// Activation rows are stored linearly (one bulk copy per row) with a pitch of
+// 16 mod 128 bytes.  Lane (g, t) reads the four 16-byte chunks 4t..4t+3 of its
+// 128-column slice; lanes with t >= 2 read them rotated by two chunks (and take
+// the two halves of their weight bytes swapped to match), which keeps the eight
+// lanes of every shared-memory phase on distinct banks.
 
 __device__ __forceinline__ const hm_row_src& src_of(const hm_gemv_desc& d, int m, int& row, int& sel) {
   sel = d.interleave ? (m & 1) : 0;
@@ -131,6 +133,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   volatile int* abort_s = flag_s + 1;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + kNST;
+  uint64_t* xbar = empty + kNST;  // bulk copies of the activation rows and gammas
 
   if (smem_u32(ring) & 1023u) {  // 128B-swizzled TMA destinations must be 1024-byte aligned
     if (tid == 0) report_error(d.err, HM_ERR_TIMEOUT);
@@ -142,6 +145,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kCons / 32);
     }
+    mbar_init(xbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -215,28 +219,32 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   const bool g1 = P.has_gamma && d.interleave && d.src[1].mode == HM_SRC_RMS;
   named_bar(kBarCons, kCons);
 
-  // ---- issue every copy of the activation k-range [MROWS][kspan] (swizzled 16-byte chunks):
-  // fp16 rows 16 B per chunk, int8 embedding rows 8 B into the first half of the chunk
+  // ---- stage the activation k-range [MROWS][kspan]: one bulk copy per fp16 / RMS row
+  // and per gamma (thread 0), 8-byte cp.async for int8 embedding rows (into the first
+  // half of each 16-byte chunk), zeros for padding rows, rejected ids and the tail
   const int cpr = kspan / 8;
   const int kend = min(kspan, K - k0);  // valid columns of this k-range (a multiple of 8)
+  if (tid == 0) {
+    uint32_t bytes = 0;
+    for (int m = 0; m < M; ++m) bytes += (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS) ? kend * 2 : 0;
+    bytes += (g0 ? kend * 2 : 0) + (g1 ? kend * 2 : 0);
+    mbar_arrive_expect_tx(xbar, bytes);
+    for (int m = 0; m < M; ++m)
+      if (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS)
+        bulk_load(xsm + m * L.xp, rowp_s[m] + 2 * k0, kend * 2, xbar);
+    if (g0) bulk_load(gam_s, gam0 + k0, kend * 2, xbar);
+    if (g1) bulk_load(gam_s + kspan, gam1 + k0, kend * 2, xbar);
+  }
   for (int m = 0; m < MROWS; ++m) {
-    const int mode = rmode_s[m];
+    const int mode = m < M ? rmode_s[m] : -1;
     const uint8_t* base = rowp_s[m];
     uint8_t* xr = xsm + m * L.xp;
     for (int c = tid; c < cpr; c += kCons) {
-      uint8_t* dst = xr + xchunk(c) * 16;
       if (mode < 0 || 8 * c >= kend)
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
       else if (mode == HM_SRC_EMB)
-        cp_async8(dst, base + k0 + 8 * c);
-      else
-        cp_async16(dst, base + 2 * (k0 + 8 * c));
+        cp_async8(xr + c * 16, base + k0 + 8 * c);
     }
-  }
-  for (int c = tid; c < cpr; c += kCons) {
-    if (8 * c >= kend) continue;
-    if (g0) cp_async16(gam_s + 8 * c, gam0 + k0 + 8 * c);
-    if (g1) cp_async16(gam_s + kspan + 8 * c, gam1 + k0 + 8 * c);
   }
   // ---- RMSNorm 1/rms of RMS rows from the producers' ss partials, while the copies fly
   for (int m = warp; m < M; m += kCons / 32) {
@@ -253,6 +261,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     if (lane == 0) inv_s[m] = 1.0f / sqrtf(a / dim + eps);
   }
   cp_async_wait_all();
+  mbar_wait_ab(xbar, 0, err, abort_s);
   named_bar(kBarCons, kCons);
 
   // ---- in-place transforms: RMSNorm (fp16(x*inv) * gamma) and int8 -> fp16 embedding rows
@@ -264,19 +273,22 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       const float inv = inv_s[m];
       const __half* gs = gam_s + rsel_s[m] * kspan;
       for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
-        uint4* slot = reinterpret_cast<uint4*>(xr + xchunk(c) * 16);
+        uint4* slot = reinterpret_cast<uint4*>(xr + c * 16);
         uint4 v = *slot;
         const uint4 gv = *reinterpret_cast<const uint4*>(gs + 8 * c);
-        __half* vh = reinterpret_cast<__half*>(&v);
-        const __half* gh = reinterpret_cast<const __half*>(&gv);
+        __half2* vh = reinterpret_cast<__half2*>(&v);
+        const __half2* gh = reinterpret_cast<const __half2*>(&gv);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) vh[j] = hmul_rn(__float2half_rn(__half2float(vh[j]) * inv), gh[j]);
+        for (int j = 0; j < 4; ++j) {  // fp16(fp16(x * inv) * gamma), each step rounded once
+          const float2 f = __half22float2(vh[j]);
+          vh[j] = __hmul2(__floats2half2_rn(f.x * inv, f.y * inv), gh[j]);
+        }
         *slot = v;
       }
     } else {
       const float sc = esc_s[m];
       for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
-        uint4* slot = reinterpret_cast<uint4*>(xr + xchunk(c) * 16);
+        uint4* slot = reinterpret_cast<uint4*>(xr + c * 16);
         const uint2 q = *reinterpret_cast<const uint2*>(slot);
         const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
         uint4 v;
@@ -320,7 +332,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 
   // ---- tiles: warp w consumes box w of every stage (row block w % RT, k slice w / RT)
   const int g = lane >> 2, t = lane & 3;
-  const int rb = warp % RT, ksub = warp / RT;
+  const int rot = t >> 1;  // lanes t >= 2 read their activation chunks rotated by two
+  const int ksub = warp / RT;
   // epilogue ownership: thread -> (row r of the 16, rows m = m0, m0 + 8, ...)
   const int er = tid & 15, em0 = tid >> 4;
   int it = 0;
@@ -338,10 +351,10 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       const int slot = it % kNST;
       mbar_wait_ab(&full[slot], (it / kNST) & 1, err, abort_s);  // on timeout: carry on, error flagged
       const uint8_t* wb = ring + slot * kStage + warp * kBoxBytes;
-      const uint4 lo0 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t) ^ g) << 4));
-      const uint4 lo1 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + 1) ^ g) << 4));
-      const uint4 hi0 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t) ^ g) << 4));
-      const uint4 hi1 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t + 1) ^ g) << 4));
+      const uint4 lo0 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + rot) ^ g) << 4));
+      const uint4 lo1 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + 1 - rot) ^ g) << 4));
+      const uint4 hi0 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t + rot) ^ g) << 4));
+      const uint4 hi1 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t + 1 - rot) ^ g) << 4));
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);  // this warp's box is in registers now
       const uint32_t wa[8] = {lo0.x, lo0.y, lo0.z, lo0.w, lo1.x, lo1.y, lo1.z, lo1.w};
@@ -353,7 +366,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
         const uint8_t* xr = xsm + (8 * j + g) * L.xp;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint4 v = *reinterpret_cast<const uint4*>(xr + xchunk(cb + 4 * t + i) * 16);
+          const uint4 v = *reinterpret_cast<const uint4*>(xr + (cb + 4 * t + ((i + 2 * rot) & 3)) * 16);
           xw[j][4 * i + 0] = v.x;
           xw[j][4 * i + 1] = v.y;
           xw[j][4 * i + 2] = v.z;

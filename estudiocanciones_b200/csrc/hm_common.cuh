@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <utility>
 
@@ -235,6 +236,18 @@ static inline PFN_cuTensorMapEncodeTiled_v12000 hm_encode_fn() {
   return fn;
 }
 
+// Every kernel asks for the maximum shared-memory carveout, so consecutive
+// kernels never need a different L1/shared split on an SM (a change of split
+// drains the SM and defeats overlapping launches).  HM_CARVEOUT=0 turns it off.
+template <typename K>
+static inline void hm_carveout(K kernel) {
+  static const int on = [] {
+    const char* e = getenv("HM_CARVEOUT");
+    return e ? atoi(e) : 1;
+  }();
+  if (on) cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+}
+
 // Launch helper: every kernel is launched with the programmatic-stream-
 // serialisation attribute when `pdl` is set, so it may overlap the previous
 // kernel's tail (its own griddepcontrol.wait keeps the data dependency).
@@ -251,5 +264,10 @@ static inline cudaError_t hm_launch(void (*kernel)(KArgs...), dim3 grid, dim3 bl
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  static bool carved = false;  // once per kernel instantiation
+  if (!carved) {
+    hm_carveout(kernel);
+    carved = true;
+  }
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
