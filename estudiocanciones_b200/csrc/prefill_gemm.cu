@@ -1,0 +1,411 @@
+// Prompt-prefill GEMM with int8 weights on the 5th-generation tensor cores (sm_100a).
+//
+// Replaces the M > 16 branch of the reference's `int8_mm` (app/kernels.py:46-49:
+// weights dequantised to fp16, then an fp16 GEMM) for the prompt pass of the
+// backbone, `Stack.__call__` -> `Block.__call__` (app/engine.py:123-153, 174-178).
+//
+//   C[m, n] = fp16( sum_k A[m, k] * W[n, k] * s[n] )  (+ R[m, n], rounded again)
+//   SiLU epilogue (fused w1|w3): C[m, f] = fp16( fp16(silu(a)) * b ),
+//                                a = fp16(acc_w1 * s), b = fp16(acc_w3 * s)
+//
+// int8 -> fp16 is exact, so the product over k is the same as with the
+// reference's dequantised weights; the per-row scale is applied to the fp32
+// sum instead of to each weight (one rounding fewer).
+//
+// One CTA computes a 128 x 256 output tile (for SiLU: 128 features of w1 and the
+// same 128 of w3).  Warp roles:
+//   warp 0      TMA producer: A tile 128x64 fp16 (128B swizzle) and the int8
+//               weight tile 256x64 into a 4-stage ring.
+//   warp 1      allocates 256 TMEM columns; one thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) x4 per
+//               k-block from shared-memory descriptors, fp32 accumulators in
+//               TMEM, and releases ring slots with tcgen05.commit.
+//   warps 2-5   convert the int8 tile to fp16 in the K-major 128B-swizzled
+//               layout the MMA reads (double-buffered), then run the epilogue:
+//               tcgen05.ld of their 32 TMEM lanes, scale, round, residual/SiLU,
+//               store.
+// Every wait is bounded (HM_ERR_TIMEOUT in the caller's error word).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "hm_common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, NST = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr int kABytes = BM * BK * 2;   // 16 KB
+constexpr int kBqBytes = BN * BK;      // 16 KB
+constexpr int kBhBytes = BN * BK * 2;  // 32 KB
+
+struct GemmSmem {
+  uint8_t a[NST][kABytes];
+  uint8_t bq[NST][kBqBytes];
+  uint8_t bh[2][kBhBytes];
+  uint64_t full[NST], empty[NST], bh_full[2], bh_empty[2], acc_full;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct GemmParams {
+  const __half* s;
+  const __half* res;
+  int64_t ldr;
+  __half* c;
+  int64_t ldc;
+  int M, N, K;  // N: output columns (features for SiLU)
+  int wrows_half;  // SiLU: row offset of w3 inside W (= features)
+  int* err;
+};
+
+// ---------------------------------------------------------------- tcgen05 wrappers
+HM_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+HM_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+HM_DEV void tmem_alloc(uint32_t* dst, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+HM_DEV void tmem_dealloc(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand in the canonical 128B-swizzle
+// layout (8 rows of 128 bytes per 1024-byte atom, atoms 1024 bytes apart).
+HM_DEV uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
+  d |= static_cast<uint64_t>(1) << 46;                 // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;                 // swizzle: 128B
+  return d;
+}
+
+// Instruction descriptor: f16 x f16 -> f32, both operands K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4)                                  // D format f32
+         | (0u << 7) | (0u << 10)                   // A, B format f16
+         | (static_cast<uint32_t>(N >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
+}
+
+HM_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+HM_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+HM_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+HM_DEV float silu_f(float a) { return a / (1.f + expf(-a)); }
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_constant__ CUtensorMap amap,
+                                                               const __grid_constant__ CUtensorMap wmap,
+                                                               const __grid_constant__ GemmParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = blockIdx.x * BM;
+  const int nt = blockIdx.y;
+  const int K = P.K;
+  const int nk = K / BK;
+  int* const err = P.err;
+
+  if (tid == 0) {
+    sm.abort_flag = 0;
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1 + 4);  // MMA commit (A consumed) + 4 converter warps (int8 tile consumed)
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.bh_full[i], 4);
+      mbar_init(&sm.bh_empty[i], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort_s = &sm.abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&amap);
+      prefetch_tensormap(&wmap);
+      const int r0 = EPI == HM_EPI_SILU ? nt * (BN / 2) : nt * BN;
+      const int r1 = EPI == HM_EPI_SILU ? P.wrows_half + nt * (BN / 2) : nt * BN + BN / 2;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % NST;
+        if (kb >= NST) mbar_wait_ab(&sm.empty[s], ((kb / NST) - 1) & 1, err, abort_s);
+        mbar_arrive_expect_tx(&sm.full[s], kABytes + kBqBytes);
+        tma_load_2d_plain(sm.a[s], &amap, kb * BK, m0, &sm.full[s]);
+        tma_load_2d_plain(sm.bq[s], &wmap, kb * BK, r0, &sm.full[s]);
+        tma_load_2d_plain(sm.bq[s] + kBqBytes / 2, &wmap, kb * BK, r1, &sm.full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BM, BN);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % NST, b = kb & 1;
+        mbar_wait_ab(&sm.full[s], (kb / NST) & 1, err, abort_s);
+        mbar_wait_ab(&sm.bh_full[b], (kb >> 1) & 1, err, abort_s);
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(smem_u32(sm.a[s]));
+        const uint64_t bd = sw128_desc(smem_u32(sm.bh[b]));
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K=16 step inside the 128-byte swizzle row
+          umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        umma_commit(&sm.empty[s]);
+        umma_commit(&sm.bh_empty[b]);
+      }
+      umma_commit(&sm.acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------ converters, then epilogue
+    const int ct = tid - 64;  // 0..127
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % NST, b = kb & 1;
+      mbar_wait_ab(&sm.full[s], (kb / NST) & 1, err, abort_s);
+      if (kb >= 2) mbar_wait_ab(&sm.bh_empty[b], ((kb >> 1) - 1) & 1, err, abort_s);
+      const uint8_t* src = sm.bq[s];
+      uint8_t* dst = sm.bh[b];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int id = ct + 128 * i;  // 16-byte int8 chunk: row n, k = 16j .. 16j+15
+        const int n = id >> 2, j = id & 3;
+        const uint4 q = *reinterpret_cast<const uint4*>(src + n * BK + j * 16);
+        uint4 h0, h1;
+        i8x4_to_h2x2(q.x, h0.x, h0.y);
+        i8x4_to_h2x2(q.y, h0.z, h0.w);
+        i8x4_to_h2x2(q.z, h1.x, h1.y);
+        i8x4_to_h2x2(q.w, h1.z, h1.w);
+        uint8_t* row = dst + (n >> 3) * 1024 + (n & 7) * 128;
+        *reinterpret_cast<uint4*>(row + (((2 * j) ^ (n & 7)) << 4)) = h0;
+        *reinterpret_cast<uint4*>(row + (((2 * j + 1) ^ (n & 7)) << 4)) = h1;
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.bh_full[b]);
+        mbar_arrive(&sm.empty[s]);
+      }
+    }
+    // ---- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 = tile rows
+    mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
+    tc_fence_after();
+    const int q = warp & 3;
+    const int m = m0 + 32 * q + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
+    const int N = P.N, M = P.M;
+    const __half* const sc = P.s;
+    __half* const C = P.c;
+    const int64_t ldc = P.ldc;
+    if (EPI == HM_EPI_SILU) {
+      const int f0 = nt * (BN / 2);
+      const int wh = P.wrows_half;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+        float va[16], vb[16];
+        tmem_ld16(trow + c0, va);
+        tmem_ld16(trow + BN / 2 + c0, vb);
+        const int f = f0 + c0;
+        if (m < M && f < N) {
+          uint32_t out[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            float y[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float a = __half2float(__float2half_rn(va[i + e] * __half2float(sc[f + i + e])));
+              const float bb = __half2float(__float2half_rn(vb[i + e] * __half2float(sc[wh + f + i + e])));
+              y[e] = __half2float(__float2half_rn(silu_f(a))) * bb;
+            }
+            out[i / 2] = pack_h2(y[0], y[1]);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + f);
+          dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+          dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+        }
+      }
+    } else {
+      const int n0 = nt * BN;
+      const __half* const R = P.res;
+      const int64_t ldr = P.ldr;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(trow + c0, v);
+        const int n = n0 + c0;
+        if (m < M && n < N) {
+          uint32_t out[8];
+          uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+          if (R) {
+            const uint4* rp = reinterpret_cast<const uint4*>(R + (int64_t)m * ldr + n);
+            r0 = rp[0];
+            r1 = rp[1];
+          }
+          const __half* rh0 = reinterpret_cast<const __half*>(&r0);
+          const __half* rh1 = reinterpret_cast<const __half*>(&r1);
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            float y[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              float t = __half2float(__float2half_rn(v[i + e] * __half2float(sc[n + i + e])));
+              if (R) t += __half2float(i + e < 8 ? rh0[i + e] : rh1[i + e - 8]);
+              y[e] = t;
+            }
+            out[i / 2] = pack_h2(y[0], y[1]);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + n);
+          dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+          dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+struct MapKey {
+  const void* p;
+  int64_t rows, cols, ld;
+  int kind;
+  bool operator==(const MapKey& o) const {
+    return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld && kind == o.kind;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.p) ^ (std::hash<int64_t>()(k.rows) * 31) ^ (std::hash<int64_t>()(k.ld) * 17) ^
+           static_cast<size_t>(k.kind);
+  }
+};
+
+// kind 0: fp16 activations [rows, cols] (row stride ld elements), box 64 x 128, 128B swizzle
+// kind 1: int8 weights [rows, cols] (row stride cols bytes), box 64 x 128, no swizzle
+bool tile_map(const void* p, int64_t rows, int64_t cols, int64_t ld, int kind, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{p, rows, cols, ld, kind};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  auto enc = hm_encode_fn();
+  if (!enc) return false;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r;
+  if (kind == 0) {
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    cuuint32_t box[2] = {BK, BM};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+    cuuint32_t box[2] = {BK, BN / 2};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(p), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache[key] = m;
+  *out = m;
+  return true;
+}
+
+template <int EPI>
+cudaError_t launch_gemm(const CUtensorMap& am, const CUtensorMap& wm, const GemmParams& p, int ntiles_n,
+                        hm_stream_t st) {
+  const size_t smem = sizeof(GemmSmem) + 1024;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8w_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const dim3 grid((p.M + BM - 1) / BM, ntiles_n);
+  return hm_launch(gemm_i8w_kernel<EPI>, grid, dim3(kThreads), smem, st, false, am, wm, p);
+}
+
+}  // namespace
+
+extern "C" int hm_gemm_i8w(const void* a, int64_t lda, const int8_t* w, const void* s, const void* res,
+                           int64_t ldr, void* c, int64_t ldc, int M, int N, int K, int epi, int* err,
+                           hm_stream_t stream) {
+  if (!a || !w || !s || !c || M < 1 || N < 1 || K < BK || K % BK != 0) return HM_EARG;
+  if (epi != HM_EPI_STORE && epi != HM_EPI_SILU) return HM_EARG;
+  if (epi == HM_EPI_SILU && (res != nullptr || N % 2 != 0)) return HM_EARG;
+  const int nout = epi == HM_EPI_SILU ? N / 2 : N;  // output columns
+  // 16-byte vector stores / loads of 16-column groups and TMA stride rules
+  if (nout % 16 != 0 || lda % 8 != 0 || ldc % 8 != 0 || lda < K || ldc < nout) return HM_EARG;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(c)) & 15u) return HM_EARG;
+  if (res && (ldr % 8 != 0 || ldr < N || (reinterpret_cast<uintptr_t>(res) & 15u))) return HM_EARG;
+  if (reinterpret_cast<uintptr_t>(w) & 15u) return HM_EARG;
+  CUtensorMap am, wm;
+  if (!tile_map(a, M, K, lda, 0, &am) || !tile_map(w, N, K, K, 1, &wm)) return HM_EARG;
+  GemmParams p;
+  p.s = reinterpret_cast<const __half*>(s);
+  p.res = reinterpret_cast<const __half*>(res);
+  p.ldr = ldr;
+  p.c = reinterpret_cast<__half*>(c);
+  p.ldc = ldc;
+  p.M = M;
+  p.N = nout;
+  p.K = K;
+  p.wrows_half = epi == HM_EPI_SILU ? N / 2 : 0;
+  p.err = err;
+  cudaError_t e;
+  if (epi == HM_EPI_SILU)
+    e = launch_gemm<HM_EPI_SILU>(am, wm, p, (nout + BN / 2 - 1) / (BN / 2), stream);
+  else
+    e = launch_gemm<HM_EPI_STORE>(am, wm, p, (N + BN - 1) / BN, stream);
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}

@@ -6,7 +6,7 @@
 // noise is an input (drawn by torch's generator so the random stream matches
 // the reference), everything else is one CTA per take:
 //   l   = (CFG ? u + fp16(fp16(c - u) * cfg) : c) / temp          (fp16 mix, fp32 divide)
-//   thr = k-th largest l  (radix select on order-preserving keys)
+//   thr = k-th largest l  (radix select on order-preserving fp16 keys of the mix)
 //   l'  = l >= thr ? l : -inf
 //   p   = softmax(log_softmax(l'))                                  (fp32)
 //   id  = argmax(p / noise)   (first index on ties, NaN counts as largest)
@@ -14,8 +14,8 @@
 
 namespace {
 
-constexpr int kThreads = 1024;
-constexpr int kPer = 9;  // values per thread: V <= 9216
+constexpr int kThreads = 512;
+constexpr int kPer = 17;  // values per thread: V <= 8704
 constexpr int kWarps = kThreads / 32;
 
 struct SampParams {
@@ -32,32 +32,26 @@ struct SampParams {
   int* err;
 };
 
-__device__ __forceinline__ uint32_t f2key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+// Order-preserving 16-bit keys of fp16 values (NaN with the sign bit clear sorts
+// above +inf, as in torch.topk).  l = fp32(g) / temp is non-decreasing in g, so
+// the k-th largest l is the quotient of the k-th largest g: the selection runs on
+// the 16-bit fp16 keys (two 8-bit radix passes instead of four on fp32 keys).
+__device__ __forceinline__ uint32_t h2key(__half h) {
+  const uint32_t u = __half_as_ushort(h);
+  return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u);
 }
-__device__ __forceinline__ float key2f(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+__device__ __forceinline__ __half key2h(uint32_t k) {
+  return __ushort_as_half(static_cast<unsigned short>((k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu)));
 }
 
-// block-wide reductions with a fixed combination order (deterministic)
-__device__ float block_max(float v, float* red) {
-  v = warp_max(v);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float r = red[l];
-  r = warp_max(r);
-  return r;
-}
+// block-wide sum with a fixed combination order (deterministic)
 __device__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   __syncthreads();
   if (l == 0) red[w] = v;
   __syncthreads();
-  float r = red[l];
+  float r = l < kWarps ? red[l] : 0.f;
   r = warp_sum(r);
   return r;
 }
@@ -70,14 +64,15 @@ __device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
 }
 
 __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant__ SampParams P) {
-  __shared__ int hist[256];
+  // digit histograms: 8 copies (lane & 7) per pass keep same-digit lanes of a warp
+  // on different addresses
+  __shared__ int hist[2][8][256];
   __shared__ float red[kWarps];
   __shared__ float rv[kWarps];
   __shared__ int ri[kWarps];
   __shared__ uint32_t sel_s;
   __shared__ int kk_s;
-  pdl_trigger();
-  pdl_wait();
+  __shared__ uint32_t maxkey_s;
   const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // parameters in registers (the block barriers below would force re-reads otherwise)
   const int V = P.V, Nt = P.N, topk = P.topk;
@@ -89,43 +84,54 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
   int64_t* const outp = P.out;
   const int out_col = P.out_col;
   int* const err = P.err;
-  float l[kPer];
+  pdl_trigger();
+  for (int i = tid; i < 2 * 8 * 256; i += kThreads) (&hist[0][0][0])[i] = 0;
+  if (tid == 0) maxkey_s = 0;
+  // the noise comes from a full (non-programmatic) dependency: read it before the wait
+  float nz[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int v = tid + j * kThreads;
+    nz[j] = v < V ? noise[(int64_t)n * ldn + v] : 1.f;
+  }
+  pdl_wait();
+  __half gv[kPer];
   uint32_t key[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int v = tid + j * kThreads;
-    float val = -INFINITY;
+    __half g = __float2half_rn(0.f);
     if (v < V) {
       const __half c = logits[(int64_t)n * ldl + v];
-      __half g = c;
+      g = c;
       if (mix) {
         const __half u = logits[(int64_t)(n + Nt) * ldl + v];
         const __half d = __hsub(c, u);
         const __half e = __float2half_rn(__half2float(d) * cfg);
         g = __hadd(u, e);
       }
-      val = __fdiv_rn(__half2float(g), temp);
     }
-    l[j] = val;
-    key[j] = f2key(val);
+    gv[j] = g;
+    key[j] = h2key(g);
   }
+  uint32_t kmax = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j)
+    if (tid + j * kThreads < V) kmax = max(kmax, key[j]);
+  kmax = __reduce_max_sync(0xffffffffu, kmax);
+  __syncthreads();  // histograms and maxkey_s zeroed
+  if (lane == 0) atomicMax(&maxkey_s, kmax);
 
-  // ---- radix select of the topk-th largest key, 8 bits per pass from the top
-  uint32_t prefix = 0, pmask = 0;
+  // ---- radix select of the topk-th largest fp16 key: high byte, then low byte
+  uint32_t sel_key = 0;
   int kk = topk;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
-    __syncthreads();
+#pragma unroll 1
+  for (int pass = 0; pass < 2; ++pass) {
+    int* const h = &hist[pass][lane & 7][0];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       const int v = tid + j * kThreads;
-      const bool in = v < V && (key[j] & pmask) == prefix;
-      const uint32_t dig = (key[j] >> shift) & 255u;
-      const uint32_t act = __ballot_sync(0xffffffffu, in);
-      if (in) {
-        const uint32_t peers = __match_any_sync(act, dig);
-        if ((__ffs(peers) - 1) == lane) atomicAdd(&hist[dig], __popc(peers));
-      }
+      if (v < V && (pass == 0 || (key[j] >> 8) == sel_key)) atomicAdd(&h[pass == 0 ? (key[j] >> 8) : (key[j] & 255u)], 1);
     }
     __syncthreads();
     if (warp == 0) {
@@ -134,8 +140,12 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
       int tot = 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        cnt[i] = hist[255 - 8 * lane - i];
-        tot += cnt[i];
+        const int dgt = 255 - 8 * lane - i;
+        int c = 0;
+#pragma unroll
+        for (int cp = 0; cp < 8; ++cp) c += hist[pass][cp][dgt];
+        cnt[i] = c;
+        tot += c;
       }
       int incl = tot;
 #pragma unroll
@@ -163,47 +173,60 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
       }
     }
     __syncthreads();
-    prefix |= sel_s << shift;
-    pmask |= 255u << shift;
+    sel_key = (sel_key << 8) | sel_s;
     kk = kk_s;
-    __syncthreads();
   }
-  const float thr = key2f(prefix);
+  // Keep l >= k-th largest l.  For fp16 g and any temp in [1e-20, 1e20] the fp32
+  // quotients of distinct g stay distinct (their relative gap, >= 2^-11, is far
+  // above fp32 rounding, and they neither overflow nor underflow), so the test is
+  // the fp16 comparison g >= g_k; outside that range the quotients are compared.
+  const __half thr_h = key2h(sel_key);
+  const float thr_g = __half2float(thr_h);
+  const bool direct = temp >= 1e-20f && temp <= 1e20f;
+  const float thr_l = __fdiv_rn(thr_g, temp);
 
-  // ---- softmax(log_softmax(masked)) and the exponential race
-  float mx = -INFINITY;
+  // ---- softmax(log_softmax(masked)): only kept values divide and exponentiate
+  // the largest kept value is the quotient of the largest key (always kept)
+  const float mx = __fdiv_rn(__half2float(key2h(maxkey_s)), temp);
+  float l[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    if (!(l[j] >= thr)) l[j] = -INFINITY;
-    mx = fmaxf(mx, l[j]);
+    const int v = tid + j * kThreads;
+    const float gf = __half2float(gv[j]);
+    const bool kept = v < V && (direct ? gf >= thr_g : __fdiv_rn(gf, temp) >= thr_l);
+    l[j] = -INFINITY;
+    if (kept) l[j] = __fdiv_rn(gf, temp);
   }
-  mx = block_max(mx, red);
   float se = 0.f;
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) se += l[j] == -INFINITY ? 0.f : expf(l[j] - mx);
+  for (int j = 0; j < kPer; ++j)
+    if (l[j] != -INFINITY) se += expf(l[j] - mx);
   se = block_sum(se, red);
   const float lz = logf(se);
-  float mx2 = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    l[j] = l[j] == -INFINITY ? -INFINITY : (l[j] - mx) - lz;
-    mx2 = fmaxf(mx2, l[j]);
-  }
-  mx2 = block_max(mx2, red);
+  // max of the log-softmax is (mx - mx) - lz = -lz exactly: no reduction needed
+  const float mx2 = -lz;
   float s2 = 0.f;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    l[j] = l[j] == -INFINITY ? 0.f : expf(l[j] - mx2);
-    s2 += l[j];
+    if (l[j] != -INFINITY) {
+      l[j] = expf(((l[j] - mx) - lz) - mx2);
+      s2 += l[j];
+    } else {
+      l[j] = 0.f;
+    }
   }
   s2 = block_sum(s2, red);
+  // argmax(p / noise): a dropped value has p = 0, so 0 / noise is 0, or NaN when the
+  // noise is 0 or NaN (NaN wins the argmax, as in torch)
   float best = -INFINITY;
   int bi = 0x7fffffff;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int v = tid + j * kThreads;
     if (v < V) {
-      const float r = __fdiv_rn(__fdiv_rn(l[j], s2), noise[(int64_t)n * ldn + v]);
+      float r;
+      if (l[j] != 0.f) r = __fdiv_rn(__fdiv_rn(l[j], s2), nz[j]);
+      else r = (nz[j] == 0.f || nz[j] != nz[j]) ? __int_as_float(0x7fffffff) : 0.f;
       if (better(r, v, best, bi)) {
         best = r;
         bi = v;
@@ -225,8 +248,8 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
   }
   __syncthreads();
   if (warp == 0) {
-    best = rv[lane];
-    bi = ri[lane];
+    best = lane < kWarps ? rv[lane] : -INFINITY;
+    bi = lane < kWarps ? ri[lane] : 0x7fffffff;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best, o);

@@ -11,6 +11,9 @@ here                   reference                                   C entry point
 ``rope_cache``         ``_rope_cache`` launch (``:79-107``)         ``hm_rope_kv_write``
 ``attn``               ``_attn`` + ``_attn_combine`` (``:112-167``) ``hm_decode_attn``
 ``silu_mul``           ``_silu_mul`` launch (``:172-180``)          ``hm_silu_mul``
+``gemm_i8w``           ``int8_mm`` for M > 16 (``:46-49``)           ``hm_gemm_i8w`` (tcgen05)
+``prefill_attn``       causal SDPA of ``Block.__call__``            ``hm_prefill_attn``
+                       (``app/engine.py:123-153``)
 =====================  ==========================================  ==============================
 
 Launches go to the current torch CUDA stream, so everything here can be
@@ -162,3 +165,37 @@ def sample(logits: torch.Tensor, n_takes: int, cfg: float, topk: int, temp: floa
                                         noise.stride(0), cfg, topk, temp, out.data_ptr(), out.stride(0), col,
                                         error_word(logits.device).data_ptr(), int(pdl), _stream()),
           "hm_cfg_topk_sample")
+
+
+def gemm_i8w(a: torch.Tensor, w: torch.Tensor, s: torch.Tensor, res: torch.Tensor | None = None,
+             out: torch.Tensor | None = None, silu: bool = False) -> torch.Tensor:
+    """Prompt-sized ``int8_mm``: a ``[M, K]`` fp16 times int8 ``w [N, K]`` with per-row
+    scales, on the tensor cores.  ``silu``: ``w`` is the fused w1|w3 (N = 2F) and the
+    result is ``fp16(silu(a1)) * a3`` ``[M, F]``.  ``res`` may be ``out`` (in-place add)."""
+    _need_cuda(a, w, s, res, out)
+    M, K = a.shape
+    N = w.shape[0]
+    nout = N // 2 if silu else N
+    if out is None:
+        out = torch.empty(M, nout, device=a.device, dtype=torch.float16)
+    check(_lib.lib().hm_gemm_i8w(a.data_ptr(), a.stride(0), w.data_ptr(), s.data_ptr(),
+                                 res.data_ptr() if res is not None else None, res.stride(0) if res is not None else 0,
+                                 out.data_ptr(), out.stride(0), M, N, K,
+                                 _lib.HM_EPI_SILU if silu else _lib.HM_EPI_STORE,
+                                 error_word(a.device).data_ptr(), _stream()), "hm_gemm_i8w")
+    return out
+
+
+def prefill_attn(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, P: int, o: torch.Tensor | None = None,
+                 scale: float | None = None) -> torch.Tensor:
+    """Causal attention of a whole prompt: q ``[B*P, Hq*hd]`` (row ``b*P + p``) over
+    ``kc/vc[b, :, :P]``; returns o like q."""
+    _need_cuda(q, kc, vc, o)
+    B, Hk, L, hd = kc.shape
+    Hq = q.shape[1] // hd
+    if o is None:
+        o = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(hd) if scale is None else scale
+    check(_lib.lib().hm_prefill_attn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, P, Hq, Hk, hd, L,
+                                     scale, error_word(q.device).data_ptr(), _stream()), "hm_prefill_attn")
+    return o

@@ -1,23 +1,74 @@
 """Prompt prefill of the backbone: fills the static KV cache for positions [0, P).
 
 The reference runs the prompt through ``Stack.__call__`` (``app/engine.py:174-178,
-390-398``): dequantised fp16 GEMMs, torch RMSNorm/RoPE, ``index_copy_`` into the
-cache and causal SDPA.  Here every row of every prompt position goes through
-the same sm_100a decode launches (fused RMSNorm/RoPE/KV-write GEMVs and decode
-attention over ``[0, p]``, which is causal attention), one position per replay
-of a captured backbone-step graph.  The unnormalised hidden state of the last
-position is left in the runtime's residual buffer for the first frame.
+390-398``): per layer an RMSNorm, the dequantised fp16 GEMMs of ``int8_mm``'s
+M > 16 branch (``app/kernels.py:46-49``), RoPE, ``index_copy_`` into the cache,
+causal SDPA over ``repeat_interleave``d K/V, SiLU·mul and the residual adds.
+
+Here the B*P prompt rows go through, per layer:
+
+* ``hm_rmsnorm``                     RMSNorm of the residual stream
+* ``hm_gemm_i8w``                    q|k|v projection (tcgen05 tensor cores, int8 weights)
+* ``hm_rope_kv_write``               RoPE of q and k; k, v written into the cache slots
+* ``hm_prefill_attn``                causal GQA attention, K/V shared by each head group
+* ``hm_gemm_i8w`` (+ residual)       output projection, added in place
+* ``hm_rmsnorm``, ``hm_gemm_i8w`` SiLU epilogue (w1|w3 fused, SiLU·mul in the epilogue),
+  ``hm_gemm_i8w`` (+ residual)       the MLP
+
+The unnormalised hidden state of the last position of every row is left in the
+runtime's residual buffer (with its sums of squares) for the first frame.
+``prefill_backbone_steps`` is the position-by-position alternative through the
+decode launches (used by the tests as a second GPU path).
 """
 from __future__ import annotations
 
 import torch
 
+from . import kernels
 from ._lib import HMError
+
+
+def _rows_to_runtime(rt, x_last: torch.Tensor) -> None:
+    from .engine import SS_COLS
+    B, D = x_last.shape
+    rt.x_bb.copy_(x_last)
+    rt.ss_bb.copy_((x_last.float() ** 2).reshape(B, D // SS_COLS, SS_COLS).sum(-1).t())
 
 
 @torch.inference_mode()
 def prefill_backbone(model, h: torch.Tensor) -> None:
     """h ``[B, P, D]`` fp16 prompt embeddings on the device."""
+    rt = model._rt
+    if rt is None:
+        raise HMError("alloc() first")
+    B, P, D = h.shape
+    stack = model.backbone
+    L = stack.L
+    if P > L:
+        raise HMError(f"prompt of {P} positions does not fit the {L}-slot cache")
+    dev = h.device
+    M = B * P
+    x = h.reshape(M, D).contiguous().clone()
+    pos = torch.arange(P, device=dev, dtype=torch.long).repeat(B)
+    b0 = stack.blocks[0]
+    q = torch.empty(M, b0.h * b0.hd, device=dev, dtype=torch.float16)
+    for blk in stack.blocks:
+        hn = kernels.rms(x, blk.n1)
+        qkv = kernels.gemm_i8w(hn, blk.qkv.q8, blk.qkv.s8)
+        kernels.rope_cache(qkv, stack.rope, pos, q, blk.kc, blk.vc, P, blk.h, blk.kvh, L)
+        o = kernels.prefill_attn(q, blk.kc, blk.vc, P)
+        kernels.gemm_i8w(o, blk.o.q8, blk.o.s8, res=x, out=x)
+        hn = kernels.rms(x, blk.n2)
+        mm = kernels.gemm_i8w(hn, blk.w13.q8, blk.w13.s8, silu=True)
+        kernels.gemm_i8w(mm, blk.w2.q8, blk.w2.s8, res=x, out=x)
+    _rows_to_runtime(rt, x.reshape(B, P, D)[:, P - 1])
+
+
+@torch.inference_mode()
+def prefill_backbone_steps(model, h: torch.Tensor) -> None:
+    """The same through the decode launches: one position per replay of a captured
+    backbone-step graph (fused RMSNorm/RoPE/KV-write GEMVs, decode attention over
+    ``[0, p]``, which is causal attention)."""
     rt = model._rt
     if rt is None:
         raise HMError("alloc() first")

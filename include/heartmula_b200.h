@@ -177,6 +177,24 @@ int hm_cfg_topk_sample(const void* logits, int64_t ld_logits, int B, int N, int 
                        int64_t ld_noise, float cfg, int topk, float temp, int64_t* out, int64_t out_ld, int out_col,
                        int* err, int pdl, hm_stream_t stream);
 
+/* ------------------------------------------------------------------ prompt prefill
+ * Tensor-core GEMM with int8 weights for many rows (tcgen05 MMA, fp32 accumulators in TMEM):
+ *   epi HM_EPI_STORE: c[m, n] = fp16( sum_k a[m,k] * w[n,k] * s[n] ) (+ res[m, n] in fp16)
+ *   epi HM_EPI_SILU : w = [w1; w3] (N = 2F rows), c[m, f] = fp16( fp16(silu(a1)) * a3 ), f < F,
+ *                     a1/a3 the rounded w1/w3 outputs (res must be NULL)
+ * K % 64 == 0, output columns % 16 == 0, lda/ldc/ldr % 8 == 0, 16-byte aligned pointers; c may equal res.
+ * Replaces the M > 16 branch of int8_mm (app/kernels.py:46-49: dequantise, fp16 GEMM) used by
+ * the prompt pass of Block.__call__ (app/engine.py:123-153). */
+int hm_gemm_i8w(const void* a, int64_t lda, const int8_t* w, const void* s, const void* res, int64_t ldr, void* c,
+                int64_t ldc, int M, int N, int K, int epi, int* err, hm_stream_t stream);
+
+/* Causal GQA attention of a whole prompt over the cache positions [0, P) that the
+ * RoPE/KV-write step filled: q, o [B*P, Hq*hd] fp16 (row b*P + p), kc/vc [B, Hk, L, hd].
+ * hd == 128, Hq/Hk <= 4.  Replaces the prompt branch of Block.__call__'s attention
+ * (repeat_interleave + SDPA is_causal, app/engine.py:123-153). */
+int hm_prefill_attn(const void* q, const void* kc, const void* vc, void* o, int B, int P, int Hq, int Hk, int hd,
+                    int L, float scale, int* err, hm_stream_t stream);
+
 /* ------------------------------------------------------------------ info */
 int hm_device_sm_count(int device);
 /* sizeof / offsetof of the descriptor structs, for bindings to verify their layout:
