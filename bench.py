@@ -50,7 +50,7 @@ def args_():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn", "sampler"],
+    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn", "sampler", "prefill"],
                     help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures")
     ap.add_argument("--layers", type=int, default=4, help="backbone layers of the small cases")
     ap.add_argument("--reps", type=int, default=3)
@@ -386,6 +386,47 @@ def run_ours(a, world, rank, local):
         print(json.dumps(out), flush=True)
 
 
+def prefill_flops(m, B, P):
+    """Multiply-add FLOPs of the prompt pass: every backbone GEMM over B*P rows plus
+    causal attention (QK^T and PV over the lower triangle)."""
+    Mrows = B * P
+    f = 0
+    for b in m.backbone.blocks:
+        f += 2 * Mrows * (b.qkv.N * b.qkv.K + b.o.N * b.o.K + b.w13.N * b.w13.K + b.w2.N * b.w2.K)
+        f += 2 * 2 * B * b.h * b.hd * (P * (P + 1) // 2)
+    return f
+
+
+def run_prefill_case(a, bb_layers=None):
+    """Config 2: the prompt prefill of B rows x P tokens through the 28-layer backbone
+    (tensor-core GEMMs and causal attention), timed with CUDA events."""
+    from dataclasses import replace
+    from estudiocanciones_b200.checkpoint import BASELINE_SHAPE, synthetic_tensors
+    from estudiocanciones_b200.engine import HeartMuLaLite
+    from estudiocanciones_b200.prefill import prefill_backbone
+    dev = torch.device("cuda", 0)
+    shape = replace(BASELINE_SHAPE, text_vocab=1024, **({"bb_layers": bb_layers} if bb_layers else {}))
+    m = HeartMuLaLite(synthetic_tensors(shape, seed=0, device=dev, gamma_one=True), device=dev)
+    B, P = 2 * a.takes, a.prompt
+    m.alloc(a.takes, B, P + 256)
+    h = (torch.randn(B, P, shape.bb_dim, generator=torch.Generator(device=dev).manual_seed(0), device=dev)
+         * 0.05).half()
+    for _ in range(2):
+        prefill_backbone(m, h)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.reps):
+        prefill_backbone(m, h)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.reps
+    fl = prefill_flops(m, B, P)
+    print(json.dumps({"case": "prefill", "rows": B, "prompt": P, "layers": len(m.backbone.blocks),
+                      "ms": round(ms, 3), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+                      "flop": fl}), flush=True)
+
+
 def run_case(a):
     """Small single-kernel cases for profiling: the GEMV launches of a few backbone
     layers (weights > L2 but well under a GB), one decode-attention launch at the
@@ -451,6 +492,9 @@ def run_case(a):
 
 def main():
     a = args_()
+    if a.case == "prefill":
+        run_prefill_case(a)
+        return
     if a.case != "frame":
         run_case(a)
         return

@@ -255,9 +255,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     const int tiles = s.ss_tiles;
     const int64_t ld = s.ss_ld;
     const float dim = static_cast<float>(s.dim), eps = s.eps;
-    float a = 0.f;
-    for (int t = lane; t < tiles; t += 32) a += ss[(int64_t)t * ld + row];
-    a = warp_sum(a);
+    const float a = warp_sum_partials(ss, tiles, ld, row, lane);
     if (lane == 0) inv_s[m] = 1.0f / sqrtf(a / dim + eps);
   }
   cp_async_wait_all();
@@ -641,6 +639,9 @@ cudaError_t launch_mt(int mt, const CUtensorMap& map, const GemvParams& p, cudaS
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+// weight tensor map for the persistent stage runner (same boxes and cache)
+bool hm_seq_weight_map(const int8_t* w, int N, int K, CUtensorMap* out) { return weight_map(w, N, K, out); }
 
 extern "C" int hm_gemv_pick_kspan(int M, int N, int K, int epi, int kspan) {
   (void)N;

@@ -219,6 +219,24 @@ HM_DEV float warp_max(float v) {
 
 // fp16(a) * fp16(b) rounded once to fp16 (the product of two fp16 values is
 // exact in fp32, so this equals an IEEE fp16 multiply).
+// Sum over t < tiles of ss[t*ld + row] by one warp, lane-strided in increasing t
+// (the same order as a plain strided loop), with 16 loads per lane in flight at
+// once instead of one memory latency per 32 partials.
+HM_DEV float warp_sum_partials(const float* ss, int tiles, int64_t ld, int row, int lane) {
+  float a = 0.f;
+  for (int base = 0; base < tiles; base += 512) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int t = base + lane + 32 * i;
+      v[i] = t < tiles ? ss[(int64_t)t * ld + row] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a += v[i];
+  }
+  return warp_sum(a);
+}
+
 HM_DEV __half hmul_rn(__half a, __half b) { return __float2half_rn(__half2float(a) * __half2float(b)); }
 HM_DEV __half hadd_rn(__half a, __half b) { return __hadd(a, b); }
 

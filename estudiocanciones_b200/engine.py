@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 from pathlib import Path
 
 import torch
@@ -214,23 +215,77 @@ class StackBuffers:
 
 class FramePlan:
     """An ordered list of launches on fixed buffers.  ``run()`` issues them on the
-    current stream; running it inside ``torch.cuda.graph`` captures the frame."""
+    current stream; running it inside ``torch.cuda.graph`` captures the frame.
 
-    def __init__(self, ctx: _Ctx, pdl: bool = True):
+    ``persistent``: runs of consecutive GEMV / attention / embedding-sum steps that
+    the stage runner supports are recorded into stage sequences (``hm_seq_*``) and
+    each run becomes ONE cooperative launch; everything else stays a launch of its
+    own and closes the current sequence."""
+
+    def __init__(self, ctx: _Ctx, pdl: bool = True, persistent: bool = False):
         self.ctx = ctx
         self.ops = []
         self.pdl = int(pdl)
+        self.persistent = bool(persistent)
         self._keep = []
+        self._seg = None
+        self._segs = []
         self.n_kernels = 0
+        self.n_stages = 0
+
+    def __del__(self):
+        try:
+            L = _lib.lib()
+            for q in self._segs:
+                L.hm_seq_destroy(q)
+        except Exception:
+            pass
+        self._segs = []
 
     def run(self):
+        if self._seg is not None:
+            self._flush()
         st = torch.cuda.current_stream().cuda_stream
         for op in self.ops:
             op(st)
 
+    # ------------------------------------------------------------------ stage sequences
+    def _seg_try(self, add):
+        """Offer one step to the open sequence; False if the runner cannot take it."""
+        if not self.persistent:
+            return False
+        L = _lib.lib()
+        if self._seg is None:
+            self._seg = L.hm_seq_create()
+            if not self._seg:
+                raise _lib.HMError("hm_seq_create failed")
+            self._segs.append(self._seg)
+        rc = add(L, self._seg)
+        if rc == 0:
+            self.n_stages += 1
+            return True
+        if rc not in (_lib.HM_EARG, _lib.HM_ENOSPACE):
+            check(rc, "hm_seq_add")
+        self._flush()
+        return False
+
+    def _flush(self):
+        q = self._seg
+        self._seg = None
+        if q is None:
+            return
+        L = _lib.lib()
+        if L.hm_seq_size(q) == 0:
+            return
+        check(L.hm_seq_finalize(q), "hm_seq_finalize")
+        err = self.ctx.err.data_ptr()
+        fn = L.hm_seq_launch
+        self.ops.append(lambda st: check(fn(q, err, st), "hm_seq_launch"))
+        self.n_kernels += 1
+
     # ------------------------------------------------------------------ primitives
     def _gemv(self, lin: Linear, M, src0, src1=None, epi=HM_EPI_STORE, y=None, res=None, ss_out=None,
-              rope=None, pos=None, S=1, blk: Block | None = None, q_out=None, kspan=0):
+              rope=None, pos=None, S=1, blk: Block | None = None, q_out=None, kspan=0, keep=False):
         L = _lib.lib()
         d = GemvDesc()
         d.w, d.s, d.N, d.K, d.M = lin.q8.data_ptr(), lin.s8.data_ptr(), lin.N, lin.K, M
@@ -256,6 +311,9 @@ class FramePlan:
         d.err, d.kspan, d.pdl = self.ctx.err.data_ptr(), kspan, self.pdl
         self._keep.append(d)
         ref = C.byref(d)
+        if kspan == 0 and self._seg_try(lambda Lb, q: Lb.hm_seq_add_gemv(q, ref, int(keep))):
+            return
+        self._flush()
         fn = L.hm_gemv_i8_fused
         self.ops.append(lambda st: check(fn(ref, st), "hm_gemv_i8_fused"))
         self.n_kernels += 1
@@ -284,6 +342,8 @@ class FramePlan:
 
     def sumsq(self, x, ss, R):
         """ss partials of an fp16 matrix that no fused producer wrote (API entry points)."""
+        self._flush()
+
         def op(st, x=x, ss=ss, R=R):
             D = x.shape[1]
             part = (x[:R].float() ** 2).reshape(R, D // SS_COLS, SS_COLS).sum(-1)
@@ -297,32 +357,39 @@ class FramePlan:
         args = (q.data_ptr(), blk.kc.data_ptr(), blk.vc.data_ptr(), pos.data_ptr(), o.data_ptr(), R, S, blk.h,
                 blk.kvh, blk.hd, blk.kc.shape[2], 1.0 / math.sqrt(blk.hd), nsplit, self.ctx.attn_ws.data_ptr(),
                 self.ctx.attn_ws.numel(), self.ctx.attn_tk, 32768, self.ctx.err.data_ptr(), self.pdl)
+        if self._seg_try(lambda Lb, qq: Lb.hm_seq_add_attn(qq, *args[:17])):
+            return
+        self._flush()
         fn = L.hm_decode_attn
         self.ops.append(lambda st: check(fn(*args, st), "hm_decode_attn"))
         self.n_kernels += 1
 
     # ------------------------------------------------------------------ composites
-    def stack(self, stack: Stack, bufs: StackBuffers, pos, S, R, nsplit):
+    def stack(self, stack: Stack, bufs: StackBuffers, pos, S, R, nsplit, keep=False):
         """The per-layer loop of ``Stack.decode`` with everything fused into 5 launches per layer.
         Expects ``bufs.x`` and its ss partials in ``bufs.ss``; leaves the (un-normalised)
         output in ``bufs.x`` with fresh ss partials."""
         for b in stack.blocks:
             self._gemv(b.qkv, R, self.src_rms(bufs.x, bufs.ss, b.n1), epi=HM_EPI_ROPE_KV, rope=stack.rope,
-                       pos=pos, S=S, blk=b, q_out=bufs.q)
+                       pos=pos, S=S, blk=b, q_out=bufs.q, keep=keep)
             self.attn(b, bufs.q, bufs.o, pos, S, R, nsplit)
-            self._gemv(b.o, R, self.src_f16(bufs.o), y=bufs.x, res=bufs.x, ss_out=bufs.ss)
-            self._gemv(b.w13, R, self.src_rms(bufs.x, bufs.ss, b.n2), epi=HM_EPI_SILU, y=bufs.mm)
-            self._gemv(b.w2, R, self.src_f16(bufs.mm), y=bufs.x, res=bufs.x, ss_out=bufs.ss)
+            self._gemv(b.o, R, self.src_f16(bufs.o), y=bufs.x, res=bufs.x, ss_out=bufs.ss, keep=keep)
+            self._gemv(b.w13, R, self.src_rms(bufs.x, bufs.ss, b.n2), epi=HM_EPI_SILU, y=bufs.mm, keep=keep)
+            self._gemv(b.w2, R, self.src_f16(bufs.mm), y=bufs.x, res=bufs.x, ss_out=bufs.ss, keep=keep)
 
     def emb_sum(self, emb: Emb, tok, R, ncb, vocab, x, ss):
         L = _lib.lib()
         args = (tok.data_ptr(), tok.stride(0), R, ncb, vocab, emb.q8.data_ptr(), emb.s8.data_ptr(), emb.q8.shape[0],
                 x.shape[1], x.data_ptr(), ss.data_ptr(), ss.stride(0), self.ctx.err.data_ptr(), self.pdl)
+        if self._seg_try(lambda Lb, q: Lb.hm_seq_add_emb_sum(q, *args[:12])):
+            return
+        self._flush()
         fn = L.hm_emb_sum_i8
         self.ops.append(lambda st: check(fn(*args, st), "hm_emb_sum_i8"))
         self.n_kernels += 1
 
     def sample(self, logits, n_takes, cfg, topk, temp, noise, out, col):
+        self._flush()
         L = _lib.lib()
         B, V = logits.shape
         args = (logits.data_ptr(), logits.stride(0), B, n_takes, V, noise.data_ptr(), noise.stride(0), float(cfg),
@@ -332,6 +399,7 @@ class FramePlan:
         self.n_kernels += 1
 
     def commit(self, tok_out, tok_in, pos, n_keep, stream, frame):
+        self._flush()
         L = _lib.lib()
         B, ncb = tok_out.shape
         args = (tok_out.data_ptr(), tok_in.data_ptr(), B, ncb, pos.data_ptr(), n_keep, _p(stream), frame.data_ptr(),
@@ -341,6 +409,7 @@ class FramePlan:
         self.n_kernels += 1
 
     def torch_op(self, f):
+        self._flush()
         self.ops.append(lambda st: f())
 
 
@@ -580,6 +649,9 @@ class _Runtime:
         self.noise_stream = torch.cuda.Stream(device=dev)
         self.draw_noise = True
         self.pdl = True
+        # HM_PERSISTENT=1: one cooperative launch (stage sequence) per run of fused steps
+        # instead of separate launches; off by default until it is the faster path
+        self.persistent = os.environ.get("HM_PERSISTENT", "0") != "0"
         self.force = torch.zeros(B, m.n_cb, dtype=torch.long, device=dev)
         self.rec = torch.zeros(m.n_cb, B, m.vocab, dtype=torch.float16, device=dev)
         self.ctx.reserve(m, B, self.nsplit)
@@ -638,7 +710,7 @@ class _Runtime:
         m = self.m
         B, N = self.B, self.N
         V = m.vocab
-        plan = FramePlan(self.ctx, pdl=self.pdl)
+        plan = FramePlan(self.ctx, pdl=self.pdl, persistent=self.persistent)
         join = self._noise_ops(plan)
         if teacher:
             # teacher forcing: record every head's logits and take the forced ids
@@ -664,17 +736,18 @@ class _Runtime:
         sample(0, self.noise[0])
         # decoder pass 0: rows (2b, 2b+1) = (last_h[b], emb(0, c0[b])) at positions (0, 1)
         last_h = plan.src_f16(bb.x) if normed_input else plan.src_rms(bb.x, bb.ss, m.backbone.norm)
-        plan._gemv(m.projection, 2 * B, last_h,
-                   plan.src_emb(m.audio_emb, self.tok_out, 0, 0), y=dec.x, ss_out=dec.ss)
-        plan.stack(m.decoder, dec, self.dpos0, 2, 2 * B, 1)
-        plan._gemv(m.audio_head[0], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm, row_mul=2, row_add=1),
+        plan._gemv(m.projection, 2 * B, last_h, plan.src_emb(m.audio_emb, self.tok_out, 0, 0), y=dec.x,
+                   ss_out=dec.ss, keep=True)
+        plan.stack(m.decoder, dec, self.dpos0, 2, 2 * B, 1, keep=True)
+        plan._gemv(m.audio_head[0], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm, row_mul=2, row_add=1), keep=True,
                    y=self.logits)
         sample(1, self.noise[1])
         for c in range(2, m.n_cb):
-            plan._gemv(m.projection, B, plan.src_emb(m.audio_emb, self.tok_out, c - 1, (c - 1) * V),
+            plan._gemv(m.projection, B, plan.src_emb(m.audio_emb, self.tok_out, c - 1, (c - 1) * V), keep=True,
                        y=dec.x, ss_out=dec.ss)
-            plan.stack(m.decoder, dec, self.dpos[c], 1, B, 1)
-            plan._gemv(m.audio_head[c - 1], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm), y=self.logits)
+            plan.stack(m.decoder, dec, self.dpos[c], 1, B, 1, keep=True)
+            plan._gemv(m.audio_head[c - 1], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm), y=self.logits,
+                       keep=True)
             sample(c, self.noise[c])
         if commit:
             plan.commit(self.tok_out, self.tok_in, self.pos, N, self.stream_out, self.frame)
