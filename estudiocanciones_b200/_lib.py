@@ -40,7 +40,7 @@ class GemvDesc(C.Structure):
                 ("S", C.c_int), ("Hq", C.c_int), ("Hk", C.c_int), ("hd", C.c_int), ("L", C.c_int),
                 ("q_out", _P), ("kc", _P), ("vc", _P),
                 ("ws", _P), ("ws_bytes", C.c_size_t), ("counters", _P), ("n_counters", C.c_int),
-                ("err", _P), ("kspan", C.c_int), ("pdl", C.c_int)]
+                ("err", _P), ("kspan", C.c_int), ("pdl", C.c_int), ("l2_keep", C.c_int)]
 
 
 SIGNATURES = {
@@ -112,5 +112,5 @@ def abi_mismatches() -> list[str]:
     """Compare the ctypes struct layouts with the library's own sizeof/offsetof."""
     L = lib()
     want = {0: C.sizeof(RowSrc), 1: C.sizeof(GemvDesc), 2: GemvDesc.src.offset, 3: GemvDesc.ws.offset,
-            4: GemvDesc.pdl.offset}
+            4: GemvDesc.pdl.offset, 5: GemvDesc.l2_keep.offset}
     return [f"layout[{k}]: C {L.hm_abi_layout(k)} vs ctypes {v}" for k, v in want.items() if L.hm_abi_layout(k) != v]

@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       int* const perr = d.err;
       const int half_n = d.N / 2;
       prefetch_tensormap(&wmap);
-      const uint64_t pol = policy_evict_first();
+      const uint64_t pol = d.l2_keep ? policy_evict_last() : policy_evict_first();
       for (int it = 0; it < nstages; ++it) {
         const int slot = it % kNST;
         if (it >= kNST) mbar_wait_ab(&empty[slot], ((it / kNST) - 1) & 1, perr, abort_s);
@@ -750,8 +750,9 @@ extern "C" size_t hm_abi_layout(int which) {
     case 2: return offsetof(hm_gemv_desc, src);
     case 3: return offsetof(hm_gemv_desc, ws);
     case 4: return offsetof(hm_gemv_desc, pdl);
+    case 5: return offsetof(hm_gemv_desc, l2_keep);
     default: return 0;
   }
 }
 
-extern "C" const char* hm_version(void) { return "heartmula_b200 0.2 sm_100a"; }
+extern "C" const char* hm_version(void) { return "heartmula_b200 0.3 sm_100a"; }

@@ -308,7 +308,7 @@ class FramePlan:
         self.ctx.need(wsb, 0)
         d.ws, d.ws_bytes = self.ctx.ws.data_ptr(), self.ctx.ws.numel()
         d.counters, d.n_counters = self.ctx.gemv_tk, 32768
-        d.err, d.kspan, d.pdl = self.ctx.err.data_ptr(), kspan, self.pdl
+        d.err, d.kspan, d.pdl, d.l2_keep = self.ctx.err.data_ptr(), kspan, self.pdl, int(keep)
         self._keep.append(d)
         ref = C.byref(d)
         if kspan == 0 and self._seg_try(lambda Lb, q: Lb.hm_seq_add_gemv(q, ref, int(keep))):

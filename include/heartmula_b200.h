@@ -105,6 +105,7 @@ typedef struct {
   int* err;
   int kspan;                    /* 0 = automatic */
   int pdl;                      /* launch with programmatic dependent launch */
+  int l2_keep;                  /* weights read again soon (decoder passes): L2 evict-last instead of evict-first */
 } hm_gemv_desc;
 
 /* The fused GEMV: prologue rows from `src`, epilogue per `epi`.  The per-layer
@@ -231,7 +232,7 @@ int hm_prefill_attn(const void* q, const void* kc, const void* vc, void* o, int 
 int hm_device_sm_count(int device);
 /* sizeof / offsetof of the descriptor structs, for bindings to verify their layout:
  * 0 sizeof(hm_row_src), 1 sizeof(hm_gemv_desc), 2 offsetof(hm_gemv_desc, src),
- * 3 offsetof(hm_gemv_desc, ws), 4 offsetof(hm_gemv_desc, pdl). */
+ * 3 offsetof(hm_gemv_desc, ws), 4 offsetof(hm_gemv_desc, pdl), 5 offsetof(hm_gemv_desc, l2_keep). */
 size_t hm_abi_layout(int which);
 const char* hm_version(void);
 
