@@ -235,55 +235,118 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     if (g0) bulk_load(gam_s, gam0 + k0, kend * 2, xbar);
     if (g1) bulk_load(gam_s + kspan, gam1 + k0, kend * 2, xbar);
   }
+  // (row-uniform branches: fp16/RMS rows only need their tail past K zeroed, usually none)
+  const int ctail = kend / 8;  // first chunk past the valid columns
   for (int m = 0; m < MROWS; ++m) {
     const int mode = m < M ? rmode_s[m] : -1;
-    const uint8_t* base = rowp_s[m];
     uint8_t* xr = xsm + m * L.xp;
-    for (int c = tid; c < cpr; c += kCons) {
-      if (mode < 0 || 8 * c >= kend)
-        *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
-      else if (mode == HM_SRC_EMB)
-        cp_async8(xr + c * 16, base + k0 + 8 * c);
+    if (mode == HM_SRC_EMB) {
+      const uint8_t* base = rowp_s[m] + k0;
+      for (int c = tid; c < ctail; c += kCons) cp_async8(xr + c * 16, base + 8 * c);
     }
+    for (int c = (mode < 0 ? 0 : ctail) + tid; c < cpr; c += kCons)
+      *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
   }
-  // ---- RMSNorm 1/rms of RMS rows from the producers' ss partials, while the copies fly
-  for (int m = warp; m < M; m += kCons / 32) {
-    int row, sel;
-    const hm_row_src& s = src_of(d, m, row, sel);
-    if (s.mode != HM_SRC_RMS) continue;
-    const float* ss = s.ss;
-    const int tiles = s.ss_tiles;
-    const int64_t ld = s.ss_ld;
-    const float dim = static_cast<float>(s.dim), eps = s.eps;
-    const float a = warp_sum_partials(ss, tiles, ld, row, lane);
-    if (lane == 0) inv_s[m] = 1.0f / sqrtf(a / dim + eps);
+  // ---- RMSNorm 1/rms of RMS rows from the producers' ss partials, while the copies fly.
+  // Every CTA reads the same few KB of partials, so the read pattern matters: with one
+  // source of consecutive rows (the decode layout) each thread loads whole 16-byte
+  // groups of rows of its partial tiles (one request per 4 rows instead of one per
+  // value), and the CTA reduces them; otherwise one warp per row.
+  const hm_row_src& s0 = d.src[0];
+  const bool rms_vec = !d.interleave && s0.mode == HM_SRC_RMS && s0.row_mul == 1 && (s0.row_add & 3) == 0 &&
+                       (s0.ss_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(s0.ss) & 15u) == 0;
+  if (rms_vec) {
+    constexpr int NV = (MROWS + 3) / 4;
+    const int nv = (M + 3) / 4;
+    float a[4 * NV];
+#pragma unroll
+    for (int i = 0; i < 4 * NV; ++i) a[i] = 0.f;
+    const float* ss = s0.ss + s0.row_add;
+    const int tiles = s0.ss_tiles;
+    const int64_t ld = s0.ss_ld;
+    for (int t = tid; t < tiles; t += kCons) {
+      const float4* p4 = reinterpret_cast<const float4*>(ss + (int64_t)t * ld);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        if (j < nv) {
+          const float4 v = p4[j];
+          a[4 * j] += v.x;
+          a[4 * j + 1] += v.y;
+          a[4 * j + 2] += v.z;
+          a[4 * j + 3] += v.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4 * NV; ++i) a[i] = warp_sum(a[i]);
+    float* part = red_s;  // [4 warps][MROWS], free until the first tile
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < 4 * NV; ++i)
+        if (i < MROWS) part[warp * MROWS + i] = a[i];
+    }
+    named_bar(kBarCons, kCons);
+    if (tid < M) {
+      const float tot = ((part[tid] + part[MROWS + tid]) + part[2 * MROWS + tid]) + part[3 * MROWS + tid];
+      inv_s[tid] = 1.0f / sqrtf(tot / static_cast<float>(s0.dim) + s0.eps);
+    }
+  } else {
+    for (int m = warp; m < M; m += kCons / 32) {
+      int row, sel;
+      const hm_row_src& s = src_of(d, m, row, sel);
+      if (s.mode != HM_SRC_RMS) continue;
+      const float a = warp_sum_partials(s.ss, s.ss_tiles, s.ss_ld, row, lane);
+      if (lane == 0) inv_s[m] = 1.0f / sqrtf(a / static_cast<float>(s.dim) + s.eps);
+    }
   }
   cp_async_wait_all();
   mbar_wait_ab(xbar, 0, err, abort_s);
   named_bar(kBarCons, kCons);
 
-  // ---- in-place transforms: RMSNorm (fp16(x*inv) * gamma) and int8 -> fp16 embedding rows
+  // ---- in-place transforms.  RMSNorm, fp16(fp16(x * inv) * gamma): chunk-outer with the
+  // 8 rows of a group loaded together, so each thread has 8 independent load / math /
+  // store chains in flight (a row-outer loop is latency-bound at 4 warps per CTA).
+  bool any_rms = false, any_emb = false;
   for (int m = 0; m < M; ++m) {
-    const int mode = rmode_s[m];
-    if (mode != HM_SRC_RMS && mode != HM_SRC_EMB) continue;
-    uint8_t* xr = xsm + m * L.xp;
-    if (mode == HM_SRC_RMS) {
-      const float inv = inv_s[m];
-      const __half* gs = gam_s + rsel_s[m] * kspan;
-      for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
-        uint4* slot = reinterpret_cast<uint4*>(xr + c * 16);
-        uint4 v = *slot;
-        const uint4 gv = *reinterpret_cast<const uint4*>(gs + 8 * c);
-        __half2* vh = reinterpret_cast<__half2*>(&v);
-        const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+    any_rms |= rmode_s[m] == HM_SRC_RMS;
+    any_emb |= rmode_s[m] == HM_SRC_EMB;
+  }
+  if (any_rms) {
+    for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
+      const uint4 gv0 = *reinterpret_cast<const uint4*>(gam_s + 8 * c);
+      const uint4 gv1 = g1 ? *reinterpret_cast<const uint4*>(gam_s + kspan + 8 * c) : gv0;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {  // fp16(fp16(x * inv) * gamma), each step rounded once
-          const float2 f = __half22float2(vh[j]);
-          vh[j] = __hmul2(__floats2half2_rn(f.x * inv, f.y * inv), gh[j]);
+      for (int m0 = 0; m0 < MROWS; m0 += 8) {
+        uint4 v[8];
+        bool on[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int m = m0 + i;
+          on[i] = m < M && rmode_s[m] == HM_SRC_RMS;
+          if (on[i]) v[i] = *reinterpret_cast<const uint4*>(xsm + m * L.xp + c * 16);
         }
-        *slot = v;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (!on[i]) continue;
+          const int m = m0 + i;
+          const float inv = inv_s[m];
+          const uint4 gv = rsel_s[m] ? gv1 : gv0;
+          __half2* vh = reinterpret_cast<__half2*>(&v[i]);
+          const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // each step rounded once
+            const float2 f = __half22float2(vh[j]);
+            vh[j] = __hmul2(__floats2half2_rn(f.x * inv, f.y * inv), gh[j]);
+          }
+          *reinterpret_cast<uint4*>(xsm + m * L.xp + c * 16) = v[i];
+        }
       }
-    } else {
+    }
+  }
+  if (any_emb) {  // int8 -> fp16 embedding rows
+    for (int m = 0; m < M; ++m) {
+      if (rmode_s[m] != HM_SRC_EMB) continue;
+      uint8_t* xr = xsm + m * L.xp;
       const float sc = esc_s[m];
       for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
         uint4* slot = reinterpret_cast<uint4*>(xr + c * 16);

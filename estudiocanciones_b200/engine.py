@@ -153,6 +153,9 @@ class Stack:
 def default_nsplit(R, Hk, L, sms=None):
     """Split count for decode attention: one wave of two CTAs per SM, at most one
     split per 64 cache positions (one K/V stage)."""
+    env = os.environ.get("HM_ATTN_SPLIT")
+    if env:
+        return int(env)
     if sms is None:
         sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     return int(max(1, min(2 * sms // max(1, R * Hk), max(1, L // 64), 64)))
