@@ -312,33 +312,40 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     any_emb |= rmode_s[m] == HM_SRC_EMB;
   }
   if (any_rms) {
+    // per-row parameters in registers (the stores below go through a byte pointer,
+    // which would otherwise force every shared-memory scalar to be re-read)
+    float invr[MROWS];
+    uint32_t onmask = 0, selmask = 0;
+#pragma unroll
+    for (int m = 0; m < MROWS; ++m) {
+      const bool on = m < M && rmode_s[m] == HM_SRC_RMS;
+      invr[m] = on ? inv_s[m] : 0.f;
+      onmask |= on ? (1u << m) : 0u;
+      selmask |= (on && rsel_s[m]) ? (1u << m) : 0u;
+    }
+    uint4* const x4 = reinterpret_cast<uint4*>(xsm);
+    const int xp4 = L.xp / 16;
     for (int c = tid; c < cpr && 8 * c < kend; c += kCons) {
-      const uint4 gv0 = *reinterpret_cast<const uint4*>(gam_s + 8 * c);
-      const uint4 gv1 = g1 ? *reinterpret_cast<const uint4*>(gam_s + kspan + 8 * c) : gv0;
+      const uint4 gv0 = reinterpret_cast<const uint4*>(gam_s)[c];
+      const uint4 gv1 = g1 ? reinterpret_cast<const uint4*>(gam_s + kspan)[c] : gv0;
 #pragma unroll
       for (int m0 = 0; m0 < MROWS; m0 += 8) {
         uint4 v[8];
-        bool on[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if ((onmask >> (m0 + i)) & 1u) v[i] = x4[(m0 + i) * xp4 + c];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int m = m0 + i;
-          on[i] = m < M && rmode_s[m] == HM_SRC_RMS;
-          if (on[i]) v[i] = *reinterpret_cast<const uint4*>(xsm + m * L.xp + c * 16);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (!on[i]) continue;
-          const int m = m0 + i;
-          const float inv = inv_s[m];
-          const uint4 gv = rsel_s[m] ? gv1 : gv0;
-          __half2* vh = reinterpret_cast<__half2*>(&v[i]);
-          const __half2* gh = reinterpret_cast<const __half2*>(&gv);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {  // each step rounded once
-            const float2 f = __half22float2(vh[j]);
-            vh[j] = __hmul2(__floats2half2_rn(f.x * inv, f.y * inv), gh[j]);
-          }
-          *reinterpret_cast<uint4*>(xsm + m * L.xp + c * 16) = v[i];
+          if (!((onmask >> m) & 1u)) continue;
+          const float inv = invr[m];
+          const uint4 gv = ((selmask >> m) & 1u) ? gv1 : gv0;
+          uint4 r;
+          r.x = rms_h2(v[i].x, gv.x, inv);
+          r.y = rms_h2(v[i].y, gv.y, inv);
+          r.z = rms_h2(v[i].z, gv.z, inv);
+          r.w = rms_h2(v[i].w, gv.w, inv);
+          x4[m * xp4 + c] = r;
         }
       }
     }

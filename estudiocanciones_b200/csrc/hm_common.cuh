@@ -237,6 +237,19 @@ HM_DEV float warp_sum_partials(const float* ss, int tiles, int64_t ld, int row, 
   return warp_sum(a);
 }
 
+// RMSNorm of two packed fp16 values: fp16(fp16(x * inv) * g), each product rounded once
+// (register-only: no address-taken temporaries).
+HM_DEV uint32_t rms_h2(uint32_t xv, uint32_t gv, float inv) {
+  const float x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(xv & 0xffffu)));
+  const float x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(xv >> 16)));
+  const __half2 n = __floats2half2_rn(x0 * inv, x1 * inv);
+  const __half2 g = __halves2half2(__ushort_as_half(static_cast<unsigned short>(gv & 0xffffu)),
+                                   __ushort_as_half(static_cast<unsigned short>(gv >> 16)));
+  const __half2 r = __hmul2(n, g);
+  return static_cast<uint32_t>(__half_as_ushort(__low2half(r))) |
+         (static_cast<uint32_t>(__half_as_ushort(__high2half(r))) << 16);
+}
+
 HM_DEV __half hmul_rn(__half a, __half b) { return __float2half_rn(__half2float(a) * __half2float(b)); }
 HM_DEV __half hadd_rn(__half a, __half b) { return __hadd(a, b); }
 
