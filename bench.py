@@ -53,6 +53,7 @@ def args_():
     ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn", "sampler", "prefill"],
                     help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures")
     ap.add_argument("--layers", type=int, default=4, help="backbone layers of the small cases")
+    ap.add_argument("--prefill-layers", type=int, default=28, help="backbone layers of the prefill case")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
@@ -493,7 +494,7 @@ def run_case(a):
 def main():
     a = args_()
     if a.case == "prefill":
-        run_prefill_case(a)
+        run_prefill_case(a, bb_layers=a.prefill_layers)
         return
     if a.case != "frame":
         run_case(a)
