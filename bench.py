@@ -291,16 +291,15 @@ def run_ours(a, world, rank, local):
     rt.pdl = not a.no_pdl
     graph = rt.graph_for(1.5, 50, 1.0)
     plan = rt.plan_for(1.5, 50, 1.0, with_backbone=True, commit=True)
-    gathered = [torch.empty_like(rt.stream_out[:F_]) for _ in range(world)] if world > 1 else None
+    from estudiocanciones_b200.shard import gather_streams
 
     def step():
         rt.pos.fill_(P)
         rt.frame.zero_()
         for _ in range(F_):
             graph.replay()
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_gather(gathered, rt.stream_out[:F_])
+        if world > 1:  # finished token streams of every rank's takes -> rank 0 (NCCL)
+            gather_streams([rt.stream_out[:F_, i].t() for i in range(N)], N * world, world, rank)
 
     for _ in range(a.warmup):
         step()
@@ -349,14 +348,17 @@ def run_ours(a, world, rank, local):
            "clocks": clk}
     # ---- end to end through the public API: host prompt ids -> generate -> host token streams
     if not a.no_e2e:
-        text = torch.randint(0, 128256, (P,), generator=torch.Generator().manual_seed(rank)).pin_memory()
+        text = torch.randint(0, 128256, (P,), generator=torch.Generator().manual_seed(0)).pin_memory()
         del rt, graph
         m.release()
 
+        from estudiocanciones_b200.shard import generate_sharded
+
         def e2e_step():
-            res = m.generate_ids(text, 10, max_ms=F_ * 80, n=a.takes, cfg_scale=1.5, seed=rank,
-                                 stop_at_eos=False)
-            return [r.cpu() for r in res]
+            # this rank's takes of the whole job, streams gathered on rank 0 (NCCL) and read back
+            res = generate_sharded(m, text, 10, a.takes * world, world=world, rank=rank, max_ms=F_ * 80,
+                                   cfg_scale=1.5, stop_at_eos=False)
+            return [r.cpu() for r in res] if res is not None else []
         e2e_step()
         torch.cuda.synchronize()
         barrier(world)
