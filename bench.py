@@ -371,7 +371,8 @@ def run_ours(a, world, rank, local):
         out["e2e"] = {"value": round(world * a.takes * F_ * 0.08 / sec, 3), "unit": UNIT,
                       "h2d_bytes_per_step": P * 8, "d2h_bytes_per_step": int(d2h),
                       "ms_per_step": round(1000 * sec, 2),
-                      "includes": "prompt H2D, GPU text-embedding gather, prefill, 750 frames, EOS checks, D2H"}
+                      "includes": f"prompt H2D, GPU text-embedding gather, tensor-core prefill, {F_} frames, "
+                                  f"EOS checks every 25 frames, token streams gathered and read back"}
     # ---- CPU baseline: the reference CPU path on this host, rank 0 at N=1
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         tcpu = {k: v.cpu() for k, v in model_tensors(dev, seed=0).items()}
