@@ -55,6 +55,7 @@ constexpr int kBarCons = 1;     // named barrier of the consumer warps
 struct GemvParams {
   hm_gemv_desc d;
   int kspan, nsplit, ntiles, has_gamma;
+  int xcontig;  // the M input rows are one contiguous block: staged by one bulk copy, unpadded pitch
 };
 
 struct SmemLayout {
@@ -66,10 +67,10 @@ __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a *
 __host__ __device__ inline int rt_of(int epi) { return epi == HM_EPI_SILU ? 2 : 1; }
 __host__ __device__ inline int ks_of(int epi) { return 4 * kBox / rt_of(epi); }  // k bytes per stage
 
-__host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_gamma) {
+__host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_gamma, int xcontig = 0) {
   SmemLayout L;
   L.ring = 0;
-  L.xp = kspan * 2 + 16;
+  L.xp = kspan * 2 + (xcontig ? 0 : 16);
   L.x = kNST * kStage;
   L.gam = align_up(L.x + mrows * L.xp, 16);
   L.red = L.gam + (has_gamma ? 2 * kspan * 2 : 0);
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   const int per_tile = kspan / KS;  // stages per tile
   const int my_tiles = (P.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int nstages = my_tiles * per_tile;
-  const SmemLayout L = smem_layout(kspan, MROWS, P.has_gamma);
+  const SmemLayout L = smem_layout(kspan, MROWS, P.has_gamma, P.xcontig);
   uint8_t* ring = smem + L.ring;
   uint8_t* xsm = smem + L.x;
   __half* gam_s = reinterpret_cast<__half*>(smem + L.gam);
@@ -229,9 +230,13 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     for (int m = 0; m < M; ++m) bytes += (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS) ? kend * 2 : 0;
     bytes += (g0 ? kend * 2 : 0) + (g1 ? kend * 2 : 0);
     mbar_arrive_expect_tx(xbar, bytes);
-    for (int m = 0; m < M; ++m)
-      if (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS)
-        bulk_load(xsm + m * L.xp, rowp_s[m] + 2 * k0, kend * 2, xbar);
+    if (P.xcontig) {  // all M rows in one request (the issue cost is per request)
+      bulk_load(xsm, rowp_s[0], static_cast<uint32_t>(M) * kend * 2, xbar);
+    } else {
+      for (int m = 0; m < M; ++m)
+        if (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS)
+          bulk_load(xsm + m * L.xp, rowp_s[m] + 2 * k0, kend * 2, xbar);
+    }
     if (g0) bulk_load(gam_s, gam0 + k0, kend * 2, xbar);
     if (g1) bulk_load(gam_s + kspan, gam1 + k0, kend * 2, xbar);
   }
@@ -678,7 +683,7 @@ int auto_kspan(int M, int K, int epi) {
 
 template <int MT, int EPI>
 cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p, cudaStream_t st) {
-  const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma).total;
+  const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig).total;
   static int configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -760,6 +765,16 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
   if (p.kspan <= 0 || p.kspan % ks_of(d->epi) || kpad % p.kspan) return HM_EARG;
   if (smem_layout(p.kspan, mrows_of(d->M), has_gamma).total > 227 * 1024) return HM_EARG;
   p.nsplit = kpad / p.kspan;
+  {
+    // one bulk copy for all rows: one fp16/RMS source, consecutive rows, row pitch K,
+    // whole K in one k-range with no padding columns, 16-byte aligned block start
+    static const int contig_on = static_cast<int>(env_or("HM_GEMV_XCONTIG", 1));
+    const hm_row_src& s0 = d->src[0];
+    const char* blk = reinterpret_cast<const char*>(s0.x) + static_cast<int64_t>(s0.row_add) * s0.ldx * 2;
+    p.xcontig = contig_on && !d->interleave && (s0.mode == HM_SRC_F16 || s0.mode == HM_SRC_RMS) &&
+                s0.row_mul == 1 && s0.ldx == d->K && p.nsplit == 1 && p.kspan == d->K &&
+                (reinterpret_cast<uintptr_t>(blk) & 15u) == 0;
+  }
   p.ntiles = ntiles_of(d->N, d->epi);
   if (p.nsplit > 1) {
     if (!d->ws || !d->counters || d->n_counters < p.ntiles ||
