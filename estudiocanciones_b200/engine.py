@@ -652,9 +652,12 @@ class _Runtime:
         self.noise_stream = torch.cuda.Stream(device=dev)
         self.draw_noise = True
         self.pdl = True
-        # HM_PERSISTENT=1: one cooperative launch (stage sequence) per run of fused steps
-        # instead of separate launches; off by default until it is the faster path
-        self.persistent = os.environ.get("HM_PERSISTENT", "0") != "0"
+        # HM_PERSISTENT: "1" = one cooperative launch (stage sequence) per run of fused
+        # steps everywhere, "dec" = only for the decoder passes and heads, "0" = separate
+        # launches (default until the sequences are the faster path)
+        mode = os.environ.get("HM_PERSISTENT", "0")
+        self.persistent = mode not in ("0", "")
+        self.persistent_backbone = mode not in ("0", "", "dec")
         self.force = torch.zeros(B, m.n_cb, dtype=torch.long, device=dev)
         self.rec = torch.zeros(m.n_cb, B, m.vocab, dtype=torch.float16, device=dev)
         self.ctx.reserve(m, B, self.nsplit)
@@ -713,7 +716,7 @@ class _Runtime:
         m = self.m
         B, N = self.B, self.N
         V = m.vocab
-        plan = FramePlan(self.ctx, pdl=self.pdl, persistent=self.persistent)
+        plan = FramePlan(self.ctx, pdl=self.pdl, persistent=self.persistent and self.persistent_backbone)
         join = self._noise_ops(plan)
         if teacher:
             # teacher forcing: record every head's logits and take the forced ids
@@ -736,6 +739,7 @@ class _Runtime:
         last_h = plan.src_f16(bb.x) if normed_input else plan.src_rms(bb.x, bb.ss, m.backbone.norm)
         plan._gemv(m.c0_head, B, last_h, y=self.logits)
         plan.torch_op(join)
+        plan.persistent = self.persistent  # decoder passes
         sample(0, self.noise[0])
         # decoder pass 0: rows (2b, 2b+1) = (last_h[b], emb(0, c0[b])) at positions (0, 1)
         last_h = plan.src_f16(bb.x) if normed_input else plan.src_rms(bb.x, bb.ss, m.backbone.norm)
