@@ -383,8 +383,12 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
     prefetch_tensormap(&vmap);
   }
   pdl_trigger();
-  pdl_wait();
 
+  // Positions come from a buffer no launch of the frame writes (the frame commit, a
+  // graph replay earlier, advances them), and cache slots before pos[r] were written by
+  // earlier steps: the first K/V tiles that end before pos[r] are fetched before
+  // griddepcontrol.wait, overlapping the tail of the producing qkv launch.  The tile
+  // holding pos[r] (written by that launch) is fetched after the wait.
   const int64_t p_last = P.pos[r];
   const int b = r / S;
   int len = static_cast<int>(p_last) + 1;
@@ -408,8 +412,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
     tma_load_2d_plain(sm.v[st][0], &vmap, 0, y, &sm.bar[st]);
     tma_load_2d_plain(sm.v[st][1], &vmap, 64, y, &sm.bar[st]);
   };
+  const int n_first = min(kTcNst, ntile);
+  int n_early = 0;  // leading tiles that end before pos[r]
+  while (n_early < n_first && lo + (n_early + 1) * kTcPos <= static_cast<int>(p_last)) ++n_early;
   if (tid == 0)
-    for (int tt = 0; tt < kTcNst && tt < ntile; ++tt) issue(tt);
+    for (int tt = 0; tt < n_early; ++tt) issue(tt);
+  pdl_wait();
+  if (tid == 0) {
+    fence_proxy_async_global();  // the qkv launch's cache writes, before the TMA reads them
+    for (int tt = n_early; tt < n_first; ++tt) issue(tt);
+  }
 
   // q of this lane's head (row g of the MMA tile), as A fragments for 8 k-steps
   uint32_t qa[8][2];

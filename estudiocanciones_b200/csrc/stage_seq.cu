@@ -136,7 +136,6 @@ HM_DEV uint32_t ld_acquire_u32(const unsigned* p) {
 HM_DEV void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-HM_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t swz(const uint8_t* box, int row, int chunk) {
   return smem_u32(box + row * 128 + ((chunk ^ (row & 7)) << 4));

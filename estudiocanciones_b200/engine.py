@@ -731,13 +731,20 @@ class _Runtime:
             def sample(c, noise):
                 plan.sample(self.logits, N, cfg, topk, temp, noise, self.tok_out, c)
         bb, dec = self.bb, self.dec
+        # The first launch of a frame waits for everything before it (no programmatic
+        # dependent launch): launches of the frame may read the positions and older cache
+        # slots before their own griddepcontrol.wait, so the previous frame's commit must
+        # be complete before any of them starts.
+        plan.pdl = 0
         if with_backbone:
             plan.emb_sum(m.audio_emb, self.tok_in, B, m.n_cb, V, bb.x, bb.ss)
+            plan.pdl = int(self.pdl)
             plan.stack(m.backbone, bb, self.pos, 1, B, self.nsplit)
         # last_h = rms(x_bb, backbone.norm), fused into the consumers' prologue; an
         # already-normalised last_h (the _frame_fast entry point) is read as is
         last_h = plan.src_f16(bb.x) if normed_input else plan.src_rms(bb.x, bb.ss, m.backbone.norm)
         plan._gemv(m.c0_head, B, last_h, y=self.logits)
+        plan.pdl = int(self.pdl)
         plan.torch_op(join)
         plan.persistent = self.persistent  # decoder passes
         sample(0, self.noise[0])

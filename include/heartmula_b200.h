@@ -151,7 +151,10 @@ int hm_frame_commit(const int64_t* tok_out, int64_t* tok_in, int B, int ncb, int
  * _attn + _attn_combine (app/kernels.py:112-167): row r of batch r/S attends
  * cache positions [0, pos[r]] with GQA (no KV copy); split over `nsplit`
  * position ranges, the last CTA of each (row, kv head) merges the partials.
- * q, o fp16 [R, Hq*hd]; kc, vc fp16 [B, Hk, L, hd]; hd in {64, 128, 256, 384}. */
+ * q, o fp16 [R, Hq*hd]; kc, vc fp16 [B, Hk, L, hd]; hd in {64, 128, 256, 384}.
+ * With pdl = 1 the launch reads `pos` and the cache slots before pos[r] before it
+ * waits for the preceding launch (to overlap that launch's tail): the preceding
+ * launch may write q and the slot at pos[r] (the fused qkv GEMV does), not those. */
 int hm_decode_attn(const void* q, const void* kc, const void* vc, const int64_t* pos, void* o, int R, int S, int Hq,
                    int Hk, int hd, int L, float scale, int nsplit, void* ws, size_t ws_bytes, int* counters,
                    int n_counters, int* err, int pdl, hm_stream_t stream);

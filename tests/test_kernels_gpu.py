@@ -70,7 +70,8 @@ def test_gemv_golden(golden, i):
 @pytest.mark.parametrize("M,N,K,kspan,res", [
     (1, 64, 128, 0, False), (3, 200, 512, 0, True), (8, 5120, 3072, 0, False), (8, 3072, 8192, 1024, True),
     (9, 1536, 1024, 512, False), (16, 8197, 3072, 0, False), (20, 1024, 3072, 512, True), (32, 3072, 1024, 0, True),
-    (8, 8197, 1024, 0, False), (1, 16384, 3072, 1024, False), (32, 1024, 8192, 0, True), (5, 2048, 8192, 0, False)])
+    (8, 8197, 1024, 0, False), (1, 16384, 3072, 1024, False), (32, 1024, 8192, 0, True), (5, 2048, 8192, 0, False),
+    (8, 3072, 8192, 0, True), (8, 1024, 8192, 0, True), (8, 1024, 3072, 0, False), (7, 5120, 3072, 0, True)])
 def test_gemv_matches_oracle(M, N, K, kspan, res):
     from estudiocanciones_b200 import kernels
     gen = torch.Generator().manual_seed(M * 7 + N + K)
