@@ -50,6 +50,7 @@ SIGNATURES = {
     "hm_gemv_counters": (_I, [_I, _I]),
     "hm_gemv_pick_kspan": (_I, [_I, _I, _I, _I, _I]),
     "hm_rmsnorm": (_I, [_P, _P, _P, _I, _I, _F, _P]),
+    "hm_rms_apply": (_I, [_P, _I64, _P, _I, _I64, _P, _F, _I, _P, _I64, _I, _I, _I, _P]),
     "hm_rope_kv_write": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "hm_silu_mul": (_I, [_P, _P, _I, _I, _P]),
     "hm_emb_gather_i8": (_I, [_P, _I, _P, _P, _I64, _I, _P, _P, _P]),

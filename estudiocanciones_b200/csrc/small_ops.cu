@@ -35,6 +35,68 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__
     y[(int64_t)r * D + k] = hmul_rn(__float2half_rn(__half2float(xr[k]) * inv), w[k]);
 }
 
+// ------------------------------------------------------------------ RMSNorm from sum-of-squares partials
+// out[r, k] = fp16(fp16(x[r, k] * inv_r) * gamma[k]) with inv_r = 1/sqrt(sum_t ss[t, r] / dim + eps),
+// the partials written by the producer of x (16 columns each).  Every CTA reduces the
+// partials of all rows (a few KB, 16-byte loads) in the same order as the GEMV's fused
+// RMSNorm prologue, then normalises its 1024-column slice: the same values, computed once
+// per launch instead of once per GEMV CTA.
+__global__ void __launch_bounds__(128) rms_apply_kernel(const __half* __restrict__ x, int64_t ldx,
+                                                        const float* __restrict__ ss, int ss_tiles, int64_t ss_ld,
+                                                        const __half* __restrict__ gamma, float eps, int dim,
+                                                        __half* __restrict__ out, int64_t ldo, int R, int D) {
+  constexpr int kMaxR = 32;
+  __shared__ float part[4][kMaxR];
+  __shared__ float inv_s[kMaxR];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nv = (R + 3) / 4;
+  float a[kMaxR];
+#pragma unroll
+  for (int i = 0; i < kMaxR; ++i) a[i] = 0.f;
+  for (int t = tid; t < ss_tiles; t += 128) {
+    const float4* p4 = reinterpret_cast<const float4*>(ss + (int64_t)t * ss_ld);
+#pragma unroll
+    for (int j = 0; j < kMaxR / 4; ++j) {
+      if (j < nv) {
+        const float4 v = p4[j];
+        a[4 * j] += v.x;
+        a[4 * j + 1] += v.y;
+        a[4 * j + 2] += v.z;
+        a[4 * j + 3] += v.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxR; ++i)
+    if (i < 4 * nv) a[i] = warp_sum(a[i]);
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < kMaxR; ++i)
+      if (i < R) part[warp][i] = a[i];
+  }
+  __syncthreads();
+  if (tid < R) {
+    const float tot = ((part[0][tid] + part[1][tid]) + part[2][tid]) + part[3][tid];
+    inv_s[tid] = 1.0f / sqrtf(tot / static_cast<float>(dim) + eps);
+  }
+  __syncthreads();
+  const int c = blockIdx.x * 128 + tid;  // 8-column chunk
+  if (8 * c >= D) return;
+  const uint4 gv = reinterpret_cast<const uint4*>(gamma)[c];
+  for (int r = 0; r < R; ++r) {
+    const uint4 v = *reinterpret_cast<const uint4*>(x + (int64_t)r * ldx + 8 * c);
+    const float inv = inv_s[r];
+    uint4 o;
+    o.x = rms_h2(v.x, gv.x, inv);
+    o.y = rms_h2(v.y, gv.y, inv);
+    o.z = rms_h2(v.z, gv.z, inv);
+    o.w = rms_h2(v.w, gv.w, inv);
+    *reinterpret_cast<uint4*>(out + (int64_t)r * ldo + 8 * c) = o;
+  }
+}
+
 // ------------------------------------------------------------------ RoPE + KV-cache write
 __global__ void rope_kv_kernel(const __half* __restrict__ qkv, const float* __restrict__ rope, int rope_rows,
                                const int64_t* __restrict__ pos, __half* __restrict__ q_out, __half* __restrict__ kc,
@@ -155,6 +217,21 @@ extern "C" int hm_rmsnorm(const void* x, const void* w, void* y, int R, int D, f
   rmsnorm_kernel<<<R, 256, 0, stream>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(w),
                                         reinterpret_cast<__half*>(y), D, eps);
   const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+extern "C" int hm_rms_apply(const void* x, int64_t ldx, const float* ss, int ss_tiles, int64_t ss_ld,
+                            const void* gamma, float eps, int dim, void* out, int64_t ldo, int R, int D, int pdl,
+                            hm_stream_t stream) {
+  if (!x || !ss || !gamma || !out || R < 1 || R > 32 || D < 8 || D % 8 || ss_tiles < 1 || dim < 1) return HM_EARG;
+  if ((ss_ld & 3) || ldx % 8 || ldo % 8 ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(gamma) |
+        reinterpret_cast<uintptr_t>(ss)) & 15u))
+    return HM_EARG;
+  const cudaError_t e =
+      hm_launch(rms_apply_kernel, dim3((D / 8 + 127) / 128), dim3(128), 0, stream, pdl,
+                reinterpret_cast<const __half*>(x), ldx, ss, ss_tiles, ss_ld, reinterpret_cast<const __half*>(gamma),
+                eps, dim, reinterpret_cast<__half*>(out), ldo, R, D);
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }
 

@@ -214,6 +214,7 @@ class StackBuffers:
         self.q = torch.empty(rows, b0.h * b0.hd, device=dev, dtype=torch.float16)
         self.o = torch.empty_like(self.q)
         self.mm = torch.empty(rows, b0.ffn, device=dev, dtype=torch.float16)
+        self.xn = torch.empty(rows, D, device=dev, dtype=torch.float16)  # RMSNorm of x (split mode)
 
 
 class FramePlan:
@@ -235,6 +236,7 @@ class FramePlan:
         self._segs = []
         self.n_kernels = 0
         self.n_stages = 0
+        self.rms_split = os.environ.get("HM_RMS_SPLIT", "0") != "0" and not self.persistent
 
     def __del__(self):
         try:
@@ -353,6 +355,25 @@ class FramePlan:
             ss[:, :R].copy_(part.t())
         self.ops.append(op)
 
+    def rms_apply(self, x, ss, gamma, out, R):
+        """RMSNorm of x's first R rows from the ss partials into ``out`` (one small launch)."""
+        L = _lib.lib()
+        args = (x.data_ptr(), x.stride(0), ss.data_ptr(), ss.shape[0], ss.stride(0), gamma.data_ptr(), EPS,
+                x.shape[1], out.data_ptr(), out.stride(0), R, x.shape[1], self.pdl)
+        self._flush()
+        fn = L.hm_rms_apply
+        self.ops.append(lambda st: check(fn(*args, st), "hm_rms_apply"))
+        self.n_kernels += 1
+
+    def _rms_src(self, bufs, gamma, R):
+        """Input rows RMSNorm(x) for a GEMV: inside every GEMV CTA (fused prologue, the
+        default: measured faster) or once by ``hm_rms_apply`` into ``bufs.xn``
+        (HM_RMS_SPLIT=1; an extra launch per normalisation)."""
+        if self.rms_split and bufs.ss.stride(0) % 4 == 0 and R <= 32:
+            self.rms_apply(bufs.x, bufs.ss, gamma, bufs.xn, R)
+            return self.src_f16(bufs.xn)
+        return self.src_rms(bufs.x, bufs.ss, gamma)
+
     def attn(self, blk: Block, q, o, pos, S, R, nsplit):
         L = _lib.lib()
         wsb = L.hm_decode_attn_workspace_bytes(R, blk.h, blk.hd, nsplit)
@@ -373,11 +394,11 @@ class FramePlan:
         Expects ``bufs.x`` and its ss partials in ``bufs.ss``; leaves the (un-normalised)
         output in ``bufs.x`` with fresh ss partials."""
         for b in stack.blocks:
-            self._gemv(b.qkv, R, self.src_rms(bufs.x, bufs.ss, b.n1), epi=HM_EPI_ROPE_KV, rope=stack.rope,
+            self._gemv(b.qkv, R, self._rms_src(bufs, b.n1, R), epi=HM_EPI_ROPE_KV, rope=stack.rope,
                        pos=pos, S=S, blk=b, q_out=bufs.q, keep=keep)
             self.attn(b, bufs.q, bufs.o, pos, S, R, nsplit)
             self._gemv(b.o, R, self.src_f16(bufs.o), y=bufs.x, res=bufs.x, ss_out=bufs.ss, keep=keep)
-            self._gemv(b.w13, R, self.src_rms(bufs.x, bufs.ss, b.n2), epi=HM_EPI_SILU, y=bufs.mm, keep=keep)
+            self._gemv(b.w13, R, self._rms_src(bufs, b.n2, R), epi=HM_EPI_SILU, y=bufs.mm, keep=keep)
             self._gemv(b.w2, R, self.src_f16(bufs.mm), y=bufs.x, res=bufs.x, ss_out=bufs.ss, keep=keep)
 
     def emb_sum(self, emb: Emb, tok, R, ncb, vocab, x, ss):

@@ -123,6 +123,13 @@ int hm_gemv_pick_kspan(int M, int N, int K, int epi, int kspan);
 /* rms(x, w, eps) (app/kernels.py:58-74). x, y fp16 [R, D]; w fp16 [D]. */
 int hm_rmsnorm(const void* x, const void* w, void* y, int R, int D, float eps, hm_stream_t stream);
 
+/* RMSNorm from the sum-of-squares partials a residual producer wrote (ss[t*ss_ld + r],
+ * 16 columns each): out = fp16(fp16(x * 1/sqrt(sum/dim + eps)) * gamma), R <= 32 rows,
+ * D % 8 == 0, 16-byte aligned.  Same values as the GEMV's fused RMSNorm prologue
+ * (app/kernels.py:58-67 rounding), computed once per launch. */
+int hm_rms_apply(const void* x, int64_t ldx, const float* ss, int ss_tiles, int64_t ss_ld, const void* gamma,
+                 float eps, int dim, void* out, int64_t ldo, int R, int D, int pdl, hm_stream_t stream);
+
 /* _rope_cache (app/kernels.py:79-107): qkv [R, (Hq+2Hk)*hd] -> q_out [R, Hq*hd],
  * kc/vc [B, Hk, L, hd] written at pos[r] for batch r / S. */
 int hm_rope_kv_write(const void* qkv, const float* rope, int rope_rows, const int64_t* pos, void* q_out, void* kc,

@@ -347,3 +347,44 @@ def test_sampler_matches_oracle(seed):
     kernels.sample(logits.to(DEV), N, cfg, topk, temp, noise.to(DEV), out, 0)
     ref = O.guided_sample(logits, N, cfg, topk, temp, noise)
     assert torch.equal(out[:, :1].cpu(), ref)
+
+
+def test_rms_apply_equals_fused_rms_prologue():
+    """hm_rms_apply (RMSNorm from the producer's sum-of-squares partials, one launch)
+    gives exactly the rows the GEMV's fused RMSNorm prologue feeds its MMAs: a GEMV on
+    its output equals the GEMV with the fused prologue bit for bit."""
+    import ctypes as C
+    from estudiocanciones_b200 import _lib, kernels
+    from estudiocanciones_b200._lib import GemvDesc, RowSrc, HM_SRC_F16, HM_SRC_RMS
+    gen = torch.Generator().manual_seed(21)
+    R, D, N = 8, 3072, 1024
+    x = torch.randn(R, D, generator=gen).half().to(DEV)
+    gamma = (1 + 0.1 * torch.randn(D, generator=gen)).half().to(DEV)
+    ss = (x.float() ** 2).reshape(R, D // 16, 16).sum(-1).t().contiguous()
+    w, s = rand_lin(N, D, gen)
+    w, s = w.to(DEV), s.to(DEV)
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    err = kernels.error_word(DEV)
+    xn = torch.empty_like(x)
+    assert L.hm_rms_apply(x.data_ptr(), D, ss.data_ptr(), D // 16, R, gamma.data_ptr(), 1e-5, D, xn.data_ptr(), D,
+                          R, D, 0, st) == 0
+    ref = O.rmsnorm(x.cpu(), gamma.cpu())
+    close16(xn, ref, ulps=1, frac_exact=0.99)
+
+    def run(src):
+        d = GemvDesc()
+        d.w, d.s, d.N, d.K, d.M = w.data_ptr(), s.data_ptr(), N, D, R
+        d.src[0] = src
+        y = torch.empty(R, N, dtype=torch.float16, device=DEV)
+        d.y, d.ldy, d.err = y.data_ptr(), N, err.data_ptr()
+        assert L.hm_gemv_i8_fused(C.byref(d), st) == 0
+        return y
+    s_rms = RowSrc()
+    s_rms.mode, s_rms.row_mul, s_rms.x, s_rms.ldx = HM_SRC_RMS, 1, x.data_ptr(), D
+    s_rms.ss, s_rms.ss_tiles, s_rms.ss_ld, s_rms.gamma, s_rms.eps, s_rms.dim = ss.data_ptr(), D // 16, R, \
+        gamma.data_ptr(), 1e-5, D
+    s_f16 = RowSrc()
+    s_f16.mode, s_f16.row_mul, s_f16.x, s_f16.ldx = HM_SRC_F16, 1, xn.data_ptr(), D
+    torch.testing.assert_close(run(s_rms), run(s_f16), rtol=0, atol=0)
+    assert kernels.read_errors(DEV) == 0
