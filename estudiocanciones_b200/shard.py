@@ -44,10 +44,12 @@ def gather_streams(streams: list[torch.Tensor], n_takes: int, world: int, rank: 
     blocks (fixed shapes on every rank, as NCCL needs).  Returns the ``n_takes``
     streams in global order on rank 0 (on every rank with ``to_all``), else None.
     """
-    dist = _dist()
     mine = partition(n_takes, world, rank)
     if len(streams) != len(mine):
         raise ValueError(f"rank {rank} owns {len(mine)} takes but passed {len(streams)} streams")
+    if world == 1:  # one process: nothing to exchange, no process group needed
+        return list(streams)
+    dist = _dist()
     device = device or (streams[0].device if streams else torch.device("cpu"))
     n_cb = streams[0].shape[0] if streams else 0
     # sizes: (n_cb, T_max) of every rank

@@ -78,3 +78,13 @@ def test_gather_streams_two_gloo_ranks(n_takes, to_all):
         errs.append(errq.get())
     assert not errs, errs
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def test_gather_streams_single_process_needs_no_process_group():
+    import torch.distributed as dist
+    assert not dist.is_initialized()
+    streams = [_stream(t) for t in range(3)]
+    out = gather_streams(streams, 3, 1, 0)
+    assert len(out) == 3 and all(torch.equal(a, b) for a, b in zip(out, streams))
+    with pytest.raises(ValueError):
+        gather_streams(streams[:2], 3, 1, 0)
