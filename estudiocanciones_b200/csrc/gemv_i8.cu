@@ -177,42 +177,35 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 
   // ================================================================ consumer warps
   pdl_trigger();
-  pdl_wait();  // activations, tokens and sums of squares come from earlier launches
 
+  // Before griddepcontrol.wait: everything that depends only on the launch parameters
+  // and immutable data (row pointers of fp16 / RMS rows, the gamma copies, zeros for
+  // padding rows and tails), so the dependent part starts with the activation copy.
+  //
   // Parameter fields are copied to registers / shared memory once: the inline-asm
   // copies and barriers below clobber memory, which would otherwise force a reload
   // of every field through the parameter block on each loop iteration.
   const int K = d.K, N = d.N;
   int* const err = d.err;
 
-  // ---- per-row sources resolved once: row pointer, mode, source index, embedding scale
+  // ---- per-row sources: mode and source index; row pointers of fp16 / RMS rows
+  // (embedding rows need their token ids, which earlier launches write)
   if (tid < MROWS) {
     const int m = tid;
     int mode = -1;  // -1: padding row or rejected id -> zeros
     int sel = 0;
     const uint8_t* base = nullptr;
-    float esc = 0.f;
     if (m < M) {
       int row;
       const hm_row_src& s = src_of(d, m, row, sel);
       mode = s.mode;
-      if (mode == HM_SRC_EMB) {
-        const int64_t id = s.tok[(int64_t)row * s.tok_ld + s.tok_col] + s.tok_off;
-        if (id < 0 || id >= s.erows) {
-          report_error(err, HM_ERR_BADINDEX);
-          mode = -1;
-        } else {
-          base = reinterpret_cast<const uint8_t*>(s.etab + id * (int64_t)K);
-          esc = __half2float(reinterpret_cast<const __half*>(s.escale)[id]);
-        }
-      } else {
+      if (mode != HM_SRC_EMB)
         base = reinterpret_cast<const uint8_t*>(reinterpret_cast<const __half*>(s.x) + (int64_t)row * s.ldx);
-      }
     }
     rmode_s[m] = mode;
     rsel_s[m] = sel;
     rowp_s[m] = base;
-    esc_s[m] = esc;
+    esc_s[m] = 0.f;
   }
   const __half* gam0 = reinterpret_cast<const __half*>(d.src[0].gamma);
   const __half* gam1 = reinterpret_cast<const __half*>(d.src[1].gamma);
@@ -225,11 +218,28 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   // half of each 16-byte chunk), zeros for padding rows, rejected ids and the tail
   const int cpr = kspan / 8;
   const int kend = min(kspan, K - k0);  // valid columns of this k-range (a multiple of 8)
-  if (tid == 0) {
+  bool any_emb = false;
+  for (int m = 0; m < M; ++m) any_emb |= rmode_s[m] == HM_SRC_EMB;
+  if (tid == 0) {  // expected bytes of the whole staging; the gammas are weights: issued now
     uint32_t bytes = 0;
     for (int m = 0; m < M; ++m) bytes += (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS) ? kend * 2 : 0;
     bytes += (g0 ? kend * 2 : 0) + (g1 ? kend * 2 : 0);
     mbar_arrive_expect_tx(xbar, bytes);
+    if (g0) bulk_load(gam_s, gam0 + k0, kend * 2, xbar);
+    if (g1) bulk_load(gam_s + kspan, gam1 + k0, kend * 2, xbar);
+  }
+  // (row-uniform branches: fp16/RMS/embedding rows only need their tail zeroed, usually none)
+  const int ctail = kend / 8;  // first chunk past the valid columns
+  for (int m = 0; m < MROWS; ++m) {
+    const int mode = m < M ? rmode_s[m] : -1;
+    uint8_t* xr = xsm + m * L.xp;
+    for (int c = (mode < 0 ? 0 : ctail) + tid; c < cpr; c += kCons)
+      *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
+  }
+
+  pdl_wait();  // activations, tokens and sums of squares come from earlier launches
+
+  if (tid == 0) {
     if (P.xcontig) {  // all M rows in one request (the issue cost is per request)
       bulk_load(xsm, rowp_s[0], static_cast<uint32_t>(M) * kend * 2, xbar);
     } else {
@@ -237,20 +247,33 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
         if (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS)
           bulk_load(xsm + m * L.xp, rowp_s[m] + 2 * k0, kend * 2, xbar);
     }
-    if (g0) bulk_load(gam_s, gam0 + k0, kend * 2, xbar);
-    if (g1) bulk_load(gam_s + kspan, gam1 + k0, kend * 2, xbar);
   }
-  // (row-uniform branches: fp16/RMS rows only need their tail past K zeroed, usually none)
-  const int ctail = kend / 8;  // first chunk past the valid columns
-  for (int m = 0; m < MROWS; ++m) {
-    const int mode = m < M ? rmode_s[m] : -1;
-    uint8_t* xr = xsm + m * L.xp;
-    if (mode == HM_SRC_EMB) {
-      const uint8_t* base = rowp_s[m] + k0;
-      for (int c = tid; c < ctail; c += kCons) cp_async8(xr + c * 16, base + 8 * c);
+  if (any_emb) {
+    // ---- embedding rows: token id -> table row and scale (rejected ids -> zero row)
+    if (tid < M && rmode_s[tid] == HM_SRC_EMB) {
+      const int m = tid;
+      int row, sel;
+      const hm_row_src& s = src_of(d, m, row, sel);
+      const int64_t id = s.tok[(int64_t)row * s.tok_ld + s.tok_col] + s.tok_off;
+      if (id < 0 || id >= s.erows) {
+        report_error(err, HM_ERR_BADINDEX);
+        rmode_s[m] = -1;
+      } else {
+        rowp_s[m] = reinterpret_cast<const uint8_t*>(s.etab + id * (int64_t)K);
+        esc_s[m] = __half2float(reinterpret_cast<const __half*>(s.escale)[id]);
+      }
     }
-    for (int c = (mode < 0 ? 0 : ctail) + tid; c < cpr; c += kCons)
-      *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
+    named_bar(kBarCons, kCons);
+    for (int m = 0; m < M; ++m) {
+      const int mode = rmode_s[m];
+      uint8_t* xr = xsm + m * L.xp;
+      if (mode == HM_SRC_EMB) {
+        const uint8_t* base = rowp_s[m] + k0;
+        for (int c = tid; c < ctail; c += kCons) cp_async8(xr + c * 16, base + 8 * c);
+      } else if (mode < 0) {
+        for (int c = tid; c < ctail; c += kCons) *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
   }
   // ---- RMSNorm 1/rms of RMS rows from the producers' ss partials, while the copies fly.
   // Every CTA reads the same few KB of partials, so the read pattern matters: with one
@@ -311,11 +334,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   // ---- in-place transforms.  RMSNorm, fp16(fp16(x * inv) * gamma): chunk-outer with the
   // 8 rows of a group loaded together, so each thread has 8 independent load / math /
   // store chains in flight (a row-outer loop is latency-bound at 4 warps per CTA).
-  bool any_rms = false, any_emb = false;
-  for (int m = 0; m < M; ++m) {
-    any_rms |= rmode_s[m] == HM_SRC_RMS;
-    any_emb |= rmode_s[m] == HM_SRC_EMB;
-  }
+  bool any_rms = false;
+  for (int m = 0; m < M; ++m) any_rms |= rmode_s[m] == HM_SRC_RMS;
   if (any_rms) {
     // per-row parameters in registers (the stores below go through a byte pointer,
     // which would otherwise force every shared-memory scalar to be re-read)
