@@ -237,6 +237,44 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
   }
 
+  // epilogue parameters, in registers for the whole tile loop (read before the wait:
+  // the first touch of a parameter field misses the constant cache)
+  const __half* const scales = reinterpret_cast<const __half*>(d.s);
+  __half* const yout = reinterpret_cast<__half*>(d.y);
+  const int64_t ldy = d.ldy, ldres = d.ldres, ss_ld = d.ss_out_ld;
+  const __half* const resid = reinterpret_cast<const __half*>(d.res);
+  float* const ss_out = d.ss_out;
+  float* const wsp = reinterpret_cast<float*>(d.ws);
+  int* const counters = d.counters;
+  struct RopeP {
+    int hd, qw, kw, S, L, Hk, rope_rows;
+    const int64_t* pos;
+    const float* rope;
+    __half *qo, *kc, *vc;
+  } rp{};
+  if (EPI == HM_EPI_ROPE_KV) {
+    rp.hd = d.hd;
+    rp.qw = d.Hq * d.hd;
+    rp.kw = d.Hk * d.hd;
+    rp.S = d.S;
+    rp.L = d.L;
+    rp.Hk = d.Hk;
+    rp.rope_rows = d.rope_rows;
+    rp.pos = d.pos;
+    rp.rope = d.rope;
+    rp.qo = reinterpret_cast<__half*>(d.q_out);
+    rp.kc = reinterpret_cast<__half*>(d.kc);
+    rp.vc = reinterpret_cast<__half*>(d.vc);
+  }
+
+  // per-row weight scales of this thread's epilogue rows (immutable): the first tile's
+  // now, each next tile's while the current one streams
+  const int er = tid & 15, em0 = tid >> 4;
+  const int half_n = RT == 2 ? N / 2 : 0;
+  int nn = (int)blockIdx.x * kTileRows + er;  // row of the next tile's scale
+  float sc0n = my_tiles > 0 && nn < N ? __half2float(scales[nn]) : 0.f;
+  float sc1n = RT == 2 && my_tiles > 0 && half_n + nn < N ? __half2float(scales[half_n + nn]) : 0.f;
+
   pdl_wait();  // activations, tokens and sums of squares come from earlier launches
 
   if (tid == 0) {
@@ -394,49 +432,21 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   }
   named_bar(kBarCons, kCons);
 
-  // epilogue parameters, in registers for the whole tile loop
-  const __half* const scales = reinterpret_cast<const __half*>(d.s);
-  __half* const yout = reinterpret_cast<__half*>(d.y);
-  const int64_t ldy = d.ldy, ldres = d.ldres, ss_ld = d.ss_out_ld;
-  const __half* const resid = reinterpret_cast<const __half*>(d.res);
-  float* const ss_out = d.ss_out;
-  float* const wsp = reinterpret_cast<float*>(d.ws);
-  int* const counters = d.counters;
-  struct RopeP {
-    int hd, qw, kw, S, L, Hk, rope_rows;
-    const int64_t* pos;
-    const float* rope;
-    __half *qo, *kc, *vc;
-  } rp{};
-  if (EPI == HM_EPI_ROPE_KV) {
-    rp.hd = d.hd;
-    rp.qw = d.Hq * d.hd;
-    rp.kw = d.Hk * d.hd;
-    rp.S = d.S;
-    rp.L = d.L;
-    rp.Hk = d.Hk;
-    rp.rope_rows = d.rope_rows;
-    rp.pos = d.pos;
-    rp.rope = d.rope;
-    rp.qo = reinterpret_cast<__half*>(d.q_out);
-    rp.kc = reinterpret_cast<__half*>(d.kc);
-    rp.vc = reinterpret_cast<__half*>(d.vc);
-  }
-
   // ---- tiles: warp w consumes box w of every stage (row block w % RT, k slice w / RT)
   const int g = lane >> 2, t = lane & 3;
   const int rot = t >> 1;  // lanes t >= 2 read their activation chunks rotated by two
   const int ksub = warp / RT;
-  // epilogue ownership: thread -> (row r of the 16, rows m = m0, m0 + 8, ...)
-  const int er = tid & 15, em0 = tid >> 4;
+  // epilogue ownership: thread -> (row r of the 16 (er), rows m = em0, em0 + 8, ...)
   int it = 0;
   for (int ti = 0; ti < my_tiles; ++ti) {
     const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
-    // scales this thread's epilogue needs (immutable, prefetched while the tile streams)
     const int n0 = tile * kTileRows + er;
-    const int n1 = (RT == 2 ? N / 2 : 0) + tile * kTileRows + er;
-    const float sc0 = n0 < N ? __half2float(scales[n0]) : 0.f;
-    const float sc1 = (RT == 2 && n1 < N) ? __half2float(scales[n1]) : 0.f;
+    const float sc0 = sc0n, sc1 = sc1n;
+    if (ti + 1 < my_tiles) {
+      nn += (int)gridDim.x * kTileRows;
+      sc0n = nn < N ? __half2float(scales[nn]) : 0.f;
+      if (RT == 2) sc1n = half_n + nn < N ? __half2float(scales[half_n + nn]) : 0.f;
+    }
     float acc[MT][4];
 #pragma unroll
     for (int j = 0; j < MT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
