@@ -30,6 +30,7 @@
 //    (atomic ticket) sums them in split order and runs the epilogue.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstddef>
 #include <cstdio>
 #include <cstdlib>
@@ -45,7 +46,8 @@ constexpr int kTileRows = 16;   // rows of one MMA row block
 constexpr int kBox = 128;       // k columns (bytes) per TMA box
 constexpr int kBoxBytes = kTileRows * kBox;
 constexpr int kStage = 4 * kBoxBytes;  // four boxes per stage
-constexpr int kNST = 6;         // ring stages
+constexpr int kNST = 6;         // ring stages at the default depth
+constexpr int kMaxNST = 14;     // deepest ring (the mbarrier arrays are sized for it)
 constexpr int kCons = 128;      // consumer threads (4 MMA warps)
 constexpr int kThreads = kCons + 32;
 constexpr int kMaxM = 32;
@@ -54,8 +56,11 @@ constexpr int kBarCons = 1;     // named barrier of the consumer warps
 
 struct GemvParams {
   hm_gemv_desc d;
-  int kspan, nsplit, ntiles, has_gamma;
+  int kspan, nsplit, ntiles;
+  int has_gamma;  // gamma vectors staged: 0, 1 (src[0]) or 2 (interleaved sources)
   int xcontig;  // the M input rows are one contiguous block: staged by one bulk copy, unpadded pitch
+  int xf_loop;  // every row is RMS(src[0]): CTAs with one tile normalise in registers in the MMA loop
+  int nst;      // ring stages: deeper when the CTAs per SM leave shared memory free
 };
 
 struct SmemLayout {
@@ -67,20 +72,21 @@ __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a *
 __host__ __device__ inline int rt_of(int epi) { return epi == HM_EPI_SILU ? 2 : 1; }
 __host__ __device__ inline int ks_of(int epi) { return 4 * kBox / rt_of(epi); }  // k bytes per stage
 
-__host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_gamma, int xcontig = 0) {
+__host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_gamma, int xcontig = 0,
+                                                  int nst = kNST) {
   SmemLayout L;
   L.ring = 0;
   L.xp = kspan * 2 + (xcontig ? 0 : 16);
-  L.x = kNST * kStage;
+  L.x = nst * kStage;
   L.gam = align_up(L.x + mrows * L.xp, 16);
-  L.red = L.gam + (has_gamma ? 2 * kspan * 2 : 0);
+  L.red = L.gam + has_gamma * kspan * 2;
   L.inv = L.red + 4 * kTileRows * (mrows + 1) * 4;
   L.esc = L.inv + kMaxM * 4;
   L.rowp = align_up(L.esc + kMaxM * 4, 8);
   L.rmode = L.rowp + kMaxM * 8;
   L.flag = L.rmode + 2 * kMaxM * 4;
   L.bars = align_up(L.flag + 16, 8);
-  L.total = L.bars + (2 * kNST + 1) * 8;
+  L.total = L.bars + (2 * kMaxNST + 1) * 8;
   return L;
 }
 
@@ -120,7 +126,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   const int per_tile = kspan / KS;  // stages per tile
   const int my_tiles = (P.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int nstages = my_tiles * per_tile;
-  const SmemLayout L = smem_layout(kspan, MROWS, P.has_gamma, P.xcontig);
+  const int nst = P.nst;
+  const SmemLayout L = smem_layout(kspan, MROWS, P.has_gamma, P.xcontig, nst);
   uint8_t* ring = smem + L.ring;
   uint8_t* xsm = smem + L.x;
   __half* gam_s = reinterpret_cast<__half*>(smem + L.gam);
@@ -133,8 +140,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   int* flag_s = reinterpret_cast<int*>(smem + L.flag);
   volatile int* abort_s = flag_s + 1;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty = full + kNST;
-  uint64_t* xbar = empty + kNST;  // bulk copies of the activation rows and gammas
+  uint64_t* empty = full + kMaxNST;
+  uint64_t* xbar = empty + kMaxNST;  // bulk copies of the activation rows and gammas
 
   if (smem_u32(ring) & 1023u) {  // 128B-swizzled TMA destinations must be 1024-byte aligned
     if (tid == 0) report_error(d.err, HM_ERR_TIMEOUT);
@@ -142,7 +149,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   }
   if (tid == 0) {
     *abort_s = 0;
-    for (int i = 0; i < kNST; ++i) {
+    for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kCons / 32);
     }
@@ -159,9 +166,9 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       const int half_n = d.N / 2;
       prefetch_tensormap(&wmap);
       const uint64_t pol = d.l2_keep ? policy_evict_last() : policy_evict_first();
+      int slot = 0, round = 0;  // it = round * nst + slot
       for (int it = 0; it < nstages; ++it) {
-        const int slot = it % kNST;
-        if (it >= kNST) mbar_wait_ab(&empty[slot], ((it / kNST) - 1) & 1, perr, abort_s);
+        if (round > 0) mbar_wait_ab(&empty[slot], (round - 1) & 1, perr, abort_s);
         const int tile = (int)blockIdx.x + (it / per_tile) * (int)gridDim.x;
         const int kx = k0 + (it % per_tile) * KS;
         mbar_arrive_expect_tx(&full[slot], kStage);
@@ -169,6 +176,10 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
         for (int b = 0; b < 4; ++b)
           tma_load_2d(ring + slot * kStage + b * kBoxBytes, &wmap, kx + (b / RT) * kBox,
                       (RT == 2 && (b % RT) == 1 ? half_n : 0) + tile * kTileRows, &full[slot], pol);
+        if (++slot == nst) {
+          slot = 0;
+          ++round;
+        }
       }
     }
     pdl_wait();
@@ -236,6 +247,13 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     for (int c = (mode < 0 ? 0 : ctail) + tid; c < cpr; c += kCons)
       *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(0, 0, 0, 0);
   }
+  // RMSNorm in the MMA loop (registers) instead of a shared-memory pass: in CTAs with one
+  // tile (the pass and the loop then touch each element once either way, the loop without
+  // a barrier and a store) and one row block per stage (with two, two warps would
+  // normalise the same columns)
+  const bool xf_loop = P.xf_loop && RT == 1 && my_tiles == 1;
+  if (xf_loop)  // gamma past K meets zero activations in the MMA loop: keep it finite
+    for (int c = ctail + tid; c < cpr; c += kCons) reinterpret_cast<uint4*>(gam_s)[c] = make_uint4(0, 0, 0, 0);
 
   // epilogue parameters, in registers for the whole tile loop (read before the wait:
   // the first touch of a parameter field misses the constant cache)
@@ -374,7 +392,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   // store chains in flight (a row-outer loop is latency-bound at 4 warps per CTA).
   bool any_rms = false;
   for (int m = 0; m < M; ++m) any_rms |= rmode_s[m] == HM_SRC_RMS;
-  if (any_rms) {
+  if (any_rms && !xf_loop) {
     // per-row parameters in registers (the stores below go through a byte pointer,
     // which would otherwise force every shared-memory scalar to be re-read)
     float invr[MROWS];
@@ -437,7 +455,12 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   const int rot = t >> 1;  // lanes t >= 2 read their activation chunks rotated by two
   const int ksub = warp / RT;
   // epilogue ownership: thread -> (row r of the 16 (er), rows m = em0, em0 + 8, ...)
-  int it = 0;
+  // in-loop RMSNorm: 1/rms of this lane's activation rows (8j + g); padding rows are zeros
+  float ivr[MT];
+#pragma unroll
+  for (int j = 0; j < MT; ++j) ivr[j] = (xf_loop && 8 * j + g < M) ? inv_s[8 * j + g] : 0.f;
+  const uint4* const gam4 = reinterpret_cast<const uint4*>(gam_s);
+  int slot = 0, round = 0;  // ring position of the next stage
   for (int ti = 0; ti < my_tiles; ++ti) {
     const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
     const int n0 = tile * kTileRows + er;
@@ -450,9 +473,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     float acc[MT][4];
 #pragma unroll
     for (int j = 0; j < MT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    for (int st = 0; st < per_tile; ++st, ++it) {
-      const int slot = it % kNST;
-      mbar_wait_ab(&full[slot], (it / kNST) & 1, err, abort_s);  // on timeout: carry on, error flagged
+    for (int st = 0; st < per_tile; ++st) {
+      mbar_wait_ab(&full[slot], round & 1, err, abort_s);  // on timeout: carry on, error flagged
       const uint8_t* wb = ring + slot * kStage + warp * kBoxBytes;
       const uint4 lo0 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + rot) ^ g) << 4));
       const uint4 lo1 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + 1 - rot) ^ g) << 4));
@@ -460,6 +482,10 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       const uint4 hi1 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t + 1 - rot) ^ g) << 4));
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);  // this warp's box is in registers now
+      if (++slot == nst) {
+        slot = 0;
+        ++round;
+      }
       const uint32_t wa[8] = {lo0.x, lo0.y, lo0.z, lo0.w, lo1.x, lo1.y, lo1.z, lo1.w};
       const uint32_t wc[8] = {hi0.x, hi0.y, hi0.z, hi0.w, hi1.x, hi1.y, hi1.z, hi1.w};
       const int cb = (st * KS + ksub * kBox) / 8;  // first activation chunk of this box
@@ -474,6 +500,19 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
           xw[j][4 * i + 1] = v.y;
           xw[j][4 * i + 2] = v.z;
           xw[j][4 * i + 3] = v.w;
+        }
+      }
+      if (xf_loop) {  // fp16(fp16(x * inv) * gamma), the same rounding as the shared-memory pass
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 gv = gam4[cb + 4 * t + ((i + 2 * rot) & 3)];
+#pragma unroll
+          for (int j = 0; j < MT; ++j) {
+            xw[j][4 * i + 0] = rms_h2(xw[j][4 * i + 0], gv.x, ivr[j]);
+            xw[j][4 * i + 1] = rms_h2(xw[j][4 * i + 1], gv.y, ivr[j]);
+            xw[j][4 * i + 2] = rms_h2(xw[j][4 * i + 2], gv.z, ivr[j]);
+            xw[j][4 * i + 3] = rms_h2(xw[j][4 * i + 3], gv.w, ivr[j]);
+          }
         }
       }
 #pragma unroll
@@ -685,6 +724,20 @@ int sm_count() {
   return n;
 }
 
+int dev_attr(cudaDeviceAttr a, int dflt) {
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  return cudaDeviceGetAttribute(&v, a, dev) == cudaSuccess && v > 0 ? v : dflt;
+}
+int smem_per_sm() {
+  static const int v = dev_attr(cudaDevAttrMaxSharedMemoryPerMultiprocessor, 228 * 1024);
+  return v;
+}
+int smem_reserved_per_cta() {
+  static const int v = dev_attr(cudaDevAttrReservedSharedMemoryPerBlock, 1024);
+  return v;
+}
+
 int ntiles_of(int N, int epi) {
   return epi == HM_EPI_SILU ? (N / 2) / kTileRows : (N + kTileRows - 1) / kTileRows;
 }
@@ -712,8 +765,10 @@ int auto_kspan(int M, int K, int epi) {
 }
 
 template <int MT, int EPI>
-cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p, cudaStream_t st) {
-  const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig).total;
+cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_t st) {
+  GemvParams p = p0;
+  p.nst = kNST;
+  int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig).total;
   static int configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -728,6 +783,15 @@ cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p, cudaStream_t
     occ = 1;
   static const int cap = static_cast<int>(env_or("HM_GEMV_CTAS_PER_SM", 2));
   const int per_sm = occ < cap ? occ : cap;
+  // Deepen the ring into the shared memory those CTAs leave free: the bytes in flight per
+  // SM bound its weight stream (bandwidth = bytes in flight / memory latency), which
+  // matters when a long activation row leaves room for one CTA per SM only.
+  static const int deep = static_cast<int>(env_or("HM_GEMV_DEEP_RING", 1));
+  if (deep) {
+    const int limit = std::min(smem_per_sm() / per_sm - smem_reserved_per_cta(), 227 * 1024);
+    while (p.nst < kMaxNST && smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst + 1).total <= limit) ++p.nst;
+    smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst).total;
+  }
   int J = per_sm * sm_count() / p.nsplit;
   if (J < 1) J = 1;
   if (J > p.ntiles) J = p.ntiles;
@@ -783,7 +847,7 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
       if (!s.x || !aligned16(s.x) || (s.ldx % 8)) return HM_EARG;
       if (s.mode == HM_SRC_RMS) {
         if (!s.ss || !s.gamma || !aligned16(s.gamma) || s.dim <= 0) return HM_EARG;
-        has_gamma = 1;
+        has_gamma = d->interleave ? 2 : 1;
       }
     }
   }
@@ -804,6 +868,8 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
     p.xcontig = contig_on && !d->interleave && (s0.mode == HM_SRC_F16 || s0.mode == HM_SRC_RMS) &&
                 s0.row_mul == 1 && s0.ldx == d->K && p.nsplit == 1 && p.kspan == d->K &&
                 (reinterpret_cast<uintptr_t>(blk) & 15u) == 0;
+    static const int xf_on = static_cast<int>(env_or("HM_GEMV_XFLOOP", 1));
+    p.xf_loop = xf_on && !d->interleave && s0.mode == HM_SRC_RMS;
   }
   p.ntiles = ntiles_of(d->N, d->epi);
   if (p.nsplit > 1) {
