@@ -39,6 +39,7 @@ struct AttnParams {
   float* ws;
   int* counters;
   int* err;
+  int cluster;  // tensor-core kernel: the nsplit CTAs of a (row, KV head) form a cluster and merge in DSMEM
 };
 
 constexpr int kMaxSplit = 64;
@@ -337,13 +338,17 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
 constexpr int kTcPos = 64;   // positions per stage (4 warps x 16)
 constexpr int kTcNst = 3;
 constexpr int kTcBox = kTcPos * 128;  // bytes of one 64x64 fp16 box
+constexpr int kMaxCluster = 8;        // splits merged inside a cluster (portable cluster size)
 
 struct TcSmem {
   uint8_t k[kTcNst][2][kTcBox];  // [stage][dims 0-63 | 64-127][64 positions x 128 B]
   uint8_t v[kTcNst][2][kTcBox];
   float mw[4][kMaxG], lw[4][kMaxG];
   float cw[kMaxG][kMaxSplit], cl[kMaxG][kMaxSplit], cden[kMaxG];
+  float cm[kMaxG], cd[kMaxG];  // this CTA's split maxima and denominators (cluster merge)
+  float fw[4][kMaxG], hm[kMaxG], hd[kMaxG];  // per head: warp weights, maximum, denominator
   uint64_t bar[kTcNst];
+  uint64_t cready, cdone;  // cluster merge: partials of every split in / the leader has read them
   int flag, abort_flag;
 };
 
@@ -368,16 +373,22 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
   int* const counters = P.counters;
   const int G = Hq / Hk;
 
-  if (smem_u32(smem_raw) & 1023u) {
-    if (tid == 0) report_error(err, HM_ERR_TIMEOUT);
-    return;
-  }
+  const bool clus = P.cluster != 0 && nsplit > 1;
   if (tid == 0) {
     sm.abort_flag = 0;
     for (int i = 0; i < kTcNst; ++i) mbar_init(&sm.bar[i], 1);
+    if (clus) {
+      mbar_init(&sm.cready, nsplit - 1);
+      mbar_init(&sm.cdone, 1);
+    }
     fence_barrier_init();
   }
   __syncthreads();
+  if (clus) cluster_sync_all();  // every CTA's merge barriers exist before any remote arrival
+  if (smem_u32(smem_raw) & 1023u) {  // (the same for every CTA: all return)
+    if (tid == 0) report_error(err, HM_ERR_TIMEOUT);
+    return;
+  }
   if (tid == 0) {
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
@@ -505,6 +516,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
 
   // ---- merge the four warps (red aliases the now idle stage-0 K buffers)
   float* red = reinterpret_cast<float*>(&sm.k[0][0][0]);  // [4][kMaxG][128]
+  float* cnum = reinterpret_cast<float*>(&sm.k[1][0][0]);  // [G][128] this split's partial (cluster merge)
   if (g < G) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
@@ -517,6 +529,23 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
     }
   }
   __syncthreads();
+  // per head (once, not per element): the warps' maximum, weights and denominator
+  if (tid < G) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm.mw[w][tid]);
+    float den = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sm.mw[w][tid];
+      const float f = mw > -INFINITY ? expf(mw - M) : 0.f;
+      sm.fw[w][tid] = f;
+      den += sm.lw[w][tid] * f;
+    }
+    sm.hm[tid] = M;
+    sm.hd[tid] = den;
+  }
+  __syncthreads();
   const int64_t head0 = (int64_t)r * Hq + kh * G;
   const int64_t nh = (int64_t)R * Hq * nsplit;
   float* wm = wsg;
@@ -524,19 +553,18 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
   float* wa = wsg + 2 * nh;
   for (int i = tid; i < G * HD; i += kThreads) {
     const int gg = i / HD, d = i - gg * HD;
-    float M = -INFINITY;
+    const float M = sm.hm[gg], den = sm.hd[gg];
+    float num = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm.mw[w][gg]);
-    float num = 0.f, den = 0.f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float mw = sm.mw[w][gg];
-      const float f = mw > -INFINITY ? expf(mw - M) : 0.f;
-      num += red[(w * kMaxG + gg) * HD + d] * f;
-      den += sm.lw[w][gg] * f;
-    }
+    for (int w = 0; w < 4; ++w) num += red[(w * kMaxG + gg) * HD + d] * sm.fw[w][gg];
     if (nsplit == 1) {
       og[(head0 + gg) * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+    } else if (clus) {
+      cnum[gg * HD + d] = num;
+      if (d == 0) {
+        sm.cm[gg] = M;
+        sm.cd[gg] = den;
+      }
     } else {
       wa[((head0 + gg) * nsplit + sp) * HD + d] = num;
       if (d == 0) {
@@ -546,6 +574,65 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
     }
   }
   if (nsplit == 1) return;
+  if (clus) {
+    // ---- split merge inside the cluster: every CTA keeps its partial in its own shared
+    // memory and signals the leader (rank 0), which reads the partials through DSMEM,
+    // merges them in split order (the same arithmetic as the workspace path below) and
+    // releases the others, whose shared memory must live until it has read them.
+    __syncthreads();
+    const uint32_t rank = cluster_ctarank();
+    if (rank != 0) {
+      if (tid == 0) {
+        fence_acq_rel_cluster();
+        mbar_arrive_dsmem(dsmem_addr(&sm.cready, 0));
+        mbar_wait_cluster(&sm.cdone, 0, err);
+      }
+      return;
+    }
+    if (tid == 0) mbar_wait_cluster(&sm.cready, 0, err);
+    __syncthreads();
+    // per head (once): split maxima / denominators -> weights and the merged denominator
+    if (tid < G) {
+      float ms[kMaxCluster], ls[kMaxCluster];
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxCluster; ++s2) {
+        ms[s2] = s2 >= nsplit ? -INFINITY : (s2 == 0 ? sm.cm[tid] : ld_dsmem_f32(dsmem_addr(&sm.cm[tid], s2)));
+        ls[s2] = s2 >= nsplit ? 0.f : (s2 == 0 ? sm.cd[tid] : ld_dsmem_f32(dsmem_addr(&sm.cd[tid], s2)));
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxCluster; ++s2)
+        if (s2 < nsplit) mx = fmaxf(mx, ms[s2]);
+      float den = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxCluster; ++s2) {
+        if (s2 < nsplit) {
+          const float w = ms[s2] > -INFINITY ? expf(ms[s2] - mx) : 0.f;
+          sm.cw[tid][s2] = w;
+          den += ls[s2] * w;
+        }
+      }
+      sm.cden[tid] = den;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += kThreads) {
+      const int gg = i / HD;
+      float ns[kMaxCluster];
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxCluster; ++s2)
+        ns[s2] = s2 >= nsplit ? 0.f : (s2 == 0 ? cnum[i] : ld_dsmem_f32(dsmem_addr(&cnum[i], s2)));
+      float num = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxCluster; ++s2)
+        if (s2 < nsplit) num += ns[s2] * sm.cw[gg][s2];
+      const float den = sm.cden[gg];
+      og[(head0 + gg) * HD + i - gg * HD] = __float2half_rn(den > 0.f ? num / den : 0.f);
+    }
+    __syncthreads();  // every DSMEM read of this CTA has returned
+    if (tid == 0)
+      for (int s2 = 1; s2 < nsplit; ++s2) mbar_arrive_dsmem(dsmem_addr(&sm.cdone, s2));
+    return;
+  }
   __threadfence();
   __syncthreads();
   int* ticket = &counters[r * Hk + kh];
@@ -639,9 +726,38 @@ cudaError_t launch_attn_tc(const AttnParams& p, int B, int pdl, cudaStream_t st)
     cudaError_t e = cudaFuncSetAttribute(decode_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
+    hm_carveout(decode_attn_tc_kernel);
     configured = true;
   }
-  return hm_launch(decode_attn_tc_kernel, dim3(p.nsplit, p.Hk, p.R), dim3(kThreads), smem, st, pdl, km, vm, p);
+  // 2..8 splits: one cluster per (row, KV head), merged in DSMEM (no workspace round trip)
+  static const int clus_on = [] {
+    const char* e = getenv("HM_ATTN_CLUSTER");
+    return e ? atoi(e) : 1;
+  }();
+  AttnParams q = p;
+  q.cluster = clus_on && p.nsplit >= 2 && p.nsplit <= kMaxCluster;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.nsplit, p.Hk, p.R);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (q.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = p.nsplit;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, decode_attn_tc_kernel, km, vm, q);
 }
 
 template <int HD>
@@ -693,6 +809,7 @@ extern "C" int hm_decode_attn(const void* q, const void* kc, const void* vc, con
   p.ws = reinterpret_cast<float*>(ws);
   p.counters = counters;
   p.err = err;
+  p.cluster = 0;
   cudaError_t e;
   switch (hd) {
     case 128: e = attn_tc_enabled() ? launch_attn_tc(p, R / S, pdl, stream) : launch_attn<128>(p, pdl, stream); break;
@@ -777,6 +894,7 @@ extern "C" int hm_decode_attn_noalloc(const void* q, const void* kc, const void*
   p.ws = partials;
   p.counters = tickets;
   p.err = err;
+  p.cluster = 0;
   switch (hd) {
     case 128: e = launch_attn<128>(p, 0, stream); break;
     case 256: e = launch_attn<256>(p, 0, stream); break;

@@ -110,6 +110,56 @@ HM_DEV bool mbar_wait_ab(uint64_t* bar, uint32_t parity, int* err, volatile int*
   return false;
 }
 
+// ---------------------------------------------------------------- thread-block clusters
+HM_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster: arrive (release) and wait (acquire).
+HM_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+HM_DEV uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+HM_DEV float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+HM_DEV void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+// Arrive (release at cluster scope) on an mbarrier of another CTA of the cluster.
+HM_DEV void mbar_arrive_dsmem(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+HM_DEV bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait (acquire at cluster scope) for arrivals from other CTAs of the cluster;
+// records HM_ERR_TIMEOUT and returns false after HM_WAIT_NS.
+HM_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 28); ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > HM_WAIT_NS) break;
+  }
+  report_error(err, HM_ERR_TIMEOUT);
+  return false;
+}
+
 // ---------------------------------------------------------------- TMA
 // 2-D tiled load global -> shared, completion counted on `bar` (bytes).
 // x is the innermost coordinate (elements); callers keep x*elem_size % 16 == 0.

@@ -302,7 +302,12 @@ def test_attn_golden(golden, i):
     (16, 2, 8, 2, 128, 8, [0, 1] * 8, 1),
     (4, 1, 8, 2, 128, 8, [7, 6, 5, 2], 1),
     (4, 1, 8, 4, 384, 40, [3, 39, 0, 20], 3),
-    (2, 1, 24, 8, 128, 4282, [4281, 4023], 16)])
+    (2, 1, 24, 8, 128, 4282, [4281, 4023], 16),
+    # 2..8 splits merge inside a thread-block cluster (DSMEM); rows whose later splits are empty
+    (8, 1, 24, 8, 128, 1350, [0, 1, 63, 64, 200, 975, 1348, 1349], 2),
+    (8, 1, 24, 8, 128, 1350, [0, 5, 64, 130, 700, 975, 1100, 1349], 4),
+    (8, 1, 24, 8, 128, 1350, [0, 2, 65, 127, 512, 974, 1200, 1349], 8),
+    (16, 2, 8, 2, 128, 300, [0, 1] * 4 + [100, 101] * 2 + [298, 299] * 2, 4)])
 def test_attn_matches_oracle(R, S, Hq, Hk, hd, L, pos, ns):
     from estudiocanciones_b200 import kernels
     gen = torch.Generator().manual_seed(R + L + ns)
