@@ -776,22 +776,43 @@ cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_
     if (e != cudaSuccess) return e;
     configured = 227 * 1024;
   }
-  // one wave: CTAs per SM from the occupancy calculator (capped), tiles strided over the grid
-  int occ = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<MT, EPI>, kThreads, smem) != cudaSuccess ||
-      occ < 1)
-    occ = 1;
-  static const int cap = static_cast<int>(env_or("HM_GEMV_CTAS_PER_SM", 2));
-  const int per_sm = occ < cap ? occ : cap;
-  // Deepen the ring into the shared memory those CTAs leave free: the bytes in flight per
-  // SM bound its weight stream (bandwidth = bytes in flight / memory latency), which
-  // matters when a long activation row leaves room for one CTA per SM only.
+  // One wave of CTAs, tiles strided over the grid.  CTAs per SM: enough for one tile per
+  // CTA when the shape has more tiles than SMs and the activations are short enough for
+  // up to four CTAs with a ring of at least four stages; otherwise up to two CTAs (what
+  // the shared memory allows) with the default ring, deepened into the memory they
+  // leave free: the bytes in flight per SM bound its weight stream (bandwidth = bytes
+  // in flight / memory latency), which matters when a long activation row leaves room
+  // for one CTA per SM only.
+  static const int cap = static_cast<int>(env_or("HM_GEMV_CTAS_PER_SM", 4));
   static const int deep = static_cast<int>(env_or("HM_GEMV_DEEP_RING", 1));
-  if (deep) {
-    const int limit = std::min(smem_per_sm() / per_sm - smem_reserved_per_cta(), 227 * 1024);
-    while (p.nst < kMaxNST && smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst + 1).total <= limit) ++p.nst;
-    smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst).total;
+  const int units = p.ntiles * p.nsplit;
+  const int want = std::max(2, (units + sm_count() - 1) / sm_count());
+  auto lay = [&](int n) { return smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, n).total; };
+  int per_sm = 0;
+  for (int ps = std::min(cap, want); ps >= 1 && !per_sm; --ps) {
+    const int limit = std::min(smem_per_sm() / ps - smem_reserved_per_cta(), 227 * 1024);
+    int n = kNST;
+    if (ps > 2) {
+      n = kMaxNST;
+      while (n >= 4 && lay(n) > limit) --n;
+      if (n < 4) continue;
+    } else {
+      if (lay(n) > limit) continue;
+      if (deep)
+        while (n < kMaxNST && lay(n + 1) <= limit) ++n;
+    }
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<MT, EPI>, kThreads, lay(n)) != cudaSuccess ||
+        occ < ps)
+      continue;
+    per_sm = ps;
+    p.nst = n;
   }
+  if (!per_sm) {
+    per_sm = 1;
+    p.nst = kNST;
+  }
+  smem = lay(p.nst);
   int J = per_sm * sm_count() / p.nsplit;
   if (J < 1) J = 1;
   if (J > p.ntiles) J = p.ntiles;

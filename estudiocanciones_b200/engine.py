@@ -774,7 +774,10 @@ class _Runtime:
         plan._gemv(m.projection, 2 * B, last_h, plan.src_emb(m.audio_emb, self.tok_out, 0, 0), y=dec.x,
                    ss_out=dec.ss, keep=True)
         plan.stack(m.decoder, dec, self.dpos0, 2, 2 * B, 1, keep=True)
-        plan._gemv(m.audio_head[0], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm, row_mul=2, row_add=1), keep=True,
+        # the decoder layers and the projection are read 7 times per frame (kept in L2); each
+        # audio head once (streamed, so it does not push the decoder weights out of L2)
+        head_keep = os.environ.get("HM_HEAD_KEEP", "0") != "0"
+        plan._gemv(m.audio_head[0], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm, row_mul=2, row_add=1), keep=head_keep,
                    y=self.logits)
         sample(1, self.noise[1])
         for c in range(2, m.n_cb):
@@ -782,7 +785,7 @@ class _Runtime:
                        y=dec.x, ss_out=dec.ss)
             plan.stack(m.decoder, dec, self.dpos[c], 1, B, 1, keep=True)
             plan._gemv(m.audio_head[c - 1], B, plan.src_rms(dec.x, dec.ss, m.decoder.norm), y=self.logits,
-                       keep=True)
+                       keep=head_keep)
             sample(c, self.noise[c])
         if commit:
             plan.commit(self.tok_out, self.tok_in, self.pos, N, self.stream_out, self.frame)
