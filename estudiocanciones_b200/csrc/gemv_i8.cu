@@ -51,6 +51,7 @@ constexpr int kMaxNST = 14;     // deepest ring (the mbarrier arrays are sized f
 constexpr int kCons = 128;      // consumer threads (4 MMA warps)
 constexpr int kThreads = kCons + 32;
 constexpr int kMaxM = 32;
+constexpr int kMaxCSplit = 8;   // k-ranges of one tile in a cluster (portable cluster size)
 constexpr int kXBudget = 128 * 1024;  // bytes of staged activations per CTA
 constexpr int kBarCons = 1;     // named barrier of the consumer warps
 
@@ -61,10 +62,11 @@ struct GemvParams {
   int xcontig;  // the M input rows are one contiguous block: staged by one bulk copy, unpadded pitch
   int xf_loop;  // every row is RMS(src[0]): CTAs with one tile normalise in registers in the MMA loop
   int nst;      // ring stages: deeper when the CTAs per SM leave shared memory free
+  int cluster;  // the nsplit k-ranges of a tile run as one thread-block cluster and reduce in DSMEM
 };
 
 struct SmemLayout {
-  int ring, x, gam, red, inv, esc, rowp, rmode, flag, bars, total;  // flag: [0] tile owner, [1] abort
+  int ring, x, gam, red, cpart, inv, esc, rowp, rmode, flag, bars, total;  // flag: [0] tile owner, [1] abort
   int xp;  // activation row pitch in bytes
 };
 
@@ -80,13 +82,14 @@ __host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_
   L.x = nst * kStage;
   L.gam = align_up(L.x + mrows * L.xp, 16);
   L.red = L.gam + has_gamma * kspan * 2;
-  L.inv = L.red + 4 * kTileRows * (mrows + 1) * 4;
+  L.cpart = L.red + 4 * kTileRows * (mrows + 1) * 4;  // this k-range's partial tile (cluster split)
+  L.inv = L.cpart + 2 * kTileRows * mrows * 4;
   L.esc = L.inv + kMaxM * 4;
   L.rowp = align_up(L.esc + kMaxM * 4, 8);
   L.rmode = L.rowp + kMaxM * 8;
   L.flag = L.rmode + 2 * kMaxM * 4;
   L.bars = align_up(L.flag + 16, 8);
-  L.total = L.bars + (2 * kMaxNST + 1) * 8;
+  L.total = L.bars + (2 * kMaxNST + 3) * 8;
   return L;
 }
 
@@ -142,6 +145,9 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + kMaxNST;
   uint64_t* xbar = empty + kMaxNST;  // bulk copies of the activation rows and gammas
+  uint64_t* cready = xbar + 1;       // cluster split: the other k-ranges' partials are in (rank 0)
+  uint64_t* cdone = xbar + 2;        // cluster split: rank 0 has read this CTA's partial
+  float* cpart_s = reinterpret_cast<float*>(smem + L.cpart);
 
   if (smem_u32(ring) & 1023u) {  // 128B-swizzled TMA destinations must be 1024-byte aligned
     if (tid == 0) report_error(d.err, HM_ERR_TIMEOUT);
@@ -154,9 +160,14 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       mbar_init(&empty[i], kCons / 32);
     }
     mbar_init(xbar, 1);
+    if (P.cluster) {
+      mbar_init(cready, P.nsplit - 1);
+      mbar_init(cdone, 1);
+    }
     fence_barrier_init();
   }
   __syncthreads();
+  if (P.cluster) cluster_sync_all();  // every CTA's split barriers exist before any remote arrival
 
   // ================================================================ producer warp
   if (warp == kCons / 32) {
@@ -295,14 +306,10 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 
   pdl_wait();  // activations, tokens and sums of squares come from earlier launches
 
-  if (tid == 0) {
-    if (P.xcontig) {  // all M rows in one request (the issue cost is per request)
-      bulk_load(xsm, rowp_s[0], static_cast<uint32_t>(M) * kend * 2, xbar);
-    } else {
-      for (int m = 0; m < M; ++m)
-        if (rmode_s[m] == HM_SRC_F16 || rmode_s[m] == HM_SRC_RMS)
-          bulk_load(xsm + m * L.xp, rowp_s[m] + 2 * k0, kend * 2, xbar);
-    }
+  if (P.xcontig) {  // all M rows in one request (the issue cost is per request)
+    if (tid == 0) bulk_load(xsm, rowp_s[0], static_cast<uint32_t>(M) * kend * 2, xbar);
+  } else if (tid < M && (rmode_s[tid] == HM_SRC_F16 || rmode_s[tid] == HM_SRC_RMS)) {
+    bulk_load(xsm + tid * L.xp, rowp_s[tid] + 2 * k0, kend * 2, xbar);  // one row per thread
   }
   if (any_emb) {
     // ---- embedding rows: token id -> table row and scale (rejected ids -> zero row)
@@ -545,7 +552,45 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 
     // ---- split-K (only when the activations did not fit): last CTA sums partials in split order
     bool owner = true;
-    if (P.nsplit > 1) {
+    if (P.nsplit > 1 && P.cluster) {
+      // ---- cluster split: every k-range keeps its partial tile in its own shared memory;
+      // rank 0 (k-range 0) sums them through DSMEM in split order -- the arithmetic of the
+      // workspace path below -- and runs the epilogue; the others wait until it has read
+      // their partial (their shared memory must outlive the reads)
+      const int per = RT * kTileRows * M;
+      for (int i = tid; i < per; i += kCons) {
+        const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
+        cpart_s[i] = tile_sum(b, r, m);
+      }
+      named_bar(kBarCons, kCons);
+      if (cluster_ctarank() != 0) {
+        if (tid == 0) {
+          fence_acq_rel_cluster();
+          mbar_arrive_dsmem(dsmem_addr(cready, 0));
+          mbar_wait_cluster(cdone, ti & 1, err);
+        }
+        named_bar(kBarCons, kCons);
+        owner = false;
+      } else {
+        if (tid == 0) mbar_wait_cluster(cready, ti & 1, err);
+        named_bar(kBarCons, kCons);
+        for (int i = tid; i < per; i += kCons) {
+          const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
+          float v[kMaxCSplit];
+#pragma unroll
+          for (int sp = 0; sp < kMaxCSplit; ++sp)
+            v[sp] = sp >= P.nsplit ? 0.f : (sp == 0 ? cpart_s[i] : ld_dsmem_f32(dsmem_addr(cpart_s + i, sp)));
+          float a = 0.f;
+#pragma unroll
+          for (int sp = 0; sp < kMaxCSplit; ++sp)
+            if (sp < P.nsplit) a += v[sp];
+          red_s[(b * kTileRows + r) * MP + m] = a;  // warp-b slot now holds the full sum
+        }
+        named_bar(kBarCons, kCons);  // every DSMEM read of this tile has returned
+        if (tid == 0)
+          for (int sp = 1; sp < P.nsplit; ++sp) mbar_arrive_dsmem(dsmem_addr(cdone, sp));
+      }
+    } else if (P.nsplit > 1) {
       float* ws = wsp;
       const int per = RT * kTileRows * M;
       float* mine = ws + ((int64_t)split * P.ntiles + tile) * per;
@@ -764,32 +809,20 @@ int auto_kspan(int M, int K, int epi) {
   return ks;
 }
 
+// One wave of CTAs, tiles strided over the grid.  CTAs per SM: enough for one tile per CTA
+// when the shape has more tiles than SMs and the activations are short enough for up to
+// four CTAs with a ring of at least four stages; otherwise up to two CTAs (what the shared
+// memory allows) with the default ring, deepened into the memory they leave free: the
+// bytes in flight per SM bound its weight stream (bandwidth = bytes in flight / memory
+// latency), which matters when a long activation row leaves room for one CTA per SM only.
 template <int MT, int EPI>
-cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_t st) {
-  GemvParams p = p0;
-  p.nst = kNST;
-  int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig).total;
-  static int configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
-    if (e != cudaSuccess) return e;
-    configured = 227 * 1024;
-  }
-  // One wave of CTAs, tiles strided over the grid.  CTAs per SM: enough for one tile per
-  // CTA when the shape has more tiles than SMs and the activations are short enough for
-  // up to four CTAs with a ring of at least four stages; otherwise up to two CTAs (what
-  // the shared memory allows) with the default ring, deepened into the memory they
-  // leave free: the bytes in flight per SM bound its weight stream (bandwidth = bytes
-  // in flight / memory latency), which matters when a long activation row leaves room
-  // for one CTA per SM only.
+void choose_occupancy(const GemvParams& p, int* per_sm_out, int* nst_out) {
   static const int cap = static_cast<int>(env_or("HM_GEMV_CTAS_PER_SM", 4));
   static const int deep = static_cast<int>(env_or("HM_GEMV_DEEP_RING", 1));
   const int units = p.ntiles * p.nsplit;
   const int want = std::max(2, (units + sm_count() - 1) / sm_count());
   auto lay = [&](int n) { return smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, n).total; };
-  int per_sm = 0;
-  for (int ps = std::min(cap, want); ps >= 1 && !per_sm; --ps) {
+  for (int ps = std::min(cap, want); ps >= 1; --ps) {
     const int limit = std::min(smem_per_sm() / ps - smem_reserved_per_cta(), 227 * 1024);
     int n = kNST;
     if (ps > 2) {
@@ -805,18 +838,92 @@ cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<MT, EPI>, kThreads, lay(n)) != cudaSuccess ||
         occ < ps)
       continue;
-    per_sm = ps;
-    p.nst = n;
+    *per_sm_out = ps;
+    *nst_out = n;
+    return;
   }
-  if (!per_sm) {
-    per_sm = 1;
-    p.nst = kNST;
+  *per_sm_out = 1;
+  *nst_out = kNST;
+}
+
+// Split of K over the CTAs of a cluster (1 = none) for a shape whose activations fit one
+// CTA: the split that minimises the stages streamed by the busiest CTA, plus a reduction
+// cost per split tile.  It pays when there are too few tiles for the CTAs the GPU holds
+// (a long K and a short N) or when a few CTAs would stream a second whole tile.
+template <int MT, int EPI>
+int choose_cluster_split(const GemvParams& p) {
+  constexpr int kRedStages = 4;  // a DSMEM reduction round costs about as much as four stages
+  const int stages = p.kspan / ks_of(EPI);  // the whole K in one k-range (nsplit 1)
+  int best = 1;
+  long best_cost = -1;
+  for (int sp = 1; sp <= kMaxCSplit; sp *= 2) {
+    if (stages % sp) continue;
+    GemvParams q = p;
+    q.kspan = p.kspan / sp;
+    q.nsplit = sp;
+    q.xcontig = sp == 1 ? p.xcontig : 0;
+    if (smem_layout(q.kspan, 8 * MT, q.has_gamma, q.xcontig).total > 227 * 1024) continue;
+    int per_sm = 1, nst = kNST;
+    choose_occupancy<MT, EPI>(q, &per_sm, &nst);
+    const int J = std::max(1, std::min(q.ntiles, per_sm * sm_count() / sp));
+    const long tiles_per_cta = (q.ntiles + J - 1) / J;
+    const long cost = tiles_per_cta * (stages / sp + (sp > 1 ? kRedStages : 0));
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
   }
-  smem = lay(p.nst);
+  return best;
+}
+
+template <int MT, int EPI>
+cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_t st) {
+  GemvParams p = p0;
+  static int configured = 0;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
+    if (e != cudaSuccess) return e;
+    hm_carveout(gemv_i8_kernel<MT, EPI>);
+    configured = 1;
+  }
+  if (p.cluster < 0) {  // automatic cluster split (whole-K k-range requested)
+    const int sp = choose_cluster_split<MT, EPI>(p);
+    p.cluster = sp > 1;
+    if (sp > 1) {
+      p.kspan /= sp;
+      p.nsplit = sp;
+      p.xcontig = 0;
+    }
+  }
+  int per_sm = 1;
+  choose_occupancy<MT, EPI>(p, &per_sm, &p.nst);
+  const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst).total;
   int J = per_sm * sm_count() / p.nsplit;
   if (J < 1) J = 1;
   if (J > p.ntiles) J = p.ntiles;
-  return hm_launch(gemv_i8_kernel<MT, EPI>, dim3(J, p.nsplit), dim3(kThreads), smem, st, p.d.pdl, map, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(J, p.nsplit);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (p.d.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = p.nsplit;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<MT, EPI>, map, p);
 }
 
 template <int EPI>
@@ -876,10 +983,20 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
   p.d = *d;
   p.has_gamma = has_gamma;
   const int kpad = padded_k(d->K, d->epi);
-  p.kspan = hm_gemv_pick_kspan(d->M, d->N, d->K, d->epi, d->kspan);
+  // kspan < 0: K split over -kspan CTAs of a cluster (2, 4 or 8), reduced in DSMEM
+  const int csplit = d->kspan < 0 ? -d->kspan : 0;
+  if (csplit && (csplit > kMaxCSplit || (csplit & (csplit - 1)) || (kpad / ks_of(d->epi)) % csplit)) return HM_EARG;
+  p.kspan = csplit ? kpad / csplit : hm_gemv_pick_kspan(d->M, d->N, d->K, d->epi, d->kspan);
   if (p.kspan <= 0 || p.kspan % ks_of(d->epi) || kpad % p.kspan) return HM_EARG;
   if (smem_layout(p.kspan, mrows_of(d->M), has_gamma).total > 227 * 1024) return HM_EARG;
   p.nsplit = kpad / p.kspan;
+  // automatic k-range with the whole K in one CTA: with HM_GEMV_CSPLIT=1 the launch may
+  // still split it over a cluster when a stage-count model says that balances the CTAs
+  // better.  Off by default: measured slower on the decode shapes (a cluster starts only
+  // when all of its CTAs fit at once, which delays it behind the previous launch's tail,
+  // and a DSMEM reduction round costs more than the stages it saves).
+  static const int csplit_auto = static_cast<int>(env_or("HM_GEMV_CSPLIT", 0));
+  p.cluster = csplit > 1 ? 1 : (d->kspan == 0 && p.nsplit == 1 && csplit_auto ? -1 : 0);
   {
     // one bulk copy for all rows: one fp16/RMS source, consecutive rows, row pitch K,
     // whole K in one k-range with no padding columns, 16-byte aligned block start
@@ -893,7 +1010,7 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
     p.xf_loop = xf_on && !d->interleave && s0.mode == HM_SRC_RMS;
   }
   p.ntiles = ntiles_of(d->N, d->epi);
-  if (p.nsplit > 1) {
+  if (p.nsplit > 1 && p.cluster != 1) {
     if (!d->ws || !d->counters || d->n_counters < p.ntiles ||
         d->ws_bytes < hm_gemv_workspace_bytes(d->M, d->N, d->K, d->epi, p.kspan))
       return HM_EARG;

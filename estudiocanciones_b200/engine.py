@@ -314,7 +314,11 @@ class FramePlan:
         d.ws, d.ws_bytes = self.ctx.ws.data_ptr(), self.ctx.ws.numel()
         d.counters, d.n_counters = self.ctx.gemv_tk, 32768
         d.err, d.kspan, d.pdl, d.l2_keep = self.ctx.err.data_ptr(), kspan, self.pdl, int(keep)
-        self._keep.append(d)
+        # the descriptor holds raw pointers: keep it and every tensor it points into alive
+        # for the plan's lifetime (a temporary passed by the caller would otherwise be
+        # freed, and its memory reused, before the launch runs)
+        self._keep.append((d, getattr(src0, "refs", None), getattr(src1, "refs", None), y, res, ss_out, rope, pos,
+                           q_out))
         ref = C.byref(d)
         if kspan == 0 and self._seg_try(lambda Lb, q: Lb.hm_seq_add_gemv(q, ref, int(keep))):
             return
@@ -327,6 +331,7 @@ class FramePlan:
     def src_f16(x, row_mul=1, row_add=0):
         s = RowSrc()
         s.mode, s.row_mul, s.row_add, s.x, s.ldx = HM_SRC_F16, row_mul, row_add, x.data_ptr(), x.stride(0)
+        s.refs = (x,)  # the plan keeps the tensors behind the pointers alive (see _gemv)
         return s
 
     @staticmethod
@@ -335,6 +340,7 @@ class FramePlan:
         s.mode, s.row_mul, s.row_add, s.x, s.ldx = HM_SRC_RMS, row_mul, row_add, x.data_ptr(), x.stride(0)
         s.ss, s.ss_tiles, s.ss_ld = ss.data_ptr(), ss.shape[0], ss.stride(0)
         s.gamma, s.eps, s.dim = gamma.data_ptr(), EPS, x.shape[1]
+        s.refs = (x, ss, gamma)
         return s
 
     @staticmethod
@@ -343,6 +349,7 @@ class FramePlan:
         s.mode, s.row_mul, s.row_add = HM_SRC_EMB, row_mul, row_add
         s.etab, s.escale, s.erows = emb.q8.data_ptr(), emb.s8.data_ptr(), emb.q8.shape[0]
         s.tok, s.tok_ld, s.tok_col, s.tok_off = tok.data_ptr(), tok.stride(0), col, off
+        s.refs = (emb.q8, emb.s8, tok)
         return s
 
     def sumsq(self, x, ss, R):

@@ -44,7 +44,10 @@ typedef struct CUstream_st* hm_stream_t; /* == cudaStream_t */
  * Replaces int8_mm / _gemv8 (app/kernels.py:20-54; M <= 16 branch, extended to 32).
  * `ws`/`counters`: split-K scratch, sized by hm_gemv_workspace_bytes /
  * hm_gemv_counters; counters must be zero before the first call and are left
- * zero by every call.  kspan = 0 picks the split automatically. */
+ * zero by every call.  kspan = 0 picks the split automatically; kspan > 0 splits K into
+ * k-ranges of kspan columns reduced through `ws` (the last CTA of a tile sums them);
+ * kspan = -s (s = 2, 4 or 8) splits K over the s CTAs of a thread-block cluster, reduced
+ * in distributed shared memory (no scratch; bit-identical to kspan = K / s). */
 int hm_gemv_i8(const void* x, int64_t ldx, const int8_t* w, const void* s, const void* res, int64_t ldres, void* y,
                int64_t ldy, int M, int N, int K, void* ws, size_t ws_bytes, int* counters, int n_counters, int* err,
                int kspan, int pdl, hm_stream_t stream);
@@ -103,7 +106,7 @@ typedef struct {
   int* counters;
   int n_counters;
   int* err;
-  int kspan;                    /* 0 = automatic */
+  int kspan;                    /* 0 = automatic, > 0 k-range width, -2/-4/-8 cluster split */
   int pdl;                      /* launch with programmatic dependent launch */
   int l2_keep;                  /* weights read again soon (decoder passes): L2 evict-last instead of evict-first */
 } hm_gemv_desc;

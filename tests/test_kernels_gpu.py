@@ -393,3 +393,69 @@ def test_rms_apply_equals_fused_rms_prologue():
     s_f16.mode, s_f16.row_mul, s_f16.x, s_f16.ldx = HM_SRC_F16, 1, xn.data_ptr(), D
     torch.testing.assert_close(run(s_rms), run(s_f16), rtol=0, atol=0)
     assert kernels.read_errors(DEV) == 0
+
+
+# ----------------------------------------------------------------------------- GEMV split over a cluster
+@pytest.mark.parametrize("M,N,K,epi,src,csplit", [
+    (8, 1024, 8192, "store_res", "f16", 4),    # decoder w2 shape
+    (8, 3072, 8192, "store_res", "f16", 2),    # backbone w2 shape
+    (8, 1024, 8192, "store_res", "f16", 8),
+    (5, 3072, 3072, "store_res", "rms", 2),    # RMS prologue, padding rows
+    (8, 4096, 3072, "silu", "rms", 2),
+    (16, 1024, 4096, "store", "f16", 4),       # two MMA row groups
+    (8, 1536, 1024, "rope", "rms", 2)])
+def test_gemv_cluster_split_equals_workspace_split(M, N, K, epi, src, csplit):
+    """kspan = -s splits K over the s CTAs of a thread-block cluster (partials summed
+    in DSMEM by rank 0); it must give exactly the workspace split with kspan = K / s
+    (same partials, same split order), including the residual, the sum-of-squares
+    partials of the next RMSNorm and the RoPE / KV-cache and SiLU epilogues."""
+    from estudiocanciones_b200.engine import Block, Linear
+    gen = torch.Generator().manual_seed(M * 7 + N + K + csplit)
+    x = torch.randn(M, K, generator=gen).half().to(DEV)
+    gamma = (1 + 0.1 * torch.randn(K, generator=gen)).half().to(DEV)
+    w, s = rand_lin(N, K, gen)
+    lin = Linear(w.to(DEV), s.to(DEV))
+    res0 = torch.randn(M, N, generator=gen).half().to(DEV)
+    ss_x = _ss(x)  # a row source holds pointers only: keep its tensors alive until the launch
+    kspan_ws = K // csplit
+    outs = []
+    for kspan in (-csplit, kspan_ws):
+        p = _plan()
+        srcx = p.src_rms(x, ss_x, gamma) if src == "rms" else p.src_f16(x)
+        if epi == "store_res":
+            y = res0.clone()
+            ss_out = torch.zeros(N // 16, M, device=DEV)
+            p._gemv(lin, M, srcx, y=y, res=y, ss_out=ss_out, kspan=kspan)
+            p.run()
+            outs.append((y, ss_out))
+        elif epi == "store":
+            y = torch.empty(M, N, dtype=torch.float16, device=DEV)
+            p._gemv(lin, M, srcx, y=y, kspan=kspan)
+            p.run()
+            outs.append((y,))
+        elif epi == "silu":
+            y = torch.empty(M, N // 2, dtype=torch.float16, device=DEV)
+            p._gemv(lin, M, srcx, epi=HM_EPI_SILU, y=y, kspan=kspan)
+            p.run()
+            outs.append((y,))
+        else:
+            Hq, Hk, hd, L = 8, 2, 128, 16
+            blk = Block.__new__(Block)
+            blk.h, blk.kvh, blk.hd = Hq, Hk, hd
+            blk.kc = torch.zeros(M, Hk, L, hd, dtype=torch.float16, device=DEV)
+            blk.vc = torch.zeros_like(blk.kc)
+            q = torch.empty(M, Hq * hd, dtype=torch.float16, device=DEV)
+            pos = torch.arange(M, device=DEV) % L
+            p._gemv(lin, M, srcx, epi=HM_EPI_ROPE_KV, rope=O.rope_table(hd, L).to(DEV), pos=pos, S=1, blk=blk,
+                    q_out=q, kspan=kspan)
+            p.run()
+            outs.append((q, blk.kc, blk.vc))
+    torch.cuda.synchronize()
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    assert kernels_errors() == 0
+
+
+def kernels_errors():
+    from estudiocanciones_b200 import kernels
+    return kernels.read_errors(DEV)
