@@ -301,6 +301,7 @@ def test_attn_golden(golden, i):
     (1, 1, 24, 8, 128, 512, [511], 37),
     (16, 2, 8, 2, 128, 8, [0, 1] * 8, 1),
     (4, 1, 8, 2, 128, 8, [7, 6, 5, 2], 1),
+    (4, 1, 8, 2, 128, 64, [15, 16, 17, 63], 1),
     (4, 1, 8, 4, 384, 40, [3, 39, 0, 20], 3),
     (2, 1, 24, 8, 128, 4282, [4281, 4023], 16),
     # 2..8 splits merge inside a thread-block cluster (DSMEM); rows whose later splits are empty
