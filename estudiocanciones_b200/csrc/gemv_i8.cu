@@ -998,9 +998,12 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
   static const int csplit_auto = static_cast<int>(env_or("HM_GEMV_CSPLIT", 0));
   p.cluster = csplit > 1 ? 1 : (d->kspan == 0 && p.nsplit == 1 && csplit_auto ? -1 : 0);
   {
-    // one bulk copy for all rows: one fp16/RMS source, consecutive rows, row pitch K,
-    // whole K in one k-range with no padding columns, 16-byte aligned block start
-    static const int contig_on = static_cast<int>(env_or("HM_GEMV_XCONTIG", 1));
+    // one bulk copy for all rows (HM_GEMV_XCONTIG=1): one fp16/RMS source, consecutive
+    // rows, row pitch K, whole K in one k-range, 16-byte aligned block start.  Off by
+    // default: the unpadded row pitch (a multiple of 128 bytes) puts two rows of every
+    // quarter-warp's fragment loads on the same banks, and the per-row copies, issued
+    // by one thread each, measured faster.
+    static const int contig_on = static_cast<int>(env_or("HM_GEMV_XCONTIG", 0));
     const hm_row_src& s0 = d->src[0];
     const char* blk = reinterpret_cast<const char*>(s0.x) + static_cast<int64_t>(s0.row_add) * s0.ldx * 2;
     p.xcontig = contig_on && !d->interleave && (s0.mode == HM_SRC_F16 || s0.mode == HM_SRC_RMS) &&
