@@ -115,8 +115,12 @@ __device__ __forceinline__ int block_row(const hm_gemv_desc& d, int epi, int til
 template <int MT, int EPI>
 __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant__ CUtensorMap wmap,
                                                            const __grid_constant__ GemvParams P) {
-  constexpr int RT = EPI == HM_EPI_SILU ? 2 : 1;
-  constexpr int KS = 4 * kBox / RT;
+  // EPI < 0: one instantiation for every epilogue, read from the parameters (the
+  // launches of a layer then share their prologue and MMA-loop code in the SM's
+  // instruction cache); EPI >= 0 folds it at compile time
+  const int epi = EPI >= 0 ? EPI : P.d.epi;
+  const int RT = epi == HM_EPI_SILU ? 2 : 1;
+  const int KS = 4 * kBox / RT;
   constexpr int MROWS = 8 * MT;
   constexpr int MP = MROWS + 1;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -281,7 +285,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     const float* rope;
     __half *qo, *kc, *vc;
   } rp{};
-  if (EPI == HM_EPI_ROPE_KV) {
+  if (epi == HM_EPI_ROPE_KV) {
     rp.hd = d.hd;
     rp.qw = d.Hq * d.hd;
     rp.kw = d.Hk * d.hd;
@@ -621,7 +625,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 
     // ---- epilogues (the owner of the tile only)
     if (owner) {
-      if (EPI == HM_EPI_STORE) {
+      if (epi == HM_EPI_STORE) {
         __half* y = yout;
         const __half* res = resid;
         const int n = n0;
@@ -642,7 +646,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
             if (er == 0 && m < M) ss_out[(int64_t)tile * ss_ld + m] = sq;
           }
         }
-      } else if (EPI == HM_EPI_ROPE_KV) {
+      } else if (epi == HM_EPI_ROPE_KV) {
         const int hd = rp.hd, qw = rp.qw, kw = rp.kw;
         __half* qo = rp.qo;
         __half* kc = rp.kc;
@@ -853,7 +857,7 @@ void choose_occupancy(const GemvParams& p, int* per_sm_out, int* nst_out) {
 template <int MT, int EPI>
 int choose_cluster_split(const GemvParams& p) {
   constexpr int kRedStages = 4;  // a DSMEM reduction round costs about as much as four stages
-  const int stages = p.kspan / ks_of(EPI);  // the whole K in one k-range (nsplit 1)
+  const int stages = p.kspan / ks_of(EPI >= 0 ? EPI : p.d.epi);  // the whole K in one k-range (nsplit 1)
   int best = 1;
   long best_cost = -1;
   for (int sp = 1; sp <= kMaxCSplit; sp *= 2) {
@@ -1022,6 +1026,11 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
   if (!weight_map(d->w, d->N, d->K, &map)) return HM_EARG;
   const int mt = d->M <= 8 ? 1 : (d->M <= 16 ? 2 : 4);
   cudaError_t e;
+  static const int generic = static_cast<int>(env_or("HM_GEMV_ONE_KERNEL", 1));
+  if (generic && (d->epi == HM_EPI_STORE || d->epi == HM_EPI_ROPE_KV || d->epi == HM_EPI_SILU)) {
+    e = launch_mt<-1>(mt, map, p, stream);
+    return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+  }
   switch (d->epi) {
     case HM_EPI_STORE: e = launch_mt<HM_EPI_STORE>(mt, map, p, stream); break;
     case HM_EPI_ROPE_KV: e = launch_mt<HM_EPI_ROPE_KV>(mt, map, p, stream); break;
