@@ -48,12 +48,15 @@ constexpr int kBoxBytes = kTileRows * kBox;
 constexpr int kStage = 4 * kBoxBytes;  // four boxes per stage
 constexpr int kNST = 6;         // ring stages at the default depth
 constexpr int kMaxNST = 14;     // deepest ring (the mbarrier arrays are sized for it)
-constexpr int kCons = 128;      // consumer threads (4 MMA warps)
-constexpr int kThreads = kCons + 32;
+constexpr int kGW = 4;          // MMA warps of one consumer group (one box of a stage each)
+constexpr int kGT = 32 * kGW;   // threads of one consumer group
+constexpr int kMaxGroups = 4;   // consumer groups of the wide kernel
+__host__ __device__ constexpr int threads_of(int groups) { return 32 * (kGW * groups + 1); }
 constexpr int kMaxM = 32;
 constexpr int kMaxCSplit = 8;   // k-ranges of one tile in a cluster (portable cluster size)
 constexpr int kXBudget = 128 * 1024;  // bytes of staged activations per CTA
-constexpr int kBarCons = 1;     // named barrier of the consumer warps
+constexpr int kBarCons = 1;     // named barrier of all consumer warps
+constexpr int kBarGrp = 2;      // named barriers 2.. : one per consumer group
 
 struct GemvParams {
   hm_gemv_desc d;
@@ -63,10 +66,11 @@ struct GemvParams {
   int xf_loop;  // every row is RMS(src[0]): CTAs with one tile normalise in registers in the MMA loop
   int nst;      // ring stages: deeper when the CTAs per SM leave shared memory free
   int cluster;  // the nsplit k-ranges of a tile run as one thread-block cluster and reduce in DSMEM
+  int groups;   // consumer groups in use (wide kernel): each streams its own tiles through its own ring
 };
 
 struct SmemLayout {
-  int ring, x, gam, red, cpart, inv, esc, rowp, rmode, flag, bars, total;  // flag: [0] tile owner, [1] abort
+  int ring, x, gam, red, cpart, inv, esc, rowp, rmode, flag, bars, total;  // flag: [g] tile owner of group g, [7] abort
   int xp;  // activation row pitch in bytes
 };
 
@@ -75,21 +79,21 @@ __host__ __device__ inline int rt_of(int epi) { return epi == HM_EPI_SILU ? 2 : 
 __host__ __device__ inline int ks_of(int epi) { return 4 * kBox / rt_of(epi); }  // k bytes per stage
 
 __host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_gamma, int xcontig = 0,
-                                                  int nst = kNST) {
+                                                  int nst = kNST, int groups = 1) {
   SmemLayout L;
-  L.ring = 0;
+  L.ring = 0;  // one ring of nst stages per consumer group
   L.xp = kspan * 2 + (xcontig ? 0 : 16);
-  L.x = nst * kStage;
+  L.x = groups * nst * kStage;
   L.gam = align_up(L.x + mrows * L.xp, 16);
   L.red = L.gam + has_gamma * kspan * 2;
-  L.cpart = L.red + 4 * kTileRows * (mrows + 1) * 4;  // this k-range's partial tile (cluster split)
+  L.cpart = L.red + groups * kGW * kTileRows * (mrows + 1) * 4;  // this k-range's partial tile (cluster split)
   L.inv = L.cpart + 2 * kTileRows * mrows * 4;
   L.esc = L.inv + kMaxM * 4;
   L.rowp = align_up(L.esc + kMaxM * 4, 8);
   L.rmode = L.rowp + kMaxM * 8;
   L.flag = L.rmode + 2 * kMaxM * 4;
-  L.bars = align_up(L.flag + 16, 8);
-  L.total = L.bars + (2 * kMaxNST + 3) * 8;
+  L.bars = align_up(L.flag + 32, 8);
+  L.total = L.bars + (2 * groups * kMaxNST + 3) * 8;
   return L;
 }
 
@@ -98,6 +102,23 @@ __host__ __device__ inline SmemLayout smem_layout(int kspan, int mrows, int has_
 // 128-column slice; lanes with t >= 2 read them rotated by two chunks (and take
 // the two halves of their weight bytes swapped to match), which keeps the eight
 // lanes of every shared-memory phase on distinct banks.
+
+// Named barrier of consumer group `grp` (kGT threads).  The ids are spelled as constants
+// so ptxas reserves only the barriers the kernel names (a register id reserves all 16,
+// which limits the CTAs per SM).
+template <int GR>
+__device__ __forceinline__ void group_bar(int grp) {
+  if (GR == 1) {
+    named_bar(kBarCons, kGT);  // one group: the consumer barrier itself (two barriers per CTA)
+  } else {
+    switch (grp) {
+      case 0: named_bar(kBarGrp, kGT); break;
+      case 1: named_bar(kBarGrp + 1, kGT); break;
+      case 2: named_bar(kBarGrp + 2, kGT); break;
+      default: named_bar(kBarGrp + 3, kGT); break;
+    }
+  }
+}
 
 __device__ __forceinline__ const hm_row_src& src_of(const hm_gemv_desc& d, int m, int& row, int& sel) {
   sel = d.interleave ? (m & 1) : 0;
@@ -112,9 +133,18 @@ __device__ __forceinline__ int block_row(const hm_gemv_desc& d, int epi, int til
   return (epi == HM_EPI_SILU && rb == 1) ? d.N / 2 + tile * kTileRows : tile * kTileRows;
 }
 
-template <int MT, int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant__ CUtensorMap wmap,
-                                                           const __grid_constant__ GemvParams P) {
+// GR consumer groups of four MMA warps (GR = 1: one group, the split-K and many-row
+// shapes; GR = 4: the wide kernel, one CTA per SM).  Each group owns a ring of weight
+// stages fed by its own producer lane and streams its own tiles (the CTA's tiles g,
+// g + groups, ...), so the tiles of an SM run concurrently; all groups share one
+// staging of the activations, which every consumer warp helps to prepare.
+// (launch bounds: the narrow 8-row kernel is left to the compiler's register choice -- a
+// minimum-blocks bound changed its schedule and measured ~10 % slower at the same
+// register count; the wider-row kernels ask for two CTAs per SM, the wide kernel one)
+template <int MT, int EPI, int GR>
+__global__ void __launch_bounds__(threads_of(GR), GR == 1 ? (MT == 1 ? 0 : 2) : 1) gemv_i8_kernel(const __grid_constant__ CUtensorMap wmap,
+                                                                    const __grid_constant__ GemvParams P) {
+  constexpr int kCons = kGT * GR;  // consumer threads
   // EPI < 0: one instantiation for every epilogue, read from the parameters (the
   // launches of a layer then share their prologue and MMA-loop code in the SM's
   // instruction cache); EPI >= 0 folds it at compile time
@@ -132,9 +162,9 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   const int M = d.M;
   const int per_tile = kspan / KS;  // stages per tile
   const int my_tiles = (P.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  const int nstages = my_tiles * per_tile;
+  const int G = GR == 1 ? 1 : P.groups;  // groups in use (<= GR)
   const int nst = P.nst;
-  const SmemLayout L = smem_layout(kspan, MROWS, P.has_gamma, P.xcontig, nst);
+  const SmemLayout L = smem_layout(kspan, MROWS, P.has_gamma, P.xcontig, nst, G);
   uint8_t* ring = smem + L.ring;
   uint8_t* xsm = smem + L.x;
   __half* gam_s = reinterpret_cast<__half*>(smem + L.gam);
@@ -145,10 +175,10 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   int* rmode_s = reinterpret_cast<int*>(smem + L.rmode);
   int* rsel_s = rmode_s + kMaxM;
   int* flag_s = reinterpret_cast<int*>(smem + L.flag);
-  volatile int* abort_s = flag_s + 1;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty = full + kMaxNST;
-  uint64_t* xbar = empty + kMaxNST;  // bulk copies of the activation rows and gammas
+  volatile int* abort_s = flag_s + 7;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [group][kMaxNST]
+  uint64_t* empty = full + G * kMaxNST;
+  uint64_t* xbar = empty + G * kMaxNST;  // bulk copies of the activation rows and gammas
   uint64_t* cready = xbar + 1;       // cluster split: the other k-ranges' partials are in (rank 0)
   uint64_t* cdone = xbar + 2;        // cluster split: rank 0 has read this CTA's partial
   float* cpart_s = reinterpret_cast<float*>(smem + L.cpart);
@@ -159,10 +189,11 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   }
   if (tid == 0) {
     *abort_s = 0;
-    for (int i = 0; i < nst; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kCons / 32);
-    }
+    for (int g = 0; g < G; ++g)
+      for (int i = 0; i < nst; ++i) {
+        mbar_init(&full[g * kMaxNST + i], 1);
+        mbar_init(&empty[g * kMaxNST + i], kGW);
+      }
     mbar_init(xbar, 1);
     if (P.cluster) {
       mbar_init(cready, P.nsplit - 1);
@@ -176,21 +207,27 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   // ================================================================ producer warp
   if (warp == kCons / 32) {
     pdl_trigger();
-    if (lane == 0) {
+    if (lane < G) {  // lane g feeds group g's ring with the stages of the group's tiles
+      const int g = lane;
       int* const perr = d.err;
       const int half_n = d.N / 2;
-      prefetch_tensormap(&wmap);
+      if (g == 0) prefetch_tensormap(&wmap);
       const uint64_t pol = d.l2_keep ? policy_evict_last() : policy_evict_first();
+      const int tiles_g = my_tiles > g ? (my_tiles - g + G - 1) / G : 0;
+      const int nstages = tiles_g * per_tile;
+      uint8_t* const gring = ring + g * nst * kStage;
+      uint64_t* const gfull = full + g * kMaxNST;
+      uint64_t* const gempty = empty + g * kMaxNST;
       int slot = 0, round = 0;  // it = round * nst + slot
       for (int it = 0; it < nstages; ++it) {
-        if (round > 0) mbar_wait_ab(&empty[slot], (round - 1) & 1, perr, abort_s);
-        const int tile = (int)blockIdx.x + (it / per_tile) * (int)gridDim.x;
+        if (round > 0) mbar_wait_ab(&gempty[slot], (round - 1) & 1, perr, abort_s);
+        const int tile = (int)blockIdx.x + (g + (it / per_tile) * G) * (int)gridDim.x;
         const int kx = k0 + (it % per_tile) * KS;
-        mbar_arrive_expect_tx(&full[slot], kStage);
+        mbar_arrive_expect_tx(&gfull[slot], kStage);
 #pragma unroll
         for (int b = 0; b < 4; ++b)
-          tma_load_2d(ring + slot * kStage + b * kBoxBytes, &wmap, kx + (b / RT) * kBox,
-                      (RT == 2 && (b % RT) == 1 ? half_n : 0) + tile * kTileRows, &full[slot], pol);
+          tma_load_2d(gring + slot * kStage + b * kBoxBytes, &wmap, kx + (b / RT) * kBox,
+                      (RT == 2 && (b % RT) == 1 ? half_n : 0) + tile * kTileRows, &gfull[slot], pol);
         if (++slot == nst) {
           slot = 0;
           ++round;
@@ -266,7 +303,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   // tile (the pass and the loop then touch each element once either way, the loop without
   // a barrier and a store) and one row block per stage (with two, two warps would
   // normalise the same columns)
-  const bool xf_loop = P.xf_loop && RT == 1 && my_tiles == 1;
+  const bool xf_loop = P.xf_loop && RT == 1 && my_tiles <= G;
   if (xf_loop)  // gamma past K meets zero activations in the MMA loop: keep it finite
     for (int c = ctail + tid; c < cpr; c += kCons) reinterpret_cast<uint4*>(gam_s)[c] = make_uint4(0, 0, 0, 0);
 
@@ -300,13 +337,16 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     rp.vc = reinterpret_cast<__half*>(d.vc);
   }
 
-  // per-row weight scales of this thread's epilogue rows (immutable): the first tile's
-  // now, each next tile's while the current one streams
-  const int er = tid & 15, em0 = tid >> 4;
+  // consumer group of this warp and the group's tiles (the CTA's tiles grp, grp + G, ...)
+  const int grp = GR == 1 ? 0 : warp / kGW, gw = GR == 1 ? warp : warp % kGW, gtid = GR == 1 ? tid : tid % kGT;
+  const int tiles_g = grp < G && my_tiles > grp ? (my_tiles - grp + G - 1) / G : 0;
+  // per-row weight scales of this thread's epilogue rows (immutable): the group's first
+  // tile's now, each next tile's while the current one streams
+  const int er = gtid & 15, em0 = gtid >> 4;
   const int half_n = RT == 2 ? N / 2 : 0;
-  int nn = (int)blockIdx.x * kTileRows + er;  // row of the next tile's scale
-  float sc0n = my_tiles > 0 && nn < N ? __half2float(scales[nn]) : 0.f;
-  float sc1n = RT == 2 && my_tiles > 0 && half_n + nn < N ? __half2float(scales[half_n + nn]) : 0.f;
+  int nn = ((int)blockIdx.x + grp * (int)gridDim.x) * kTileRows + er;  // row of the next tile's scale
+  float sc0n = tiles_g > 0 && nn < N ? __half2float(scales[nn]) : 0.f;
+  float sc1n = RT == 2 && tiles_g > 0 && half_n + nn < N ? __half2float(scales[half_n + nn]) : 0.f;
 
   pdl_wait();  // activations, tokens and sums of squares come from earlier launches
 
@@ -359,7 +399,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
     const float* ss = s0.ss + s0.row_add;
     const int tiles = s0.ss_tiles;
     const int64_t ld = s0.ss_ld;
-    for (int t = tid; t < tiles; t += kCons) {
+    // the first group's threads only: the same summation order for every kernel shape
+    for (int t = tid; t < (tid < kGT ? tiles : 0); t += kGT) {
       const float4* p4 = reinterpret_cast<const float4*>(ss + (int64_t)t * ld);
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
@@ -375,7 +416,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 #pragma unroll
     for (int i = 0; i < 4 * NV; ++i) a[i] = warp_sum(a[i]);
     float* part = red_s;  // [4 warps][MROWS], free until the first tile
-    if (lane == 0) {
+    if (lane == 0 && tid < kGT) {
 #pragma unroll
       for (int i = 0; i < 4 * NV; ++i)
         if (i < MROWS) part[warp * MROWS + i] = a[i];
@@ -461,10 +502,16 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   }
   named_bar(kBarCons, kCons);
 
-  // ---- tiles: warp w consumes box w of every stage (row block w % RT, k slice w / RT)
+  // ---- tiles: warp gw of a group consumes box gw of every stage of the group's ring
+  // (row block gw % RT, k slice gw / RT); groups without tiles are done
+  if (tiles_g == 0) return;
   const int g = lane >> 2, t = lane & 3;
   const int rot = t >> 1;  // lanes t >= 2 read their activation chunks rotated by two
-  const int ksub = warp / RT;
+  const int ksub = gw / RT;
+  uint8_t* const gring = ring + grp * nst * kStage;
+  uint64_t* const gfull = full + grp * kMaxNST;
+  uint64_t* const gempty = empty + grp * kMaxNST;
+  float* const red_g = red_s + grp * kGW * kTileRows * MP;
   // epilogue ownership: thread -> (row r of the 16 (er), rows m = em0, em0 + 8, ...)
   // in-loop RMSNorm: 1/rms of this lane's activation rows (8j + g); padding rows are zeros
   float ivr[MT];
@@ -472,12 +519,12 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
   for (int j = 0; j < MT; ++j) ivr[j] = (xf_loop && 8 * j + g < M) ? inv_s[8 * j + g] : 0.f;
   const uint4* const gam4 = reinterpret_cast<const uint4*>(gam_s);
   int slot = 0, round = 0;  // ring position of the next stage
-  for (int ti = 0; ti < my_tiles; ++ti) {
-    const int tile = (int)blockIdx.x + ti * (int)gridDim.x;
+  for (int ti = 0; ti < tiles_g; ++ti) {
+    const int tile = (int)blockIdx.x + (grp + ti * G) * (int)gridDim.x;
     const int n0 = tile * kTileRows + er;
     const float sc0 = sc0n, sc1 = sc1n;
-    if (ti + 1 < my_tiles) {
-      nn += (int)gridDim.x * kTileRows;
+    if (ti + 1 < tiles_g) {
+      nn += G * (int)gridDim.x * kTileRows;
       sc0n = nn < N ? __half2float(scales[nn]) : 0.f;
       if (RT == 2) sc1n = half_n + nn < N ? __half2float(scales[half_n + nn]) : 0.f;
     }
@@ -485,14 +532,14 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 #pragma unroll
     for (int j = 0; j < MT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     for (int st = 0; st < per_tile; ++st) {
-      mbar_wait_ab(&full[slot], round & 1, err, abort_s);  // on timeout: carry on, error flagged
-      const uint8_t* wb = ring + slot * kStage + warp * kBoxBytes;
+      mbar_wait_ab(&gfull[slot], round & 1, err, abort_s);  // on timeout: carry on, error flagged
+      const uint8_t* wb = gring + slot * kStage + gw * kBoxBytes;
       const uint4 lo0 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + rot) ^ g) << 4));
       const uint4 lo1 = *reinterpret_cast<const uint4*>(wb + g * kBox + (((2 * t + 1 - rot) ^ g) << 4));
       const uint4 hi0 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t + rot) ^ g) << 4));
       const uint4 hi1 = *reinterpret_cast<const uint4*>(wb + (g + 8) * kBox + (((2 * t + 1 - rot) ^ g) << 4));
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);  // this warp's box is in registers now
+      if (lane == 0) mbar_arrive(&gempty[slot]);  // this warp's box is in registers now
       if (++slot == nst) {
         slot = 0;
         ++round;
@@ -535,8 +582,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
         for (int j = 0; j < MT; ++j) mma_16816(acc[j], a0, a1, a2, a3, xw[j][2 * s], xw[j][2 * s + 1]);
       }
     }
-    // ---- partial sums of the four warps -> red_s[warp][row][m]
-    float* rw = red_s + warp * kTileRows * MP;
+    // ---- partial sums of the group's four warps -> red_g[warp][row][m]
+    float* rw = red_g + gw * kTileRows * MP;
 #pragma unroll
     for (int j = 0; j < MT; ++j) {
       const int m = 8 * j + 2 * t;
@@ -545,12 +592,12 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       rw[(g + 8) * MP + m] = acc[j][2];
       rw[(g + 8) * MP + m + 1] = acc[j][3];
     }
-    named_bar(kBarCons, kCons);
+    group_bar<GR>(grp);
     // value of (row block b, row r, activation row m): warps b, b+RT, ... summed in order
     auto tile_sum = [&](int b, int r, int m) {
       float a = 0.f;
 #pragma unroll
-      for (int w = b; w < 4; w += RT) a += red_s[(w * kTileRows + r) * MP + m];
+      for (int w = b; w < kGW; w += RT) a += red_g[(w * kTileRows + r) * MP + m];
       return a;
     };
 
@@ -562,23 +609,23 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
       // workspace path below -- and runs the epilogue; the others wait until it has read
       // their partial (their shared memory must outlive the reads)
       const int per = RT * kTileRows * M;
-      for (int i = tid; i < per; i += kCons) {
+      for (int i = gtid; i < per; i += kGT) {
         const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
         cpart_s[i] = tile_sum(b, r, m);
       }
-      named_bar(kBarCons, kCons);
+      group_bar<GR>(grp);
       if (cluster_ctarank() != 0) {
-        if (tid == 0) {
+        if (gtid == 0) {
           fence_acq_rel_cluster();
           mbar_arrive_dsmem(dsmem_addr(cready, 0));
           mbar_wait_cluster(cdone, ti & 1, err);
         }
-        named_bar(kBarCons, kCons);
+        group_bar<GR>(grp);
         owner = false;
       } else {
-        if (tid == 0) mbar_wait_cluster(cready, ti & 1, err);
-        named_bar(kBarCons, kCons);
-        for (int i = tid; i < per; i += kCons) {
+        if (gtid == 0) mbar_wait_cluster(cready, ti & 1, err);
+        group_bar<GR>(grp);
+        for (int i = gtid; i < per; i += kGT) {
           const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
           float v[kMaxCSplit];
 #pragma unroll
@@ -588,39 +635,39 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
 #pragma unroll
           for (int sp = 0; sp < kMaxCSplit; ++sp)
             if (sp < P.nsplit) a += v[sp];
-          red_s[(b * kTileRows + r) * MP + m] = a;  // warp-b slot now holds the full sum
+          red_g[(b * kTileRows + r) * MP + m] = a;  // warp-b slot now holds the full sum
         }
-        named_bar(kBarCons, kCons);  // every DSMEM read of this tile has returned
-        if (tid == 0)
+        group_bar<GR>(grp);  // every DSMEM read of this tile has returned
+        if (gtid == 0)
           for (int sp = 1; sp < P.nsplit; ++sp) mbar_arrive_dsmem(dsmem_addr(cdone, sp));
       }
     } else if (P.nsplit > 1) {
       float* ws = wsp;
       const int per = RT * kTileRows * M;
       float* mine = ws + ((int64_t)split * P.ntiles + tile) * per;
-      for (int i = tid; i < per; i += kCons) {
+      for (int i = gtid; i < per; i += kGT) {
         const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
         mine[i] = tile_sum(b, r, m);
       }
       __threadfence();
-      named_bar(kBarCons, kCons);
-      if (tid == 0) flag_s[0] = (atomicAdd(&counters[tile], 1) == P.nsplit - 1);
-      named_bar(kBarCons, kCons);
-      owner = flag_s[0] != 0;
+      group_bar<GR>(grp);
+      if (gtid == 0) flag_s[grp] = (atomicAdd(&counters[tile], 1) == P.nsplit - 1);
+      group_bar<GR>(grp);
+      owner = flag_s[grp] != 0;
       if (owner) {
         __threadfence();
-        for (int i = tid; i < per; i += kCons) {
+        for (int i = gtid; i < per; i += kGT) {
           const int b = i / (kTileRows * M), r = (i / M) % kTileRows, m = i % M;
           float a = 0.f;
           for (int sp = 0; sp < P.nsplit; ++sp) a += __ldcg(ws + ((int64_t)sp * P.ntiles + tile) * per + i);
-          red_s[(b * kTileRows + r) * MP + m] = a;  // warp-b slot now holds the full sum
+          red_g[(b * kTileRows + r) * MP + m] = a;  // warp-b slot now holds the full sum
         }
-        if (tid == 0) counters[tile] = 0;
-        named_bar(kBarCons, kCons);
+        if (gtid == 0) counters[tile] = 0;
+        group_bar<GR>(grp);
       }
     }
     auto value = [&](int b, int r, int m) {
-      return P.nsplit > 1 ? red_s[(b * kTileRows + r) * MP + m] : tile_sum(b, r, m);
+      return P.nsplit > 1 ? red_g[(b * kTileRows + r) * MP + m] : tile_sum(b, r, m);
     };
 
     // ---- epilogues (the owner of the tile only)
@@ -703,7 +750,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const __grid_constant
         }
       }
     }
-    named_bar(kBarCons, kCons);  // red_s is reused by the next tile
+    group_bar<GR>(grp);  // red_g is reused by the next tile
   }
 }
 
@@ -839,7 +886,8 @@ void choose_occupancy(const GemvParams& p, int* per_sm_out, int* nst_out) {
         while (n < kMaxNST && lay(n + 1) <= limit) ++n;
     }
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<MT, EPI>, kThreads, lay(n)) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<MT, EPI, 1>, threads_of(1), lay(n)) !=
+            cudaSuccess ||
         occ < ps)
       continue;
     *per_sm_out = ps;
@@ -880,35 +928,24 @@ int choose_cluster_split(const GemvParams& p) {
   return best;
 }
 
-template <int MT, int EPI>
-cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_t st) {
-  GemvParams p = p0;
+template <int MT, int EPI, int GR>
+cudaError_t configure_kernel() {
   static int configured = 0;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel<MT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel<MT, EPI, GR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
     if (e != cudaSuccess) return e;
-    hm_carveout(gemv_i8_kernel<MT, EPI>);
+    hm_carveout(gemv_i8_kernel<MT, EPI, GR>);
     configured = 1;
   }
-  if (p.cluster < 0) {  // automatic cluster split (whole-K k-range requested)
-    const int sp = choose_cluster_split<MT, EPI>(p);
-    p.cluster = sp > 1;
-    if (sp > 1) {
-      p.kspan /= sp;
-      p.nsplit = sp;
-      p.xcontig = 0;
-    }
-  }
-  int per_sm = 1;
-  choose_occupancy<MT, EPI>(p, &per_sm, &p.nst);
-  const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst).total;
-  int J = per_sm * sm_count() / p.nsplit;
-  if (J < 1) J = 1;
-  if (J > p.ntiles) J = p.ntiles;
+  return cudaSuccess;
+}
+
+template <int MT, int EPI, int GR>
+cudaError_t launch_grid(const CUtensorMap& map, const GemvParams& p, int J, int smem, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(J, p.nsplit);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads_of(GR));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
@@ -927,7 +964,68 @@ cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<MT, EPI>, map, p);
+  return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<MT, EPI, GR>, map, p);
+}
+
+// The wide kernel (8 rows, one k-range): one CTA per SM, as many consumer groups as the
+// SM has tiles (up to four), each with the deepest ring that fits.  Returns false when
+// the shape does not fit it (the narrow kernel runs instead).
+template <int EPI>
+bool wide_shape(GemvParams& p, int* J, int* smem) {
+  if (configure_kernel<1, EPI, kMaxGroups>() != cudaSuccess) return false;  // before the occupancy query
+  const int nsm = sm_count();
+  *J = std::min(p.ntiles, nsm);
+  for (int G = std::min(kMaxGroups, (p.ntiles + *J - 1) / *J); G >= 1; --G) {
+    int n = kMaxNST;
+    while (n >= 2 && smem_layout(p.kspan, 8, p.has_gamma, p.xcontig, n, G).total > 227 * 1024) --n;
+    if (n < 2) continue;
+    int occ = 0;
+    const int sm = smem_layout(p.kspan, 8, p.has_gamma, p.xcontig, n, G).total;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<1, EPI, kMaxGroups>,
+                                                      threads_of(kMaxGroups), sm) != cudaSuccess ||
+        occ < 1)
+      return false;
+    p.groups = G;
+    p.nst = n;
+    *smem = sm;
+    return true;
+  }
+  return false;
+}
+
+template <int MT, int EPI>
+cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_t st) {
+  GemvParams p = p0;
+  p.groups = 1;
+  cudaError_t e = configure_kernel<MT, EPI, 1>();
+  if (e != cudaSuccess) return e;
+  if (p.cluster < 0) {  // automatic cluster split (whole-K k-range requested)
+    const int sp = choose_cluster_split<MT, EPI>(p);
+    p.cluster = sp > 1;
+    if (sp > 1) {
+      p.kspan /= sp;
+      p.nsplit = sp;
+      p.xcontig = 0;
+    }
+  }
+  int per_sm = 1;
+  choose_occupancy<MT, EPI>(p, &per_sm, &p.nst);
+  // HM_GEMV_WIDE: 1 (default) the wide kernel when the narrow one cannot give every tile
+  // its own CTA (some CTAs would stream a second tile after their first), 2 for every
+  // 8-row launch with one k-range, 0 never.  (A wide CTA cannot share its SM with the
+  // previous launch's tail, so short launches that fit the narrow kernel keep it.)
+  static const int wide = static_cast<int>(env_or("HM_GEMV_WIDE", 1));
+  if (MT == 1 && p.nsplit == 1 && !p.cluster &&
+      (wide == 2 || (wide == 1 && p.ntiles > per_sm * sm_count()))) {
+    GemvParams q = p;
+    int J = 0, smem = 0;
+    if (wide_shape<EPI>(q, &J, &smem)) return launch_grid<1, EPI, kMaxGroups>(map, q, J, smem, st);
+  }
+  const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst).total;
+  int J = per_sm * sm_count() / p.nsplit;
+  if (J < 1) J = 1;
+  if (J > p.ntiles) J = p.ntiles;
+  return launch_grid<MT, EPI, 1>(map, p, J, smem, st);
 }
 
 template <int EPI>
