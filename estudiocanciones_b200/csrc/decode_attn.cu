@@ -338,7 +338,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
 constexpr int kTcPos = 64;   // positions per stage (4 warps x 16)
 constexpr int kTcNst = 3;
 constexpr int kTcBox = kTcPos * 128;  // bytes of one 64x64 fp16 box
-constexpr int kMaxCluster = 8;        // splits merged inside a cluster (portable cluster size)
+constexpr int kMaxCluster = 4;        // splits merged inside a cluster
+constexpr int kMaxPushG = 4;          // query heads per KV head of the cluster merge
 
 struct TcSmem {
   uint8_t k[kTcNst][2][kTcBox];  // [stage][dims 0-63 | 64-127][64 positions x 128 B]
@@ -346,9 +347,12 @@ struct TcSmem {
   float mw[4][kMaxG], lw[4][kMaxG];
   float cw[kMaxG][kMaxSplit], cl[kMaxG][kMaxSplit], cden[kMaxG];
   float cm[kMaxG], cd[kMaxG];  // this CTA's split maxima and denominators (cluster merge)
+  // cluster merge, rank 0 only: the partials the other splits push (num, maxima, denominators)
+  float cpush[kMaxCluster - 1][kMaxPushG][128];
+  float cpm[kMaxCluster - 1][kMaxPushG], cpl[kMaxCluster - 1][kMaxPushG];
   float fw[4][kMaxG], hm[kMaxG], hd[kMaxG];  // per head: warp weights, maximum, denominator
   uint64_t bar[kTcNst];
-  uint64_t cready, cdone;  // cluster merge: partials of every split in / the leader has read them
+  uint64_t cready;  // cluster merge: the partials of every other split are in rank 0's shared memory
   int flag, abort_flag;
 };
 
@@ -377,10 +381,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
   if (tid == 0) {
     sm.abort_flag = 0;
     for (int i = 0; i < kTcNst; ++i) mbar_init(&sm.bar[i], 1);
-    if (clus) {
-      mbar_init(&sm.cready, nsplit - 1);
-      mbar_init(&sm.cdone, 1);
-    }
+    if (clus) mbar_init(&sm.cready, nsplit - 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -560,10 +561,15 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
     if (nsplit == 1) {
       og[(head0 + gg) * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
     } else if (clus) {
-      cnum[gg * HD + d] = num;
-      if (d == 0) {
-        sm.cm[gg] = M;
-        sm.cd[gg] = den;
+      const uint32_t rank = cluster_ctarank();
+      if (rank == 0) {
+        cnum[gg * HD + d] = num;
+      } else {  // straight into rank 0's shared memory
+        st_dsmem_f32(dsmem_addr(&sm.cpush[rank - 1][gg][d], 0), num);
+        if (d == 0) {
+          st_dsmem_f32(dsmem_addr(&sm.cpm[rank - 1][gg], 0), M);
+          st_dsmem_f32(dsmem_addr(&sm.cpl[rank - 1][gg], 0), den);
+        }
       }
     } else {
       wa[((head0 + gg) * nsplit + sp) * HD + d] = num;
@@ -575,17 +581,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
   }
   if (nsplit == 1) return;
   if (clus) {
-    // ---- split merge inside the cluster: every CTA keeps its partial in its own shared
-    // memory and signals the leader (rank 0), which reads the partials through DSMEM,
-    // merges them in split order (the same arithmetic as the workspace path below) and
-    // releases the others, whose shared memory must live until it has read them.
+    // ---- split merge inside the cluster: the other splits have pushed their partials
+    // into rank 0's shared memory; they signal rank 0 and exit (nothing reads their own
+    // shared memory), rank 0 merges in split order (the same arithmetic as the workspace
+    // path below) from local memory.
     __syncthreads();
     const uint32_t rank = cluster_ctarank();
     if (rank != 0) {
       if (tid == 0) {
         fence_acq_rel_cluster();
         mbar_arrive_dsmem(dsmem_addr(&sm.cready, 0));
-        mbar_wait_cluster(&sm.cdone, 0, err);
       }
       return;
     }
@@ -596,8 +601,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
       float ms[kMaxCluster], ls[kMaxCluster];
 #pragma unroll
       for (int s2 = 0; s2 < kMaxCluster; ++s2) {
-        ms[s2] = s2 >= nsplit ? -INFINITY : (s2 == 0 ? sm.cm[tid] : ld_dsmem_f32(dsmem_addr(&sm.cm[tid], s2)));
-        ls[s2] = s2 >= nsplit ? 0.f : (s2 == 0 ? sm.cd[tid] : ld_dsmem_f32(dsmem_addr(&sm.cd[tid], s2)));
+        ms[s2] = s2 >= nsplit ? -INFINITY : (s2 == 0 ? sm.hm[tid] : sm.cpm[s2 - 1][tid]);
+        ls[s2] = s2 >= nsplit ? 0.f : (s2 == 0 ? sm.hd[tid] : sm.cpl[s2 - 1][tid]);
       }
       float mx = -INFINITY;
 #pragma unroll
@@ -616,21 +621,14 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
     }
     __syncthreads();
     for (int i = tid; i < G * HD; i += kThreads) {
-      const int gg = i / HD;
-      float ns[kMaxCluster];
-#pragma unroll
-      for (int s2 = 0; s2 < kMaxCluster; ++s2)
-        ns[s2] = s2 >= nsplit ? 0.f : (s2 == 0 ? cnum[i] : ld_dsmem_f32(dsmem_addr(&cnum[i], s2)));
+      const int gg = i / HD, d = i - gg * HD;
       float num = 0.f;
 #pragma unroll
       for (int s2 = 0; s2 < kMaxCluster; ++s2)
-        if (s2 < nsplit) num += ns[s2] * sm.cw[gg][s2];
+        if (s2 < nsplit) num += (s2 == 0 ? cnum[i] : sm.cpush[s2 - 1][gg][d]) * sm.cw[gg][s2];
       const float den = sm.cden[gg];
-      og[(head0 + gg) * HD + i - gg * HD] = __float2half_rn(den > 0.f ? num / den : 0.f);
+      og[(head0 + gg) * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
     }
-    __syncthreads();  // every DSMEM read of this CTA has returned
-    if (tid == 0)
-      for (int s2 = 1; s2 < nsplit; ++s2) mbar_arrive_dsmem(dsmem_addr(&sm.cdone, s2));
     return;
   }
   __threadfence();
@@ -735,7 +733,7 @@ cudaError_t launch_attn_tc(const AttnParams& p, int B, int pdl, cudaStream_t st)
     return e ? atoi(e) : 1;
   }();
   AttnParams q = p;
-  q.cluster = clus_on && p.nsplit >= 2 && p.nsplit <= kMaxCluster;
+  q.cluster = clus_on && p.nsplit >= 2 && p.nsplit <= kMaxCluster && p.Hq / p.Hk <= kMaxPushG;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nsplit, p.Hk, p.R);
   cfg.blockDim = dim3(kThreads);

@@ -131,6 +131,9 @@ HM_DEV float ld_dsmem_f32(uint32_t addr) {
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
+HM_DEV void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
 HM_DEV void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 // Arrive (release at cluster scope) on an mbarrier of another CTA of the cluster.
 HM_DEV void mbar_arrive_dsmem(uint32_t remote_bar) {
