@@ -95,22 +95,30 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
     nz[j] = v < V ? noise[(int64_t)n * ldn + v] : 1.f;
   }
   pdl_wait();
+  // every load of the two rows first (predicated, no branches around them, so they are
+  // all in flight together), then the mix
+  const unsigned short* const crow = reinterpret_cast<const unsigned short*>(logits + (int64_t)n * ldl);
+  const unsigned short* const urow = reinterpret_cast<const unsigned short*>(logits + (int64_t)(n + (mix ? Nt : 0)) * ldl);
+  unsigned short cb[kPer], ub[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int v = tid + j * kThreads;
+    cb[j] = v < V ? __ldg(crow + v) : 0;
+    ub[j] = v < V && mix ? __ldg(urow + v) : 0;
+  }
   __half gv[kPer];
   uint32_t key[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int v = tid + j * kThreads;
-    __half g = __float2half_rn(0.f);
-    if (v < V) {
-      const __half c = logits[(int64_t)n * ldl + v];
-      g = c;
-      if (mix) {
-        const __half u = logits[(int64_t)(n + Nt) * ldl + v];
-        const __half d = __hsub(c, u);
-        const __half e = __float2half_rn(__half2float(d) * cfg);
-        g = __hadd(u, e);
-      }
+    __half g = __ushort_as_half(cb[j]);
+    if (mix) {
+      const __half c = g, u = __ushort_as_half(ub[j]);
+      const __half d = __hsub(c, u);
+      const __half e = __float2half_rn(__half2float(d) * cfg);
+      g = __hadd(u, e);
     }
+    if (v >= V) g = __float2half_rn(0.f);
     gv[j] = g;
     key[j] = h2key(g);
   }
