@@ -103,8 +103,10 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const __grid_constant
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int v = tid + j * kThreads;
-    cb[j] = v < V ? __ldg(crow + v) : 0;
-    ub[j] = v < V && mix ? __ldg(urow + v) : 0;
+    // (plain loads: the rows are rewritten by the head GEMV before every sampler, so they
+    // must not come through the non-coherent read-only path)
+    cb[j] = v < V ? crow[v] : 0;
+    ub[j] = v < V && mix ? urow[v] : 0;
   }
   __half gv[kPer];
   uint32_t key[kPer];
