@@ -362,17 +362,21 @@ def run_ours(a, world, rank, local):
         e2e_step()
         torch.cuda.synchronize()
         barrier(world)
+        e2e_clocks = Clocks(local)
+        e2e_clocks.start()
         t0 = time.perf_counter()
         for _ in range(a.e2e_steps):
             res = e2e_step()
         torch.cuda.synchronize()
         sec = max_over_ranks((time.perf_counter() - t0) / a.e2e_steps, world)
+        e2e_clk = e2e_clocks.result()
         d2h = sum(r.numel() * 8 for r in res) + math.ceil(F_ / 25) * 25 * a.takes
         out["e2e"] = {"value": round(world * a.takes * F_ * 0.08 / sec, 3), "unit": UNIT,
                       "h2d_bytes_per_step": P * 8, "d2h_bytes_per_step": int(d2h),
                       "ms_per_step": round(1000 * sec, 2),
                       "includes": f"prompt H2D, GPU text-embedding gather, tensor-core prefill, {F_} frames, "
-                                  f"EOS checks every 25 frames, token streams gathered and read back"}
+                                  f"EOS checks every 25 frames, token streams gathered and read back",
+                      "clocks": e2e_clk}
     # ---- CPU baseline: the reference CPU path on this host, rank 0 at N=1
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         tcpu = {k: v.cpu() for k, v in model_tensors(dev, seed=0).items()}
