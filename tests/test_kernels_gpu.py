@@ -460,3 +460,90 @@ def test_gemv_cluster_split_equals_workspace_split(M, N, K, epi, src, csplit):
 def kernels_errors():
     from estudiocanciones_b200 import kernels
     return kernels.read_errors(DEV)
+
+
+# ----------------------------------------------------------------------------- wide GEMV kernel (backbone shapes)
+@pytest.mark.parametrize("M", [8, 5])
+def test_gemv_wide_silu_backbone_shape(M):
+    """w1|w3 of the backbone (N 2 x 8192, K 3072: 512 tiles, more than the narrow kernel
+    has CTAs) runs on the wide kernel: RMSNorm prologue + SiLU epilogue vs the oracle."""
+    from estudiocanciones_b200.engine import Linear
+    gen = torch.Generator().manual_seed(31 + M)
+    D, F = 3072, 8192
+    x = torch.randn(M, D, generator=gen).half()
+    gamma = (1 + 0.1 * torch.randn(D, generator=gen)).half()
+    w, s = rand_lin(2 * F, D, gen)
+    lin = Linear(w.to(DEV), s.to(DEV))
+    xd, gd = x.to(DEV), gamma.to(DEV)
+    ss = _ss(xd)
+    y = torch.empty(M, F, dtype=torch.float16, device=DEV)
+    p = _plan()
+    p._gemv(lin, M, p.src_rms(xd, ss, gd), epi=HM_EPI_SILU, y=y)
+    p.run()
+    xn = O.rmsnorm(x, gamma)
+    a = O.gemv_i8(xn, w, s)
+    ref = O.silu_mul(a)
+    sl = rms_slack(xn, w, s, a)
+    close16(y, ref, ulps=3, frac_exact=0.9, slack=2 * (sl[:, :F] * a[:, F:].float().abs() + sl[:, F:]))
+
+
+def test_gemv_wide_rope_backbone_shape():
+    """qkv of the backbone (N 5120, K 3072: 320 tiles) on the wide kernel: RoPE + KV-cache
+    write epilogue vs the oracle; cache slots nobody writes stay untouched."""
+    from estudiocanciones_b200.engine import Block, Linear
+    gen = torch.Generator().manual_seed(41)
+    Hq, Hk, hd, D, L, R = 24, 8, 128, 3072, 64, 8
+    x = torch.randn(R, D, generator=gen).half()
+    gamma = (1 + 0.1 * torch.randn(D, generator=gen)).half()
+    N = (Hq + 2 * Hk) * hd
+    w, s = rand_lin(N, D, gen)
+    pos = torch.tensor([0, 1, 5, 17, 33, 62, 63, 40])
+    rope = O.rope_table(hd, L)
+    kc0 = torch.randn(R, Hk, L, hd, generator=gen).half()
+    vc0 = torch.randn(R, Hk, L, hd, generator=gen).half()
+    blk = Block.__new__(Block)
+    blk.h, blk.kvh, blk.hd = Hq, Hk, hd
+    blk.kc, blk.vc = kc0.clone().to(DEV), vc0.clone().to(DEV)
+    lin = Linear(w.to(DEV), s.to(DEV))
+    xd, gd, rd, pd = x.to(DEV), gamma.to(DEV), rope.to(DEV), pos.to(DEV)
+    ss = _ss(xd)
+    q = torch.empty(R, Hq * hd, dtype=torch.float16, device=DEV)
+    p = _plan()
+    p._gemv(lin, R, p.src_rms(xd, ss, gd), epi=HM_EPI_ROPE_KV, rope=rd, pos=pd, S=1, blk=blk, q_out=q)
+    p.run()
+    xn = O.rmsnorm(x, gamma)
+    qkv = O.gemv_i8(xn, w, s)
+    kc, vc = kc0.clone(), vc0.clone()
+    qr = O.rope_kv_write(qkv, rope, pos, kc, vc, 1, Hq, Hk)
+    sl = rms_slack(xn, w, s, qkv).float().abs()
+    qsl = sl[:, : Hq * hd]
+    qsl = torch.maximum(qsl, qsl.reshape(R, Hq, hd // 2, 2).flip(-1).reshape(R, -1))
+    close16(q, qr, ulps=2, frac_exact=0.9, slack=qsl)
+    close16(blk.kc, kc, ulps=2, frac_exact=0.95, slack=2e-3 * kc.float().abs() + 5e-4)
+    close16(blk.vc, vc, ulps=2, frac_exact=0.95, slack=2e-3 * vc.float().abs() + 5e-4)
+    mask = torch.ones(R, L, dtype=torch.bool)
+    for r in range(R):
+        mask[r, int(pos[r])] = False
+    idx = mask.nonzero(as_tuple=True)
+    assert torch.equal(blk.kc.cpu().permute(0, 2, 1, 3)[idx], kc0.permute(0, 2, 1, 3)[idx])
+    assert torch.equal(blk.vc.cpu().permute(0, 2, 1, 3)[idx], vc0.permute(0, 2, 1, 3)[idx])
+
+
+def test_gemv_wide_store_residual_backbone_w2_shape():
+    """w2 of the backbone (N 3072, K 8192: one narrow CTA per SM, 192 tiles) on the wide
+    kernel: residual + sum-of-squares partials vs the oracle."""
+    from estudiocanciones_b200.engine import Linear
+    gen = torch.Generator().manual_seed(43)
+    M, D, N = 8, 8192, 3072
+    x = (torch.randn(M, D, generator=gen) * 0.5).half()
+    w, s = rand_lin(N, D, gen)
+    res = torch.randn(M, N, generator=gen).half()
+    lin = Linear(w.to(DEV), s.to(DEV))
+    xd, yd = x.to(DEV), res.to(DEV).clone()
+    ss_out = torch.zeros(N // 16, M, device=DEV)
+    p = _plan()
+    p._gemv(lin, M, p.src_f16(xd), y=yd, res=yd, ss_out=ss_out)
+    p.run()
+    ref = O.gemv_i8(x, w, s, res)
+    close16(yd, ref, ulps=2, frac_exact=0.9, slack=acc_slack(x, w, s))
+    torch.testing.assert_close(ss_out.cpu(), _ss(yd).cpu(), rtol=1e-5, atol=1e-4)
