@@ -54,7 +54,6 @@ constexpr int kMaxGroups = 4;   // consumer groups of the wide kernel
 __host__ __device__ constexpr int threads_of(int groups) { return 32 * (kGW * groups + 1); }
 constexpr int kMaxM = 32;
 constexpr int kMaxCSplit = 8;   // k-ranges of one tile in a cluster (portable cluster size)
-constexpr int kXBudget = 128 * 1024;  // bytes of staged activations per CTA
 constexpr int kBarCons = 1;     // named barrier of all consumer warps
 constexpr int kBarGrp = 2;      // named barriers 2.. : one per consumer group
 
@@ -128,10 +127,6 @@ __device__ __forceinline__ const hm_row_src& src_of(const hm_gemv_desc& d, int m
   return s;
 }
 
-// first weight row of row block rb (0: w1 / the only block, 1: w3) of tile `tile`
-__device__ __forceinline__ int block_row(const hm_gemv_desc& d, int epi, int tile, int rb) {
-  return (epi == HM_EPI_SILU && rb == 1) ? d.N / 2 + tile * kTileRows : tile * kTileRows;
-}
 
 // GR consumer groups of four MMA warps (GR = 1: one group, the split-K and many-row
 // shapes; GR = 4: the wide kernel, one CTA per SM).  Each group owns a ring of weight
