@@ -491,6 +491,12 @@ class HeartMuLaLite:
 
     def release(self):
         """Free caches, graphs and buffers (``app/engine.py:463-469``)."""
+        rt = self._rt
+        if rt is not None:
+            # the plans' operations close over the runtime (a reference cycle): clear them so
+            # the graphs and buffers go now, not whenever the cyclic collector next runs
+            rt.graphs.clear()
+            rt.plans.clear()
         self.graphs.clear()
         self._rt = None
         self.backbone.free()
