@@ -20,10 +20,12 @@
 //               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) x4 per
 //               k-block from shared-memory descriptors, fp32 accumulators in
 //               TMEM, and releases ring slots with tcgen05.commit.
-//   warps 2-5   convert the int8 tile to fp16 in the K-major 128B-swizzled
-//               layout the MMA reads (double-buffered), then run the epilogue:
-//               tcgen05.ld of their 32 TMEM lanes, scale, round, residual/SiLU,
-//               store.
+//   warps 2-9   convert the int8 tile to fp16 in the K-major 128B-swizzled
+//               layout the MMA reads (double-buffered; eight warps, so two per
+//               SM sub-partition hide each other's latency: with four the
+//               conversion, not the MMA, set the pace), then run the epilogue:
+//               tcgen05.ld of their 32 TMEM lanes (warp % 4) over half of the
+//               tile's columns each, scale, round, residual/SiLU, store.
 // Every wait is bounded (HM_ERR_TIMEOUT in the caller's error word).
 #include <cudaTypedefs.h>
 
@@ -35,7 +37,8 @@
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, NST = 4;
-constexpr int kThreads = 192;
+constexpr int kConvW = 8;                  // converter / epilogue warps
+constexpr int kThreads = 64 + 32 * kConvW;  // + TMA warp + MMA warp
 constexpr uint32_t kTmemCols = 256;
 constexpr int kABytes = BM * BK * 2;   // 16 KB
 constexpr int kBqBytes = BN * BK;      // 16 KB
@@ -140,10 +143,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
     sm.abort_flag = 0;
     for (int i = 0; i < NST; ++i) {
       mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1 + 4);  // MMA commit (A consumed) + 4 converter warps (int8 tile consumed)
+      mbar_init(&sm.empty[i], 1 + kConvW);  // MMA commit (A consumed) + the converter warps (int8 tile consumed)
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.bh_full[i], 4);
+      mbar_init(&sm.bh_full[i], kConvW);
       mbar_init(&sm.bh_empty[i], 1);
     }
     mbar_init(&sm.acc_full, 1);
@@ -193,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
     }
   } else {
     // ------------------------------------------------------------ converters, then epilogue
-    const int ct = tid - 64;  // 0..127
+    const int ct = tid - 64;  // 0 .. 32 * kConvW - 1
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % NST, b = kb & 1;
       mbar_wait_ab(&sm.full[s], (kb / NST) & 1, err, abort_s);
@@ -201,8 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
       const uint8_t* src = sm.bq[s];
       uint8_t* dst = sm.bh[b];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int id = ct + 128 * i;  // 16-byte int8 chunk: row n, k = 16j .. 16j+15
+      for (int i = 0; i < (BN * BK / 16) / (32 * kConvW); ++i) {
+        const int id = ct + 32 * kConvW * i;  // 16-byte int8 chunk: row n, k = 16j .. 16j+15
         const int n = id >> 2, j = id & 3;
         const uint4 q = *reinterpret_cast<const uint4*>(src + n * BK + j * 16);
         uint4 h0, h1;
@@ -221,10 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
         mbar_arrive(&sm.empty[s]);
       }
     }
-    // ---- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 = tile rows
+    // ---- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 = tile rows, and the
+    // (w - 2) / 4 -th part of the tile's columns
     mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
     tc_fence_after();
     const int q = warp & 3;
+    constexpr int kParts = kConvW / 4;
+    const int part = (warp - 2) / 4;
     const int m = m0 + 32 * q + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
     const int N = P.N, M = P.M;
@@ -235,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
       const int f0 = nt * (BN / 2);
       const int wh = P.wrows_half;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+      for (int c0 = part * (BN / 2 / kParts); c0 < (part + 1) * (BN / 2 / kParts); c0 += 16) {
         float va[16], vb[16];
         tmem_ld16(trow + c0, va);
         tmem_ld16(trow + BN / 2 + c0, vb);
@@ -263,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
       const __half* const R = P.res;
       const int64_t ldr = P.ldr;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = part * (BN / kParts); c0 < (part + 1) * (BN / kParts); c0 += 16) {
         float v[16];
         tmem_ld16(trow + c0, v);
         const int n = n0 + c0;
