@@ -370,7 +370,7 @@ def run_ours(a, world, rank, local):
         torch.cuda.synchronize()
         sec = max_over_ranks((time.perf_counter() - t0) / a.e2e_steps, world)
         e2e_clk = e2e_clocks.result()
-        d2h = sum(r.numel() * 8 for r in res) + math.ceil(F_ / 25) * 25 * a.takes
+        d2h = sum(r.numel() * 8 for r in res) + math.ceil(F_ / 25) * 8 * a.takes  # streams + EOS reads
         out["e2e"] = {"value": round(world * a.takes * F_ * 0.08 / sec, 3), "unit": UNIT,
                       "h2d_bytes_per_step": P * 8, "d2h_bytes_per_step": int(d2h),
                       "ms_per_step": round(1000 * sec, 2),

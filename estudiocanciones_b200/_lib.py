@@ -55,7 +55,7 @@ SIGNATURES = {
     "hm_silu_mul": (_I, [_P, _P, _I, _I, _P]),
     "hm_emb_gather_i8": (_I, [_P, _I, _P, _P, _I64, _I, _P, _P, _P]),
     "hm_emb_sum_i8": (_I, [_P, _I64, _I, _I, _I64, _P, _P, _I64, _I, _P, _P, _I64, _P, _I, _P]),
-    "hm_frame_commit": (_I, [_P, _P, _I, _I, _P, _I, _P, _P, _I64, _I, _P]),
+    "hm_frame_commit": (_I, [_P, _P, _I, _I, _P, _I, _P, _P, _I64, _P, _I64, _I, _P]),
     "hm_decode_attn": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P, _I, _P, _I, _P]),
     "hm_decode_attn_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "hm_decode_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),

@@ -194,11 +194,20 @@ __global__ void __launch_bounds__(256) emb_sum_kernel(const int64_t* __restrict_
 // tok_out[:n_keep], pos += 1 for every row, frame counter += 1.
 __global__ void frame_commit_kernel(const int64_t* __restrict__ tok_out, int64_t* __restrict__ tok_in, int B, int ncb,
                                     int64_t* __restrict__ pos, int n_keep, int64_t* __restrict__ stream,
-                                    int64_t* __restrict__ frame, int64_t max_frames) {
+                                    int64_t* __restrict__ frame, int64_t max_frames, int64_t* __restrict__ ends,
+                                    int64_t eos_id) {
   pdl_trigger();
   pdl_wait();
   const int tid = threadIdx.x;
   const int64_t f = *frame;
+  // EOS tracking (generate's scan, app/engine.py:432-437): the first stream frame >= 1 in
+  // which any codebook id of take b is >= eos_id, kept in ends[b] (-1 until then)
+  if (ends && f >= 1)
+    for (int b = tid; b < n_keep; b += blockDim.x) {
+      bool eos = false;
+      for (int j = 0; j < ncb; ++j) eos |= tok_out[b * ncb + j] >= eos_id;
+      if (eos && ends[b] < 0) ends[b] = f;
+    }
   for (int i = tid; i < B * ncb; i += blockDim.x) {
     const int64_t v = tok_out[i];
     tok_in[i] = v;
@@ -276,9 +285,10 @@ extern "C" int hm_emb_sum_i8(const int64_t* tok, int64_t tok_ld, int R, int ncb,
 }
 
 extern "C" int hm_frame_commit(const int64_t* tok_out, int64_t* tok_in, int B, int ncb, int64_t* pos, int n_keep,
-                               int64_t* stream_out, int64_t* frame, int64_t max_frames, int pdl, hm_stream_t stream) {
-  if (!tok_out || !tok_in || !pos || !frame || B < 1 || B > 1024 || ncb < 1) return HM_EARG;
+                               int64_t* stream_out, int64_t* frame, int64_t max_frames, int64_t* ends, int64_t eos_id,
+                               int pdl, hm_stream_t stream) {
+  if (!tok_out || !tok_in || !pos || !frame || B < 1 || B > 1024 || ncb < 1 || n_keep < 0 || n_keep > B) return HM_EARG;
   const cudaError_t e = hm_launch(frame_commit_kernel, dim3(1), dim3(256), 0, stream, pdl, tok_out, tok_in, B, ncb,
-                                  pos, n_keep, stream_out, frame, max_frames);
+                                  pos, n_keep, stream_out, frame, max_frames, ends, eos_id);
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }

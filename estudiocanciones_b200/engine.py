@@ -429,12 +429,12 @@ class FramePlan:
         self.ops.append(lambda st: check(fn(*args, st), "hm_cfg_topk_sample"))
         self.n_kernels += 1
 
-    def commit(self, tok_out, tok_in, pos, n_keep, stream, frame):
+    def commit(self, tok_out, tok_in, pos, n_keep, stream, frame, ends=None):
         self._flush()
         L = _lib.lib()
         B, ncb = tok_out.shape
         args = (tok_out.data_ptr(), tok_in.data_ptr(), B, ncb, pos.data_ptr(), n_keep, _p(stream), frame.data_ptr(),
-                0 if stream is None else stream.shape[0], self.pdl)
+                0 if stream is None else stream.shape[0], _p(ends), AUDIO_EOS, self.pdl)
         fn = L.hm_frame_commit
         self.ops.append(lambda st: check(fn(*args, st), "hm_frame_commit"))
         self.n_kernels += 1
@@ -623,6 +623,7 @@ class HeartMuLaLite:
         rt.draw_noise = not fixed_noise
         rt.stream_out.zero_()
         rt.frame.zero_()
+        rt.ends.fill_(-1)
         rt.pos.fill_(P)
         plan0 = rt.plan_for(cfg_scale, topk, temperature, with_backbone=False, commit=True)
         plan0.run()            # first frame from the prompt's last hidden state
@@ -640,11 +641,12 @@ class HeartMuLaLite:
                 rt.plan_for(cfg_scale, topk, temperature, with_backbone=True, commit=True).run()
             cur = i + 1
             if (i + 1) % check_every == 0 or i == n_frames - 1:
-                a = max(1, i + 2 - check_every)
-                eos = (rt.stream_out[a:i + 2] >= AUDIO_EOS).any(-1).cpu()
+                # the frame commit tracks each take's first EOS frame on the device (the
+                # reference scans out[a:i+2] here): read N integers
+                dev_ends = rt.ends.tolist()
                 for c in range(N):
-                    if ends[c] is None and eos[:, c].any():
-                        ends[c] = a + int(eos[:, c].nonzero()[0, 0])
+                    if ends[c] is None and dev_ends[c] >= 0:
+                        ends[c] = dev_ends[c]
                 if stop_at_eos and all(e is not None for e in ends):
                     last = i + 1
                     break
@@ -680,6 +682,7 @@ class _Runtime:
         self.max_frames = L
         self.stream_out = torch.zeros(L, N, m.n_cb, dtype=torch.long, device=dev)
         self.frame = torch.zeros(1, dtype=torch.long, device=dev)
+        self.ends = torch.full((N,), -1, dtype=torch.long, device=dev)  # first EOS frame per take (device)
         self.nsplit = default_nsplit(B, m.backbone.blocks[0].kvh, L)
         self.plans = {}
         self.graphs = {}
@@ -728,11 +731,12 @@ class _Runtime:
             plan = self.plan_for(cfg, topk, temp, with_backbone=True, commit=True)
             # one eager warm-up frame (as the reference's _capture does, app/engine.py:450-456);
             # it writes the cache slot at the current position, which the replay rewrites
-            saved = (self.tok_in.clone(), self.pos.clone(), self.frame.clone())
+            saved = (self.tok_in.clone(), self.pos.clone(), self.frame.clone(), self.ends.clone())
             plan.run()
             self.tok_in.copy_(saved[0])
             self.pos.copy_(saved[1])
             self.frame.copy_(saved[2])
+            self.ends.copy_(saved[3])
             g = torch.cuda.CUDAGraph()
             s = torch.cuda.Stream(device=self.m.dev)
             s.wait_stream(torch.cuda.current_stream())
@@ -743,6 +747,7 @@ class _Runtime:
             self.tok_in.copy_(saved[0])
             self.pos.copy_(saved[1])
             self.frame.copy_(saved[2])
+            self.ends.copy_(saved[3])
             self.graphs[key] = g
         return g
 
@@ -801,5 +806,5 @@ class _Runtime:
                        keep=head_keep)
             sample(c, self.noise[c])
         if commit:
-            plan.commit(self.tok_out, self.tok_in, self.pos, N, self.stream_out, self.frame)
+            plan.commit(self.tok_out, self.tok_in, self.pos, N, self.stream_out, self.frame, self.ends)
         return plan

@@ -151,11 +151,15 @@ int hm_emb_sum_i8(const int64_t* tok, int64_t tok_ld, int R, int ncb, int64_t vo
                   const void* scale, int64_t rows, int D, void* x_out, float* ss_out, int64_t ss_ld, int* err, int pdl,
                   hm_stream_t stream);
 
-/* End of one decode frame (the bookkeeping of generate's loop, app/engine.py:419-431,
+/* End of one decode frame (the bookkeeping of generate's loop, app/engine.py:419-437,
  * kept on the device): tok_in <- tok_out, stream[frame] <- tok_out[:n_keep],
- * pos[b] += 1, frame += 1.  tok_* are int64 [B, ncb]; stream int64 [max_frames, n_keep, ncb]. */
+ * pos[b] += 1, frame += 1.  tok_* are int64 [B, ncb]; stream int64 [max_frames, n_keep, ncb].
+ * EOS tracking (ends may be NULL): ends[b] (int64 [n_keep], -1 = none yet) <- frame, the
+ * first stream frame >= 1 in which any id of take b is >= eos_id (the reference's EOS scan
+ * of out[1:], AUDIO_EOS = 8193), so the host reads n_keep integers instead of scanning. */
 int hm_frame_commit(const int64_t* tok_out, int64_t* tok_in, int B, int ncb, int64_t* pos, int n_keep,
-                    int64_t* stream_out, int64_t* frame, int64_t max_frames, int pdl, hm_stream_t stream);
+                    int64_t* stream_out, int64_t* frame, int64_t max_frames, int64_t* ends, int64_t eos_id, int pdl,
+                    hm_stream_t stream);
 
 /* ------------------------------------------------------------------ decode attention
  * _attn + _attn_combine (app/kernels.py:112-167): row r of batch r/S attends
