@@ -50,7 +50,7 @@ def args_():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn", "sampler", "prefill"],
+    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn", "sampler", "prefill", "q8"],
                     help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures")
     ap.add_argument("--layers", type=int, default=4, help="backbone layers of the small cases")
     ap.add_argument("--prefill-layers", type=int, default=28, help="backbone layers of the prefill case")
@@ -435,6 +435,33 @@ def run_prefill_case(a, bb_layers=None):
                       "flop": fl}), flush=True)
 
 
+def run_q8_case(a):
+    """Checkpoint conversion: hm_q8_rows on the largest matrix of the converter (the
+    fp32 text-embedding table, 128256 x 3072), timed with CUDA events; bytes = fp32
+    read + int8 write + bf16 scales, against the measured HBM copy bandwidth."""
+    from estudiocanciones_b200 import convert
+    dev = torch.device("cuda", 0)
+    N, K = 128256, 3072
+    x = torch.randn(N, K, generator=torch.Generator(device=dev).manual_seed(0), device=dev) * 0.02
+    for _ in range(3):
+        convert.q8_rows(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.reps):
+        convert.q8_rows(x)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.reps
+    nbytes = N * K * 4 + N * K + N * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    peak, kind = peaks()
+    print(json.dumps({"case": "q8", "rows": N, "cols": K, "ms": round(ms, 3), "GBps": round(gbs, 1),
+                      "frac": round(gbs / peak, 3), "peak_GBps": peak, "peak_kind": kind,
+                      "note": "inputs (1.58 GB) exceed L2; each launch reads every row once from HBM"}),
+          flush=True)
+
+
 def run_case(a):
     """Small single-kernel cases for profiling: the GEMV launches of a few backbone
     layers (weights > L2 but well under a GB), one decode-attention launch at the
@@ -502,6 +529,9 @@ def main():
     a = args_()
     if a.case == "prefill":
         run_prefill_case(a, bb_layers=a.prefill_layers)
+        return
+    if a.case == "q8":
+        run_q8_case(a)
         return
     if a.case != "frame":
         run_case(a)

@@ -16,6 +16,7 @@ HM_SRC_F16, HM_SRC_RMS, HM_SRC_EMB = 0, 1, 2
 HM_EPI_STORE, HM_EPI_ROPE_KV, HM_EPI_SILU = 0, 1, 2
 HM_ERR_TIMEOUT, HM_ERR_BADINDEX = 1, 2
 HM_EARG = -1
+HM_DT_F32, HM_DT_BF16, HM_DT_F16 = 0, 1, 2
 HM_ENOSPACE = -2
 
 # Every exported symbol of include/heartmula_b200.h with (restype, argtypes).
@@ -56,6 +57,7 @@ SIGNATURES = {
     "hm_emb_gather_i8": (_I, [_P, _I, _P, _P, _I64, _I, _P, _P, _P]),
     "hm_emb_sum_i8": (_I, [_P, _I64, _I, _I, _I64, _P, _P, _I64, _I, _P, _P, _I64, _P, _I, _P]),
     "hm_frame_commit": (_I, [_P, _P, _I, _I, _P, _I, _P, _P, _I64, _P, _I64, _I, _P]),
+    "hm_q8_rows": (_I, [_P, _I, _I64, _I64, _I64, _P, _I64, _P, _P]),
     "hm_decode_attn": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P, _I, _P, _I, _P]),
     "hm_decode_attn_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "hm_decode_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),

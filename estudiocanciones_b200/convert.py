@@ -1,0 +1,99 @@
+"""Checkpoint converter: official HeartMuLa weights -> the int8 checkpoint format the
+engine loads (``app/convert_final.py:24-47``, ``convert_mula``), with the per-row int8
+quantisation (``q8_rows``, ``app/convert_final.py:17-21``) done by the ``hm_q8_rows``
+kernel and the shards read straight onto the GPU.
+
+Format (unchanged from the reference): every 2-D tensor except
+``unconditional_text_embedding.weight`` (and, with ``keep_emb``, the embedding tables)
+becomes ``<key>.q8`` int8 ``[N, K]`` + ``<key>.s8`` bf16 ``[N]``; ``audio_head``
+``[heads, D, V]`` becomes ``audio_head.<i>.q8`` ``[V, D]`` / ``.s8`` per head; the RoPE
+``pos_embeddings`` and ``muq_linear.weight`` are dropped (the table is recomputed, the
+MuQ input is always zero so only the bias counts); everything else is stored as bf16.
+
+    python -m estudiocanciones_b200.convert <HeartMuLa dir> <out.safetensors> [--keep-emb-bf16]
+"""
+from __future__ import annotations
+
+import json
+import sys
+from pathlib import Path
+
+import torch
+
+from . import _lib
+from ._lib import HMError, check
+
+_DT = {torch.float32: _lib.HM_DT_F32, torch.bfloat16: _lib.HM_DT_BF16, torch.float16: _lib.HM_DT_F16}
+
+
+def q8_rows(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row symmetric int8 quantisation of a 2-D CUDA tensor (fp32 / bf16 / fp16; other
+    floating types are read as fp32) on the current stream.  Returns (int8 ``[N, K]``,
+    bf16 scales ``[N]``) on the tensor's device, bit-identical to the converter's."""
+    if not t.is_cuda:
+        raise HMError("q8_rows runs on CUDA tensors (hm_q8_rows)")
+    if t.dim() != 2 or t.shape[0] < 1 or t.shape[1] < 1:
+        raise HMError(f"q8_rows wants a non-empty 2-D tensor, got {tuple(t.shape)}")
+    if t.dtype not in _DT:
+        t = t.float()
+    if t.stride(1) != 1:
+        t = t.contiguous()
+    N, K = t.shape
+    q = torch.empty(N, K, dtype=torch.int8, device=t.device)
+    s = torch.empty(N, dtype=torch.bfloat16, device=t.device)
+    st = torch.cuda.current_stream(t.device).cuda_stream
+    check(_lib.lib().hm_q8_rows(t.data_ptr(), _DT[t.dtype], N, K, t.stride(0), q.data_ptr(), K, s.data_ptr(), st),
+          "hm_q8_rows")
+    return q, s
+
+
+def shard_files(d) -> list[Path]:
+    """The safetensors shards of a checkpoint directory (``app/convert_final.py:24-29``):
+    those named by ``model.safetensors.index.json``, else ``model.safetensors``."""
+    d = Path(d)
+    idx = d / "model.safetensors.index.json"
+    if idx.exists():
+        return [d / name for name in sorted(set(json.loads(idx.read_text())["weight_map"].values()))]
+    return [d / "model.safetensors"]
+
+
+def convert_tensors(src, keep_emb: bool = False, device="cuda", quant=None) -> dict[str, torch.Tensor]:
+    """Converted tensors (on the host) of the checkpoint directory ``src``.  ``quant``
+    replaces the quantiser (default: :func:`q8_rows` on ``device``)."""
+    from safetensors import safe_open
+    quant = quant or q8_rows
+    out: dict[str, torch.Tensor] = {}
+    for sh in shard_files(src):
+        with safe_open(str(sh), "pt", device=str(device)) as f:
+            for k in f.keys():
+                if "pos_embeddings" in k or k == "muq_linear.weight":
+                    continue
+                t = f.get_tensor(k)
+                if k == "audio_head":  # [heads, D, V]: one [V, D] matrix per head
+                    for i in range(t.shape[0]):
+                        q, s = quant(t[i].t().contiguous())
+                        out[f"audio_head.{i}.q8"], out[f"audio_head.{i}.s8"] = q.cpu(), s.cpu()
+                elif t.dim() == 2 and k != "unconditional_text_embedding.weight" and not (
+                        keep_emb and "embeddings" in k):
+                    q, s = quant(t)
+                    out[k + ".q8"], out[k + ".s8"] = q.cpu(), s.cpu()
+                else:
+                    out[k] = t.to(torch.bfloat16).contiguous().cpu()
+    return out
+
+
+def convert_mula(src, dst, keep_emb: bool = False, device="cuda", quant=None) -> list[str]:
+    """Write the int8 checkpoint of ``src`` to ``dst``; returns its keys."""
+    from safetensors.torch import save_file
+    out = convert_tensors(src, keep_emb=keep_emb, device=device, quant=quant)
+    save_file(out, str(dst), metadata={"lite": json.dumps({"mode": "int8"})})
+    return sorted(out)
+
+
+if __name__ == "__main__":
+    if len(sys.argv) < 3:
+        raise SystemExit(__doc__)
+    dst = Path(sys.argv[2])
+    dst.parent.mkdir(parents=True, exist_ok=True)
+    convert_mula(sys.argv[1], dst, "--keep-emb-bf16" in sys.argv)
+    print(dst.name, round(dst.stat().st_size / 1e9, 2), "GB")

@@ -35,6 +35,11 @@ typedef struct CUstream_st* hm_stream_t; /* == cudaStream_t */
 #define HM_ENOSPACE (-2) /* the request needs more than a fixed space holds (hm_decode_attn_noalloc's scratch
                             array, a stage sequence's shared-memory activation region) */
 
+/* element types of hm_q8_rows' input */
+#define HM_DT_F32 0
+#define HM_DT_BF16 1
+#define HM_DT_F16 2
+
 /* device error-word bits */
 #define HM_ERR_TIMEOUT 1   /* a bounded wait gave up */
 #define HM_ERR_BADINDEX 2  /* token id / position outside its table; access skipped */
@@ -157,6 +162,14 @@ int hm_emb_sum_i8(const int64_t* tok, int64_t tok_ld, int R, int ncb, int64_t vo
  * EOS tracking (ends may be NULL): ends[b] (int64 [n_keep], -1 = none yet) <- frame, the
  * first stream frame >= 1 in which any id of take b is >= eos_id (the reference's EOS scan
  * of out[1:], AUDIO_EOS = 8193), so the host reads n_keep integers instead of scanning. */
+/* ------------------------------------------------------------------ checkpoint conversion
+ * q8_rows of the converter (app/convert_final.py:17-21) on the GPU: x [N, K] (row pitch
+ * ldx elements, type HM_DT_*) -> q int8 [N, K] (row pitch ldq), s bf16 [N] with
+ * s[r] = max(max|x[r]|, 1e-8) / 127 and q = clamp(round_half_even(x / s), -127, 127);
+ * bit-identical to the converter's torch arithmetic. */
+int hm_q8_rows(const void* x, int dtype, int64_t N, int64_t K, int64_t ldx, int8_t* q, int64_t ldq, void* s,
+               hm_stream_t stream);
+
 int hm_frame_commit(const int64_t* tok_out, int64_t* tok_in, int B, int ncb, int64_t* pos, int n_keep,
                     int64_t* stream_out, int64_t* frame, int64_t max_frames, int64_t* ends, int64_t eos_id, int pdl,
                     hm_stream_t stream);

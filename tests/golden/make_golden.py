@@ -17,6 +17,12 @@ It imports the reference's ``kernels.py`` and ``engine.py`` unmodified and
   prompt prefill plus decode frames, once through the CPU path and once through
   the Triton fast path (interpreter) -> ``model_cpu.npz`` / ``model_fast.npz``.
 
+* runs the checkpoint converter's ``q8_rows`` (``convert_final.py``) on seeded and
+  hand-made rows (ties, zero and tiny rows, bf16 / fp16 inputs, an ``audio_head``
+  block) -> ``q8_rows.npz``.  It calls ``.cuda()`` on its input; with no GPU in
+  the generating container that call is made an identity for the duration, so
+  the same fp32 arithmetic runs on the CPU.
+
 The fixtures hold inputs and outputs; the tiny checkpoint is regenerated in the
 tests from its seed, and its SHA-256 is stored to catch any drift.
 """
@@ -265,14 +271,57 @@ def gen_model(E, K, fast: bool, n_frames: int = 1):
     return out
 
 
+# ----------------------------------------------------------------------------- converter
+def q8_cases():
+    """Inputs of the q8_rows fixture: name -> 2-D tensor."""
+    g = torch.Generator().manual_seed(11)
+    ties = torch.tensor([[127.0, 2.5, -3.5, 0.5, -0.5, 1.5, 126.5, -127.0, 0.0, -1.5, 3.5, 64.5]])
+    tiny = torch.tensor([[1e-9, -3e-9, 5e-10, 0.0], [0.0, 0.0, 0.0, 0.0]])
+    mixed = torch.randn(6, 37, generator=g)
+    mixed[2] = 0.0
+    mixed[4] *= 1e4
+    return {
+        "f32_ties": ties,
+        "f32_tiny_zero": tiny,
+        "f32_mixed": mixed,
+        "f32_wide": torch.randn(3, 3072, generator=g) * 0.05,
+        "bf16": (torch.randn(5, 64, generator=g) * 3).to(torch.bfloat16),
+        "f16": (torch.randn(2, 48, generator=g) * 0.1).to(torch.float16),
+        "audio_head": torch.randn(2, 16, 24, generator=g),  # [heads, D, V], quantised per head as [V, D]
+    }
+
+
+def gen_q8(C):
+    cuda0 = torch.Tensor.cuda
+    torch.Tensor.cuda = lambda self, *a, **k: self  # no GPU here: the same fp32 arithmetic on the CPU
+    try:
+        out = {}
+        for name, t in q8_cases().items():
+            out[f"{name}.x"] = t.float().numpy()
+            out[f"{name}.dtype"] = np.array(str(t.dtype))
+            mats = [t[i].t().contiguous() for i in range(t.shape[0])] if name == "audio_head" else [t]
+            for j, m in enumerate(mats):
+                q, s = C.q8_rows(m)
+                out[f"{name}.{j}.q"] = q.numpy()
+                out[f"{name}.{j}.s"] = s.view(torch.int16).numpy()  # bf16 bits
+        return out
+    finally:
+        torch.Tensor.cuda = cuda0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HEARTMULA_REF_APP", ""), help="reference app/ directory")
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--only", default="", help="'q8': write q8_rows.npz only")
     a = ap.parse_args()
     if not a.ref or not Path(a.ref, "engine.py").exists():
         raise SystemExit("pass --ref <reference app dir>")
     sys.path.insert(0, a.ref)
+    import convert_final as C
+    np.savez_compressed(Path(a.out, "q8_rows.npz"), **gen_q8(C))
+    if a.only == "q8":
+        return
     import kernels as K
     import engine as E
     torch.set_num_threads(8)
