@@ -7,7 +7,9 @@ stream as the raw ``cudaStream_t`` handle of the current torch stream.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
+import gc
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libheartmula_b200.so"
@@ -99,6 +101,20 @@ def lib() -> C.CDLL:
             fn.argtypes = args
         _lib = L
     return _lib
+
+
+@contextlib.contextmanager
+def capture_no_gc():
+    """Python's cyclic collector stays off while a CUDA graph is captured: a collection
+    there could destroy a dead graph, whose memory pool then returns device memory
+    (cudaFree), and that invalidates the capture in progress."""
+    was_on = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was_on:
+            gc.enable()
 
 
 def check(rc: int, what: str) -> None:

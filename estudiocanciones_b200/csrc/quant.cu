@@ -58,7 +58,6 @@ __global__ void __launch_bounds__(kQThreads) q8_rows_kernel(const T* __restrict_
     int8_t* qr = q + r * ldq;
     float m = 0.f;
     if (VEC) {
-#pragma unroll 4
       for (int64_t k = 4 * (int64_t)tid; k < K; k += 4 * kQThreads) {
         float v[4];
         load4<T>(xr + k, v);
@@ -76,7 +75,6 @@ __global__ void __launch_bounds__(kQThreads) q8_rows_kernel(const T* __restrict_
     for (int w = 1; w < kQThreads / 32; ++w) amax = fmaxf(amax, wmax[w]);
     const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
     if (VEC) {
-#pragma unroll 4
       for (int64_t k = 4 * (int64_t)tid; k < K; k += 4 * kQThreads) {
         float v[4];
         load4<T>(xr + k, v);

@@ -26,6 +26,7 @@ from pathlib import Path
 import torch
 
 from . import _lib, kernels
+from ._lib import capture_no_gc as _capture_no_gc
 from ._lib import GemvDesc, RowSrc, check, HM_EPI_STORE, HM_EPI_ROPE_KV, HM_EPI_SILU, HM_SRC_F16, HM_SRC_RMS, HM_SRC_EMB
 from .checkpoint import (AUDIO_EOS, AUDIO_VOCAB, FRAME_MS, N_CB, TEXT_BOS, TEXT_EOS, load_tensors,
                          shape_from_tensors)
@@ -484,21 +485,26 @@ class HeartMuLaLite:
     # ------------------------------------------------------------------ runtime state
     def alloc(self, n_takes, B, L):
         """Caches (``app/engine.py:386-388``), frame buffers and the frame plan."""
+        self._drop_runtime()
         self.N, self.B = n_takes, B
         self.backbone.alloc(B, L, self.dev)
         self.decoder.alloc(B, self.n_cb, self.dev)
         self._rt = _Runtime(self, n_takes, B)
 
-    def release(self):
-        """Free caches, graphs and buffers (``app/engine.py:463-469``)."""
+    def _drop_runtime(self):
+        """Destroy the current runtime's graphs and plans now.  The plans' operations close
+        over the runtime (a reference cycle), so without this its graphs and buffers would
+        go whenever the cyclic collector next runs -- possibly during another capture."""
         rt = self._rt
         if rt is not None:
-            # the plans' operations close over the runtime (a reference cycle): clear them so
-            # the graphs and buffers go now, not whenever the cyclic collector next runs
             rt.graphs.clear()
             rt.plans.clear()
-        self.graphs.clear()
         self._rt = None
+
+    def release(self):
+        """Free caches, graphs and buffers (``app/engine.py:463-469``)."""
+        self._drop_runtime()
+        self.graphs.clear()
         self.backbone.free()
         self.decoder.free()
         torch.cuda.empty_cache()
@@ -561,7 +567,7 @@ class HeartMuLaLite:
             g = torch.cuda.CUDAGraph()
             st = torch.cuda.Stream(device=self.dev)
             st.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(st):
+            with torch.cuda.stream(st), _capture_no_gc():
                 with torch.cuda.graph(g, stream=st):
                     plan.run()
             torch.cuda.current_stream().wait_stream(st)
@@ -740,7 +746,7 @@ class _Runtime:
             g = torch.cuda.CUDAGraph()
             s = torch.cuda.Stream(device=self.m.dev)
             s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
+            with torch.cuda.stream(s), _capture_no_gc():
                 with torch.cuda.graph(g, stream=s):
                     plan.run()
             torch.cuda.current_stream().wait_stream(s)
