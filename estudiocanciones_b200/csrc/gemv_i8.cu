@@ -962,22 +962,28 @@ cudaError_t launch_grid(const CUtensorMap& map, const GemvParams& p, int J, int 
   return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<MT, EPI, GR>, map, p);
 }
 
-// The wide kernel (8 rows, one k-range): one CTA per SM, as many consumer groups as the
-// SM has tiles (up to four), each with the deepest ring that fits.  Returns false when
-// the shape does not fit it (the narrow kernel runs instead).
-template <int EPI>
+// Consumer groups of the wide kernel: four at 8 rows; three at 16 rows, whose MMA loop
+// needs more registers than a 17-warp CTA leaves per thread.
+template <int MT>
+constexpr int wide_groups() { return MT == 1 ? kMaxGroups : 3; }
+
+// The wide kernel (8 or 16 rows, one k-range): one CTA per SM, as many consumer groups
+// as the SM has tiles (up to wide_groups), each with the deepest ring that fits.
+// Returns false when the shape does not fit it (the narrow kernel runs instead).
+template <int MT, int EPI>
 bool wide_shape(GemvParams& p, int* J, int* smem) {
-  if (configure_kernel<1, EPI, kMaxGroups>() != cudaSuccess) return false;  // before the occupancy query
+  constexpr int GRW = wide_groups<MT>();
+  if (configure_kernel<MT, EPI, GRW>() != cudaSuccess) return false;  // before the occupancy query
   const int nsm = sm_count();
   *J = std::min(p.ntiles, nsm);
-  for (int G = std::min(kMaxGroups, (p.ntiles + *J - 1) / *J); G >= 1; --G) {
+  for (int G = std::min(GRW, (p.ntiles + *J - 1) / *J); G >= 1; --G) {
     int n = kMaxNST;
-    while (n >= 2 && smem_layout(p.kspan, 8, p.has_gamma, p.xcontig, n, G).total > 227 * 1024) --n;
+    while (n >= 2 && smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, n, G).total > 227 * 1024) --n;
     if (n < 2) continue;
     int occ = 0;
-    const int sm = smem_layout(p.kspan, 8, p.has_gamma, p.xcontig, n, G).total;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<1, EPI, kMaxGroups>,
-                                                      threads_of(kMaxGroups), sm) != cudaSuccess ||
+    const int sm = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, n, G).total;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_i8_kernel<MT, EPI, GRW>,
+                                                      threads_of(GRW), sm) != cudaSuccess ||
         occ < 1)
       return false;
     p.groups = G;
@@ -1007,14 +1013,16 @@ cudaError_t launch_one(const CUtensorMap& map, const GemvParams& p0, cudaStream_
   choose_occupancy<MT, EPI>(p, &per_sm, &p.nst);
   // HM_GEMV_WIDE: 1 (default) the wide kernel when the narrow one cannot give every tile
   // its own CTA (some CTAs would stream a second tile after their first), 2 for every
-  // 8-row launch with one k-range, 0 never.  (A wide CTA cannot share its SM with the
-  // previous launch's tail, so short launches that fit the narrow kernel keep it.)
+  // 8- or 16-row launch with one k-range, 0 never.  (A wide CTA cannot share its SM with
+  // the previous launch's tail, so short launches that fit the narrow kernel keep it.)
   static const int wide = static_cast<int>(env_or("HM_GEMV_WIDE", 1));
-  if (MT == 1 && p.nsplit == 1 && !p.cluster &&
-      (wide == 2 || (wide == 1 && p.ntiles > per_sm * sm_count()))) {
-    GemvParams q = p;
-    int J = 0, smem = 0;
-    if (wide_shape<EPI>(q, &J, &smem)) return launch_grid<1, EPI, kMaxGroups>(map, q, J, smem, st);
+  if constexpr (MT <= 2) {
+    if (p.nsplit == 1 && !p.cluster && (wide == 2 || (wide == 1 && p.ntiles > per_sm * sm_count()))) {
+      GemvParams q = p;
+      int J = 0, smem = 0;
+      if (wide_shape<MT, EPI>(q, &J, &smem))
+        return launch_grid<MT, EPI, wide_groups<MT>()>(map, q, J, smem, st);
+    }
   }
   const int smem = smem_layout(p.kspan, 8 * MT, p.has_gamma, p.xcontig, p.nst).total;
   int J = per_sm * sm_count() / p.nsplit;

@@ -463,10 +463,11 @@ def kernels_errors():
 
 
 # ----------------------------------------------------------------------------- wide GEMV kernel (backbone shapes)
-@pytest.mark.parametrize("M", [8, 5])
+@pytest.mark.parametrize("M", [8, 5, 16, 12])
 def test_gemv_wide_silu_backbone_shape(M):
     """w1|w3 of the backbone (N 2 x 8192, K 3072: 512 tiles, more than the narrow kernel
-    has CTAs) runs on the wide kernel: RMSNorm prologue + SiLU epilogue vs the oracle."""
+    has CTAs) runs on the wide kernel (four consumer groups at 8 rows, three at 16):
+    RMSNorm prologue + SiLU epilogue vs the oracle."""
     from estudiocanciones_b200.engine import Linear
     gen = torch.Generator().manual_seed(31 + M)
     D, F = 3072, 8192
@@ -487,17 +488,18 @@ def test_gemv_wide_silu_backbone_shape(M):
     close16(y, ref, ulps=3, frac_exact=0.9, slack=2 * (sl[:, :F] * a[:, F:].float().abs() + sl[:, F:]))
 
 
-def test_gemv_wide_rope_backbone_shape():
+@pytest.mark.parametrize("R", [8, 16])
+def test_gemv_wide_rope_backbone_shape(R):
     """qkv of the backbone (N 5120, K 3072: 320 tiles) on the wide kernel: RoPE + KV-cache
     write epilogue vs the oracle; cache slots nobody writes stay untouched."""
     from estudiocanciones_b200.engine import Block, Linear
-    gen = torch.Generator().manual_seed(41)
-    Hq, Hk, hd, D, L, R = 24, 8, 128, 3072, 64, 8
+    gen = torch.Generator().manual_seed(41 + R)
+    Hq, Hk, hd, D, L = 24, 8, 128, 3072, 64
     x = torch.randn(R, D, generator=gen).half()
     gamma = (1 + 0.1 * torch.randn(D, generator=gen)).half()
     N = (Hq + 2 * Hk) * hd
     w, s = rand_lin(N, D, gen)
-    pos = torch.tensor([0, 1, 5, 17, 33, 62, 63, 40])
+    pos = torch.tensor([0, 1, 5, 17, 33, 62, 63, 40, 2, 9, 61, 30, 3, 44, 12, 50][:R])
     rope = O.rope_table(hd, L)
     kc0 = torch.randn(R, Hk, L, hd, generator=gen).half()
     vc0 = torch.randn(R, Hk, L, hd, generator=gen).half()
@@ -527,6 +529,26 @@ def test_gemv_wide_rope_backbone_shape():
     idx = mask.nonzero(as_tuple=True)
     assert torch.equal(blk.kc.cpu().permute(0, 2, 1, 3)[idx], kc0.permute(0, 2, 1, 3)[idx])
     assert torch.equal(blk.vc.cpu().permute(0, 2, 1, 3)[idx], vc0.permute(0, 2, 1, 3)[idx])
+
+
+def test_gemv_wide_store_codebook0_head_16_rows():
+    """The codebook-0 head at 16 rows (N 8197, K 3072: 513 tiles, the last one ragged)
+    on the three-group wide kernel: RMSNorm prologue, plain store."""
+    from estudiocanciones_b200.engine import Linear
+    gen = torch.Generator().manual_seed(47)
+    M, D, N = 16, 3072, 8197
+    x = torch.randn(M, D, generator=gen).half()
+    gamma = (1 + 0.1 * torch.randn(D, generator=gen)).half()
+    w, s = rand_lin(N, D, gen)
+    lin = Linear(w.to(DEV), s.to(DEV))
+    xd, gd = x.to(DEV), gamma.to(DEV)
+    y = torch.empty(M, N, dtype=torch.float16, device=DEV)
+    p = _plan()
+    p._gemv(lin, M, p.src_rms(xd, _ss(xd), gd), y=y)
+    p.run()
+    xn = O.rmsnorm(x, gamma)
+    ref = O.gemv_i8(xn, w, s)
+    close16(y, ref, ulps=2, frac_exact=0.9, slack=rms_slack(xn, w, s, ref))
 
 
 def test_gemv_wide_store_residual_backbone_w2_shape():
