@@ -56,6 +56,13 @@ def test_host_argument_validation_without_gpu(lib):
                               0, None) == -1
     assert lib.hm_cfg_topk_sample(None, 0, 2, 1, 8197, None, 0, 1.5, 50, 1.0, None, 0, 0, None, 0, None) == -1
     assert lib.hm_rmsnorm(None, None, None, 1, 16, 1e-5, None) == -1
+    # frame commit: n_keep beyond the rows; checkpoint quantisation: null / short rows / bad type
+    assert lib.hm_frame_commit(1, 1, 2, 8, 1, 3, None, 1, 0, None, 8193, 0, None) == -1
+    assert lib.hm_q8_rows(None, 0, 4, 16, 16, 1, 16, 1, None) == -1
+    assert lib.hm_q8_rows(1, 0, 4, 16, 8, 1, 16, 1, None) == -1      # ldx < K
+    assert lib.hm_q8_rows(1, 0, 4, 16, 16, 1, 8, 1, None) == -1      # ldq < K
+    assert lib.hm_q8_rows(1, 9, 4, 16, 16, 1, 16, 1, None) == -1     # no such element type
+    assert lib.hm_q8_rows(1, 0, 0, 16, 16, 1, 16, 1, None) == -1     # no rows
 
 
 def test_workspace_sizing_is_consistent(lib):
