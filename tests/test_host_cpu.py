@@ -55,3 +55,29 @@ def test_default_attention_split():
     assert default_nsplit(1, 8, 768, sms=148) == 12
     assert default_nsplit(1, 8, 8192, sms=148) == 37
     assert default_nsplit(8, 2, 8, sms=148) == 1
+
+
+def test_graph_capture_keeps_the_cyclic_collector_off():
+    """Graph captures run with Python's cyclic collector off (a collection inside one could
+    destroy a dead graph and invalidate the capture); its previous state comes back, also
+    when the captured code raises."""
+    import gc
+    from estudiocanciones_b200._lib import capture_no_gc
+    was = gc.isenabled()
+    try:
+        gc.enable()
+        with capture_no_gc():
+            assert not gc.isenabled()
+        assert gc.isenabled()
+        try:
+            with capture_no_gc():
+                raise RuntimeError("capture failed")
+        except RuntimeError:
+            pass
+        assert gc.isenabled()
+        gc.disable()
+        with capture_no_gc():
+            assert not gc.isenabled()
+        assert not gc.isenabled()  # a caller that had it off keeps it off
+    finally:
+        (gc.enable if was else gc.disable)()
