@@ -605,15 +605,23 @@ class HeartMuLaLite:
     @torch.inference_mode()
     def generate_ids(self, text, muq_idx, *, max_ms=60_000, temperature=1.0, topk=50, cfg_scale=1.5, seed=None,
                      use_graphs=True, progress=None, abort=None, n=1, check_every=25, stop_at_eos=True,
-                     fixed_noise=False):
+                     fixed_noise=False, teacher=None, keep_state=False):
         """``generate`` from prompt token ids (host or device int64 ``[P]``).
         ``fixed_noise`` replaces the exponential noise by ones (greedy within top-k),
-        which makes runs independent of the random stream (tests)."""
+        which makes runs independent of the random stream (tests).
+
+        Parity harness (tests): ``teacher`` ``[n_frames + 1, B, n_cb]`` int64 replaces the
+        sampled ids of frame f by ``teacher[f]`` (looked up with the device frame counter,
+        so the graph path is forced too) and records every head's logits in
+        ``self.teacher_logits`` ``[(n_frames + 1) * n_cb, B, V]``; ``keep_state`` keeps the
+        caches and buffers after the call instead of releasing them."""
         if seed is not None and seed >= 0:
             torch.manual_seed(seed)
         N = n
         B = 2 * N if cfg_scale != 1.0 else N
         P = int(text.numel())
+        if P < 1:
+            raise _lib.HMError("generate needs a prompt of at least one token")
         n_frames = max_ms // FRAME_MS
         L = P + n_frames + 2
         self.alloc(N, B, L + 256)
@@ -627,13 +635,23 @@ class HeartMuLaLite:
             h[N:] = self.uncond[0]
         prefill_backbone(self, h)
         rt.draw_noise = not fixed_noise
+        forced = teacher is not None
+        if forced:
+            tf = teacher.to(self.dev).long()
+            if tf.dim() != 3 or tf.shape[0] < n_frames + 1 or tf.shape[1] != B or tf.shape[2] != self.n_cb:
+                raise _lib.HMError(f"teacher ids must be [n_frames + 1, {B}, {self.n_cb}]")
+            rt.force_tab = tf.contiguous()
+            rt.rec_tab = torch.zeros(tf.shape[0] * self.n_cb, B, self.vocab, dtype=torch.float16, device=self.dev)
         rt.stream_out.zero_()
         rt.frame.zero_()
         rt.ends.fill_(-1)
-        rt.pos.fill_(P)
-        plan0 = rt.plan_for(cfg_scale, topk, temperature, with_backbone=False, commit=True)
+        # The first frame comes from the prompt's last hidden state and writes no backbone
+        # cache slot; its commit advances every position by one, so it starts at P - 1 and
+        # the first backbone step runs at P (the reference's cur_pos = P, app/engine.py:403,420).
+        rt.pos.fill_(P - 1)
+        plan0 = rt.plan_for(cfg_scale, topk, temperature, with_backbone=False, commit=True, teacher=forced)
         plan0.run()            # first frame from the prompt's last hidden state
-        g = rt.graph_for(cfg_scale, topk, temperature) if use_graphs else None
+        g = rt.graph_for(cfg_scale, topk, temperature, teacher=forced) if use_graphs else None
         cur = 0
         ends = [None] * N
         last = n_frames
@@ -644,7 +662,7 @@ class HeartMuLaLite:
             if g is not None:
                 g.replay()
             else:
-                rt.plan_for(cfg_scale, topk, temperature, with_backbone=True, commit=True).run()
+                rt.plan_for(cfg_scale, topk, temperature, with_backbone=True, commit=True, teacher=forced).run()
             cur = i + 1
             if (i + 1) % check_every == 0 or i == n_frames - 1:
                 # the frame commit tracks each take's first EOS frame on the device (the
@@ -663,7 +681,10 @@ class HeartMuLaLite:
         for c in range(N):
             T = ends[c] if ends[c] is not None else last + 1
             res.append(rt.stream_out[:T, c].t().clone())
-        self.release()
+        if forced:
+            self.teacher_logits = rt.rec_tab
+        if not keep_state:
+            self.release()
         return res[0] if n == 1 else res
 
 
@@ -702,6 +723,8 @@ class _Runtime:
         self.persistent = mode not in ("0", "")
         self.persistent_backbone = mode not in ("0", "", "dec")
         self.force = torch.zeros(B, m.n_cb, dtype=torch.long, device=dev)
+        self.force_tab = None   # teacher ids per frame of a forced generate (parity harness)
+        self.rec_tab = None     # every head's logits of a forced generate
         self.rec = torch.zeros(m.n_cb, B, m.vocab, dtype=torch.float16, device=dev)
         self.ctx.reserve(m, B, self.nsplit)
 
@@ -730,11 +753,11 @@ class _Runtime:
             self.plans[key] = p
         return p
 
-    def graph_for(self, cfg, topk, temp):
-        key = (float(cfg), int(topk), float(temp))
+    def graph_for(self, cfg, topk, temp, teacher=False):
+        key = (float(cfg), int(topk), float(temp), bool(teacher))
         g = self.graphs.get(key)
         if g is None:
-            plan = self.plan_for(cfg, topk, temp, with_backbone=True, commit=True)
+            plan = self.plan_for(cfg, topk, temp, with_backbone=True, commit=True, teacher=teacher)
             # one eager warm-up frame (as the reference's _capture does, app/engine.py:450-456);
             # it writes the cache slot at the current position, which the replay rewrites
             saved = (self.tok_in.clone(), self.pos.clone(), self.frame.clone(), self.ends.clone())
@@ -768,8 +791,15 @@ class _Runtime:
             # instead of sampling (the parity harness of the tests)
             def pick(c, *_):
                 def op(c=c):
-                    self.rec[c].copy_(self.logits)
-                    self.tok_out[:, c].copy_(self.force[:, c])
+                    if self.force_tab is not None and commit:
+                        # forced generate: frame f (device counter) takes teacher[f] and its
+                        # logits go to row f * n_cb + c of the record
+                        f = self.frame
+                        self.rec_tab.index_copy_(0, f * m.n_cb + c, self.logits.unsqueeze(0))
+                        self.tok_out[:, c].copy_(self.force_tab.index_select(0, f)[0, :, c])
+                    else:
+                        self.rec[c].copy_(self.logits)
+                        self.tok_out[:, c].copy_(self.force[:, c])
                 plan.torch_op(op)
             sample = pick
         else:

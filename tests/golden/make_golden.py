@@ -271,6 +271,69 @@ def gen_model(E, K, fast: bool, n_frames: int = 1):
     return out
 
 
+# ----------------------------------------------------------------------------- generate
+GEN_LYRICS = "La luna canta sobre el mar\nY el viento baila sin parar"
+GEN_TAGS = "Pop, Acoustic, Female vocal"
+
+
+def gen_generate(E, n_frames: int = 10):
+    """The reference's own ``generate`` (``app/engine.py:374-448``, CPU path, fp16) on a
+    tiny checkpoint with the real text vocabulary, 2 takes x CFG, with every sampled id
+    replaced by a fixed table (teacher forcing through ``_guided``).  Take 0 emits an EOS
+    id at frame 4, so its stream is cut there by the reference's EOS scan; take 1 runs to
+    the end.  Records the prompt ids, the returned streams, every head's logits in call
+    order, and the backbone cache slots around the prompt end (captured when ``generate``
+    releases its buffers)."""
+    from dataclasses import replace
+    from wordtok import WordTokenizer
+    sh = replace(TINY_SHAPE, text_vocab=128256)
+    t = synthetic_tensors(sh, seed=TINY_SEED + 1, gamma_one=False)
+    sha = tensors_sha(t)
+    path = Path("/tmp/heartmula_tiny_gen.safetensors")
+    save_checkpoint(t, path)
+    with _DimPatch(E, sh):
+        m = E.HeartMuLaLite(path, device="cpu", dtype=torch.float16)
+    N, B = 2, 4
+    g = torch.Generator().manual_seed(21)
+    force = torch.randint(0, 8192, (n_frames + 1, N, sh.n_cb), generator=g)
+    force[4, 0, 3] = E.AUDIO_EOS          # take 0 ends at frame 4
+    force[7, 0, 5] = E.AUDIO_EOS + 2      # a later EOS-range id does not move the end
+    force = torch.cat([force, force], 1)  # both CFG halves carry the same ids
+    rec = []
+
+    def guided(self, logits, cfg_, topk_, temp_):
+        rec.append(logits.clone())
+        f, c = divmod(len(rec) - 1, sh.n_cb)
+        return force[f, :, c:c + 1].clone()
+
+    kv = {}
+    release0 = m.release
+
+    def release():
+        for j, b in enumerate((m.backbone.blocks[0], m.backbone.blocks[-1])):
+            kv[f"kc{j}"] = np16(b.kc[:, :, P - 1:P + n_frames + 1])
+            kv[f"vc{j}"] = np16(b.vc[:, :, P - 1:P + n_frames + 1])
+        release0()
+
+    text, muq_idx = m._prompt(GEN_LYRICS, GEN_TAGS, WordTokenizer())
+    P = len(text)
+    guided0 = E.HeartMuLaLite._guided
+    E.HeartMuLaLite._guided = guided
+    m.release = release
+    try:
+        res = m.generate(GEN_LYRICS, GEN_TAGS, WordTokenizer(), max_ms=n_frames * 80, cfg_scale=1.5, topk=50,
+                         temperature=1.0, seed=3, n=N)
+    finally:
+        E.HeartMuLaLite._guided = guided0
+    out = {"sha": np.array(sha), "seed": np.array(TINY_SEED + 1), "text": text.numpy(),
+           "meta": np.array([N, B, P, muq_idx, n_frames]), "force": force.numpy(),
+           "logits": np.stack([np16(x) for x in rec]), "lyrics": np.array(GEN_LYRICS), "tags": np.array(GEN_TAGS)}
+    for c, r in enumerate(res):
+        out[f"stream{c}"] = r.numpy()
+    out.update(kv)
+    return out
+
+
 # ----------------------------------------------------------------------------- converter
 def q8_cases():
     """Inputs of the q8_rows fixture: name -> 2-D tensor."""
@@ -313,7 +376,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HEARTMULA_REF_APP", ""), help="reference app/ directory")
     ap.add_argument("--out", default=str(HERE))
-    ap.add_argument("--only", default="", help="'q8': write q8_rows.npz only")
+    ap.add_argument("--only", default="", help="'q8' / 'generate': write q8_rows.npz / generate.npz only")
     a = ap.parse_args()
     if not a.ref or not Path(a.ref, "engine.py").exists():
         raise SystemExit("pass --ref <reference app dir>")
@@ -324,6 +387,10 @@ def main():
         return
     import kernels as K
     import engine as E
+    sys.path.insert(0, str(HERE))
+    if a.only == "generate":
+        np.savez_compressed(Path(a.out, "generate.npz"), **gen_generate(E))
+        return
     torch.set_num_threads(8)
     np.savez_compressed(Path(a.out, "kernels.npz"), **gen_kernels(K))
     np.savez_compressed(Path(a.out, "sampler.npz"), **gen_sampler(E))
@@ -331,6 +398,7 @@ def main():
     np.savez_compressed(Path(a.out, "model_cpu.npz"), **gen_model(E, K, fast=False, n_frames=1))
     E.HeartMuLaLite._guided = guided0
     np.savez_compressed(Path(a.out, "model_fast.npz"), **gen_model(E, K, fast=True, n_frames=1))
+    np.savez_compressed(Path(a.out, "generate.npz"), **gen_generate(E))
     for f in sorted(Path(a.out).glob("*.npz")):
         print(f.name, f.stat().st_size)
 

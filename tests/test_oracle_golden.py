@@ -131,3 +131,50 @@ def test_teacher_forced_frame_matches_reference_engine(golden, name, mode):
         assert ulp_close(ly.vc[:, :, P - 3:P], t(z[f"vc_pre{j}"]), 1e-2, 1e-2)
         assert ulp_close(ly.kc[:, :, P:P + 1], t(z[f"kc_dec{j}"]), 1e-2, 1e-2)
         assert ulp_close(ly.vc[:, :, P:P + 1], t(z[f"vc_dec{j}"]), 1e-2, 1e-2)
+
+
+def assert_argmax_except_ties(got, ref, tie=4e-3):
+    """Identical argmax wherever the reference's best logit leads its second by more than
+    ``tie``; where it does not (the 10-frame golden holds exact fp16 ties), the chosen id
+    must be within ``tie`` of the reference's best."""
+    top2 = ref.topk(2, -1).values
+    clear = (top2[..., 0] - top2[..., 1]) > tie
+    a, b = got.argmax(-1), ref.argmax(-1)
+    assert torch.equal(a[clear], b[clear])
+    picked = ref.gather(-1, a.unsqueeze(-1)).squeeze(-1)
+    assert bool((picked >= top2[..., 0] - tie).all())
+
+
+def test_forced_generate_golden_matches_oracle_steps(golden):
+    """The reference ``generate`` golden (teacher-forced, 10 frames) against the oracle
+    stepped at positions P, P+1, ...: logits of every head within the parity rule and
+    the backbone cache slots P-1 .. P+10 (the last one untouched).  Pins the fixture that
+    the GPU ``generate`` test compares with, including its position bookkeeping."""
+    from dataclasses import replace
+    z = golden("generate")
+    sh = replace(TINY_SHAPE, text_vocab=128256)
+    tensors = synthetic_tensors(sh, seed=int(z["seed"]), gamma_one=False)
+    assert tensors_sha(tensors) == str(z["sha"])
+    m = O.OracleModel(tensors, bb_heads=sh.bb_heads, dec_heads=sh.dec_heads, mode="cpu", dtype=torch.float16)
+    N, B, P, muq_idx, n_frames = (int(v) for v in z["meta"])
+    force = t(z["force"])
+    m.alloc(B, P + n_frames + 2 + 256)
+    hb = m.prefill(m.prompt_embed(t(z["text"]), N, muq_idx))
+    rec = []
+    ones = [torch.ones(N, m.vocab)] * m.n_cb
+    tok = m.frame(hb[:, -1], N, 1.5, 50, 1.0, force=force[0], record=rec, noise=ones)
+    for f in range(n_frames):
+        tok = m.step(tok, torch.full((B, 1), P + f, dtype=torch.long), N, 1.5, 50, 1.0, force=force[f + 1],
+                     record=rec, noise=ones)
+    got, ref = torch.stack(rec).float(), t(z["logits"]).float()
+    assert got.shape == ref.shape
+    assert (got - ref).abs().max().item() <= 2e-2
+    assert_argmax_except_ties(got, ref)
+    for j, ly in enumerate((m.bb[0], m.bb[-1])):
+        assert ulp_close(ly.kc[:, :, P - 1:P + n_frames + 1], t(z[f"kc{j}"]), 1e-2, 1e-2)
+        assert ulp_close(ly.vc[:, :, P - 1:P + n_frames + 1], t(z[f"vc{j}"]), 1e-2, 1e-2)
+    assert float(t(z["kc0"])[:, :, -1].abs().sum()) == 0.0     # slot P + n_frames untouched
+    assert float(t(z["kc0"])[:, :, 1].abs().sum()) > 0.0       # slot P written by the first step
+    # streams: frame 0 .. end, cut at take 0's first EOS frame (4); take 1 runs to the end
+    assert t(z["stream0"]).shape == (8, 4) and t(z["stream1"]).shape == (8, n_frames + 1)
+    assert torch.equal(t(z["stream1"]), force[:, 1].t())
