@@ -64,15 +64,6 @@ SIGNATURES = {
     "hm_decode_attn_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "hm_decode_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "hm_cfg_topk_sample": (_I, [_P, _I64, _I, _I, _I, _P, _I64, _F, _I, _F, _P, _I64, _I, _P, _I, _P]),
-    "hm_seq_create": (_P, []),
-    "hm_seq_destroy": (None, [_P]),
-    "hm_seq_size": (_I, [_P]),
-    "hm_seq_add_gemv": (_I, [_P, C.POINTER(GemvDesc), _I]),
-    "hm_seq_add_attn": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P, _I]),
-    "hm_seq_add_emb_sum": (_I, [_P, _P, _I64, _I, _I, _I64, _P, _P, _I64, _I, _P, _P, _I64]),
-    "hm_seq_finalize": (_I, [_P]),
-    "hm_seq_launch": (_I, [_P, _P, _P]),
-    "hm_seq_smem_bytes": (_SZ, []),
     "hm_gemm_i8w": (_I, [_P, _I64, _P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _P, _P]),
     "hm_prefill_attn": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P]),
     "hm_device_sm_count": (_I, [_I]),

@@ -773,8 +773,6 @@ cudaError_t launch_attn(const AttnParams& p, int pdl, cudaStream_t st) {
 
 }  // namespace
 
-// K/V cache tensor map for the persistent stage runner (same boxes and cache)
-bool hm_seq_cache_map(const void* base, int64_t rows, CUtensorMap* out) { return cache_map(base, rows, out); }
 
 extern "C" size_t hm_decode_attn_workspace_bytes(int R, int Hq, int hd, int nsplit) {
   if (nsplit <= 1) return 0;

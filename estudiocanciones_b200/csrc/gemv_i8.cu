@@ -1042,8 +1042,6 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-// weight tensor map for the persistent stage runner (same boxes and cache)
-bool hm_seq_weight_map(const int8_t* w, int N, int K, CUtensorMap* out) { return weight_map(w, N, K, out); }
 
 extern "C" int hm_gemv_pick_kspan(int M, int N, int K, int epi, int kspan) {
   (void)N;

@@ -220,74 +220,20 @@ class StackBuffers:
 
 class FramePlan:
     """An ordered list of launches on fixed buffers.  ``run()`` issues them on the
-    current stream; running it inside ``torch.cuda.graph`` captures the frame.
+    current stream; running it inside ``torch.cuda.graph`` captures the frame."""
 
-    ``persistent``: runs of consecutive GEMV / attention / embedding-sum steps that
-    the stage runner supports are recorded into stage sequences (``hm_seq_*``) and
-    each run becomes ONE cooperative launch; everything else stays a launch of its
-    own and closes the current sequence."""
-
-    def __init__(self, ctx: _Ctx, pdl: bool = True, persistent: bool = False):
+    def __init__(self, ctx: _Ctx, pdl: bool = True):
         self.ctx = ctx
         self.ops = []
         self.pdl = int(pdl)
-        self.persistent = bool(persistent)
         self._keep = []
-        self._seg = None
-        self._segs = []
         self.n_kernels = 0
-        self.n_stages = 0
-        self.rms_split = os.environ.get("HM_RMS_SPLIT", "0") != "0" and not self.persistent
-
-    def __del__(self):
-        try:
-            L = _lib.lib()
-            for q in self._segs:
-                L.hm_seq_destroy(q)
-        except Exception:
-            pass
-        self._segs = []
+        self.rms_split = os.environ.get("HM_RMS_SPLIT", "0") != "0"
 
     def run(self):
-        if self._seg is not None:
-            self._flush()
         st = torch.cuda.current_stream().cuda_stream
         for op in self.ops:
             op(st)
-
-    # ------------------------------------------------------------------ stage sequences
-    def _seg_try(self, add):
-        """Offer one step to the open sequence; False if the runner cannot take it."""
-        if not self.persistent:
-            return False
-        L = _lib.lib()
-        if self._seg is None:
-            self._seg = L.hm_seq_create()
-            if not self._seg:
-                raise _lib.HMError("hm_seq_create failed")
-            self._segs.append(self._seg)
-        rc = add(L, self._seg)
-        if rc == 0:
-            self.n_stages += 1
-            return True
-        if rc not in (_lib.HM_EARG, _lib.HM_ENOSPACE):
-            check(rc, "hm_seq_add")
-        self._flush()
-        return False
-
-    def _flush(self):
-        q = self._seg
-        self._seg = None
-        if q is None:
-            return
-        L = _lib.lib()
-        if L.hm_seq_size(q) == 0:
-            return
-        check(L.hm_seq_finalize(q), "hm_seq_finalize")
-        err = self.ctx.err.data_ptr()
-        fn = L.hm_seq_launch
-        self.ops.append(lambda st: check(fn(q, err, st), "hm_seq_launch"))
-        self.n_kernels += 1
 
     # ------------------------------------------------------------------ primitives
     def _gemv(self, lin: Linear, M, src0, src1=None, epi=HM_EPI_STORE, y=None, res=None, ss_out=None,
@@ -321,9 +267,6 @@ class FramePlan:
         self._keep.append((d, getattr(src0, "refs", None), getattr(src1, "refs", None), y, res, ss_out, rope, pos,
                            q_out))
         ref = C.byref(d)
-        if kspan == 0 and self._seg_try(lambda Lb, q: Lb.hm_seq_add_gemv(q, ref, int(keep))):
-            return
-        self._flush()
         fn = L.hm_gemv_i8_fused
         self.ops.append(lambda st: check(fn(ref, st), "hm_gemv_i8_fused"))
         self.n_kernels += 1
@@ -355,7 +298,6 @@ class FramePlan:
 
     def sumsq(self, x, ss, R):
         """ss partials of an fp16 matrix that no fused producer wrote (API entry points)."""
-        self._flush()
 
         def op(st, x=x, ss=ss, R=R):
             D = x.shape[1]
@@ -368,7 +310,6 @@ class FramePlan:
         L = _lib.lib()
         args = (x.data_ptr(), x.stride(0), ss.data_ptr(), ss.shape[0], ss.stride(0), gamma.data_ptr(), EPS,
                 x.shape[1], out.data_ptr(), out.stride(0), R, x.shape[1], self.pdl)
-        self._flush()
         fn = L.hm_rms_apply
         self.ops.append(lambda st: check(fn(*args, st), "hm_rms_apply"))
         self.n_kernels += 1
@@ -389,9 +330,6 @@ class FramePlan:
         args = (q.data_ptr(), blk.kc.data_ptr(), blk.vc.data_ptr(), pos.data_ptr(), o.data_ptr(), R, S, blk.h,
                 blk.kvh, blk.hd, blk.kc.shape[2], 1.0 / math.sqrt(blk.hd), nsplit, self.ctx.attn_ws.data_ptr(),
                 self.ctx.attn_ws.numel(), self.ctx.attn_tk, 32768, self.ctx.err.data_ptr(), self.pdl)
-        if self._seg_try(lambda Lb, qq: Lb.hm_seq_add_attn(qq, *args[:17])):
-            return
-        self._flush()
         fn = L.hm_decode_attn
         self.ops.append(lambda st: check(fn(*args, st), "hm_decode_attn"))
         self.n_kernels += 1
@@ -413,15 +351,11 @@ class FramePlan:
         L = _lib.lib()
         args = (tok.data_ptr(), tok.stride(0), R, ncb, vocab, emb.q8.data_ptr(), emb.s8.data_ptr(), emb.q8.shape[0],
                 x.shape[1], x.data_ptr(), ss.data_ptr(), ss.stride(0), self.ctx.err.data_ptr(), self.pdl)
-        if self._seg_try(lambda Lb, q: Lb.hm_seq_add_emb_sum(q, *args[:12])):
-            return
-        self._flush()
         fn = L.hm_emb_sum_i8
         self.ops.append(lambda st: check(fn(*args, st), "hm_emb_sum_i8"))
         self.n_kernels += 1
 
     def sample(self, logits, n_takes, cfg, topk, temp, noise, out, col):
-        self._flush()
         L = _lib.lib()
         B, V = logits.shape
         args = (logits.data_ptr(), logits.stride(0), B, n_takes, V, noise.data_ptr(), noise.stride(0), float(cfg),
@@ -431,7 +365,6 @@ class FramePlan:
         self.n_kernels += 1
 
     def commit(self, tok_out, tok_in, pos, n_keep, stream, frame, ends=None):
-        self._flush()
         L = _lib.lib()
         B, ncb = tok_out.shape
         args = (tok_out.data_ptr(), tok_in.data_ptr(), B, ncb, pos.data_ptr(), n_keep, _p(stream), frame.data_ptr(),
@@ -441,7 +374,6 @@ class FramePlan:
         self.n_kernels += 1
 
     def torch_op(self, f):
-        self._flush()
         self.ops.append(lambda st: f())
 
 
@@ -595,12 +527,13 @@ class HeartMuLaLite:
 
     @torch.inference_mode()
     def generate(self, lyrics, tags, tokenizer, *, max_ms=60_000, temperature=1.0, topk=50, cfg_scale=1.5,
-                 seed=None, use_graphs=True, progress=None, abort=None, n=1):
-        """Reference ``generate`` (``app/engine.py:374-448``): ``[8, T]`` per take."""
+                 seed=None, use_graphs=True, progress=None, abort=None, n=1, **harness):
+        """Reference ``generate`` (``app/engine.py:374-448``): ``[8, T]`` per take.  ``harness``:
+        the test-only keywords of :meth:`generate_ids` (``teacher``, ``keep_state``, ``fixed_noise``)."""
         text, muq_idx = self._prompt(lyrics, tags, tokenizer)
         return self.generate_ids(text, muq_idx, max_ms=max_ms, temperature=temperature, topk=topk,
                                  cfg_scale=cfg_scale, seed=seed, use_graphs=use_graphs, progress=progress,
-                                 abort=abort, n=n)
+                                 abort=abort, n=n, **harness)
 
     @torch.inference_mode()
     def generate_ids(self, text, muq_idx, *, max_ms=60_000, temperature=1.0, topk=50, cfg_scale=1.5, seed=None,
@@ -716,12 +649,6 @@ class _Runtime:
         self.noise_stream = torch.cuda.Stream(device=dev)
         self.draw_noise = True
         self.pdl = True
-        # HM_PERSISTENT: "1" = one cooperative launch (stage sequence) per run of fused
-        # steps everywhere, "dec" = only for the decoder passes and heads, "0" = separate
-        # launches (default until the sequences are the faster path)
-        mode = os.environ.get("HM_PERSISTENT", "0")
-        self.persistent = mode not in ("0", "")
-        self.persistent_backbone = mode not in ("0", "", "dec")
         self.force = torch.zeros(B, m.n_cb, dtype=torch.long, device=dev)
         self.force_tab = None   # teacher ids per frame of a forced generate (parity harness)
         self.rec_tab = None     # every head's logits of a forced generate
@@ -784,7 +711,7 @@ class _Runtime:
         m = self.m
         B, N = self.B, self.N
         V = m.vocab
-        plan = FramePlan(self.ctx, pdl=self.pdl, persistent=self.persistent and self.persistent_backbone)
+        plan = FramePlan(self.ctx, pdl=self.pdl)
         join = self._noise_ops(plan)
         if teacher:
             # teacher forcing: record every head's logits and take the forced ids
@@ -821,7 +748,6 @@ class _Runtime:
         plan._gemv(m.c0_head, B, last_h, y=self.logits)
         plan.pdl = int(self.pdl)
         plan.torch_op(join)
-        plan.persistent = self.persistent  # decoder passes
         sample(0, self.noise[0])
         # decoder pass 0: rows (2b, 2b+1) = (last_h[b], emb(0, c0[b])) at positions (0, 1)
         last_h = plan.src_f16(bb.x) if normed_input else plan.src_rms(bb.x, bb.ss, m.backbone.norm)

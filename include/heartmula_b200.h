@@ -3,9 +3,7 @@
  *
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
  * (passed as `hm_stream_t`), launches on that stream, never allocates and
- * never synchronises, so all of them can be captured into a CUDA graph.  The
- * exceptions are the set-up calls of a stage sequence (hm_seq_create /
- * hm_seq_add_* / hm_seq_finalize / hm_seq_destroy), made once, outside capture.
+ * never synchronises, so all of them can be captured into a CUDA graph.
  * Each returns 0 on success, a cudaError_t value (> 0) when the launch failed,
  * or HM_EARG (< 0) when an argument is out of the supported range.
  *
@@ -210,35 +208,6 @@ int hm_decode_attn_noalloc(const void* q, const void* kc, const void* vc, const 
 int hm_cfg_topk_sample(const void* logits, int64_t ld_logits, int B, int N, int V, const float* noise,
                        int64_t ld_noise, float cfg, int topk, float temp, int64_t* out, int64_t out_ld, int out_col,
                        int* err, int pdl, hm_stream_t stream);
-
-/* ------------------------------------------------------------------ persistent stage sequences
- * A chain of decode launches (GEMV / attention / embedding-sum steps, each depending on the
- * previous one) recorded once and run as ONE cooperative kernel with one CTA per SM: a
- * producer warp streams the weights of every GEMV step through a TMA ring without stopping at
- * step boundaries; the steps are separated by a bounded grid-wide barrier.  Same math and
- * outputs as the separate launches (hm_gemv_i8_fused, hm_decode_attn with head_dim 128,
- * hm_emb_sum_i8).  Replaces the per-layer launch chain of Stack.decode and the frame graph of
- * _frame_fast/_step (app/engine.py:180-211, 328-354, 409-461), which the reference issues as
- * separate kernels.
- * Limits: GEMV steps with M <= 8 rows whose whole-K activations fit 128 KB of shared memory
- * (HM_ENOSPACE otherwise), attention with hd == 128 and Hq/Hk <= 8, embedding sums with D % 16 == 0.
- * keep != 0 marks weights that are read again soon (evict-last L2 hint instead of evict-first).
- * hm_seq_finalize uploads the step list (allocates; call it outside stream capture);
- * hm_seq_launch is capturable (a memset of the barrier word + the kernel). */
-typedef struct hm_seq hm_seq;
-hm_seq* hm_seq_create(void);
-void hm_seq_destroy(hm_seq* seq);
-int hm_seq_size(const hm_seq* seq);
-int hm_seq_add_gemv(hm_seq* seq, const hm_gemv_desc* d, int keep);
-int hm_seq_add_attn(hm_seq* seq, const void* q, const void* kc, const void* vc, const int64_t* pos, void* o, int R,
-                    int S, int Hq, int Hk, int hd, int L, float scale, int nsplit, void* ws, size_t ws_bytes,
-                    int* counters, int n_counters);
-int hm_seq_add_emb_sum(hm_seq* seq, const int64_t* tok, int64_t tok_ld, int R, int ncb, int64_t vocab,
-                       const int8_t* tab, const void* scale, int64_t rows, int D, void* x_out, float* ss_out,
-                       int64_t ss_ld);
-int hm_seq_finalize(hm_seq* seq);
-int hm_seq_launch(hm_seq* seq, int* err, hm_stream_t stream);
-size_t hm_seq_smem_bytes(void);
 
 /* ------------------------------------------------------------------ prompt prefill
  * Tensor-core GEMM with int8 weights for many rows (tcgen05 MMA, fp32 accumulators in TMEM):
