@@ -14,7 +14,19 @@ here                   reference                                   C entry point
 ``gemm_i8w``           ``int8_mm`` for M > 16 (``:46-49``)           ``hm_gemm_i8w`` (tcgen05)
 ``prefill_attn``       causal SDPA of ``Block.__call__``            ``hm_prefill_attn``
                        (``app/engine.py:123-153``)
+``_rope_cache``        ``_rope_cache[grid](...)`` (``:79-107``)      ``hm_rope_kv_write``
+``_attn``              ``_attn[grid](...)`` (``:112-153``)           ``hm_decode_attn`` (merged)
+``_attn_combine``      ``_attn_combine[grid](...)`` (``:157-167``)   nothing (``_attn`` merged)
+``_silu_mul``          ``_silu_mul[grid](...)`` (``:172-180``)       ``hm_silu_mul``
 =====================  ==========================================  ==============================
+
+The four underscore names take the reference's own launch syntax, ``kernel[grid](*args,
+**constexprs)`` as ``Stack.decode`` writes it (``app/engine.py:184-210``), so that loop
+runs unchanged on top of this module: the grid and the Triton meta-parameters (``HD``,
+``HALF``, ``HDP``, ``G``, ``BLK``, ``NSPLIT``, ``BLOCK``, ``num_warps``) are accepted and
+not needed, because each C entry point sizes its own launch.  ``_attn`` writes the
+merged output into ``o`` itself (its split count is chosen for this GPU), so the
+reference's following ``_attn_combine`` launch has nothing left to do and returns.
 
 Launches go to the current torch CUDA stream, so everything here can be
 captured in a CUDA graph.  Scratch memory comes from the torch allocator (the
@@ -139,6 +151,15 @@ def silu_mul(a: torch.Tensor) -> torch.Tensor:
     _need_cuda(a)
     R, F2 = a.shape
     y = torch.empty(R, F2 // 2, device=a.device, dtype=a.dtype)
+    return silu_mul_into(a, y)
+
+
+def silu_mul_into(a: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """``y[r, j] = fp16(silu(a[r, j])) * a[r, F + j]`` into a caller's ``[R, F]`` tensor."""
+    _need_cuda(a, y)
+    R, F2 = a.shape
+    if y.shape != (R, F2 // 2) or not a.is_contiguous() or not y.is_contiguous():
+        raise HMError("silu_mul: a [R, 2F] and y [R, F], both contiguous")
     check(_lib.lib().hm_silu_mul(a.data_ptr(), y.data_ptr(), R, F2 // 2, _stream()), "hm_silu_mul")
     return y
 
@@ -199,3 +220,53 @@ def prefill_attn(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, P: int, o:
     check(_lib.lib().hm_prefill_attn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, P, Hq, Hk, hd, L,
                                      scale, error_word(q.device).data_ptr(), _stream()), "hm_prefill_attn")
     return o
+
+
+# ----------------------------------------------------------------------------- raw-launch stand-ins
+class _Launch:
+    """A kernel name that launches with the reference's ``kernel[grid](*args, **meta)``
+    syntax.  ``grid`` and the Triton meta-parameters are accepted and ignored: the C
+    entry point behind ``run`` sizes its own launch."""
+
+    def __init__(self, name: str, run):
+        self.__name__ = name
+        self._run = run
+
+    def __getitem__(self, grid):
+        def launch(*args, **meta):
+            return self._run(*args, **meta)
+        return launch
+
+    def __call__(self, *args, **kwargs):
+        raise TypeError(f"{self.__name__} launches as {self.__name__}[grid](...), like the reference's kernel")
+
+
+def _rope_cache_launch(qkv, rope, pos, q_out, kc, vc, S, Hq, Hk, L, **meta):
+    rope_cache(qkv, rope, pos, q_out, kc, vc, int(S), int(Hq), int(Hk), int(L))
+
+
+def _attn_launch(q, kc, vc, pos, o, pm, pl, pa, S, Hq, Hk, L, scale, **meta):
+    # the scratch tensors the reference passes for its split partials (pm, pl, pa) are not
+    # needed: the split count is chosen for this GPU and the merge happens inside
+    from .engine import default_nsplit
+    del pm, pl, pa, meta
+    R = q.shape[0]
+    attn(q, kc, vc, pos, o, int(S), int(Hq), int(Hk), int(L), float(scale),
+         nsplit=default_nsplit(R, int(Hk), int(L), sms=torch.cuda.get_device_properties(q.device).multi_processor_count))
+
+
+def _attn_combine_launch(pm, pl, pa, o, **meta):
+    """Nothing to do: ``_attn`` wrote the merged output into ``o``."""
+    del pm, pl, pa, o, meta
+
+
+def _silu_mul_launch(a, y, F_, **meta):
+    if a.shape[1] != 2 * int(F_):
+        raise HMError("_silu_mul: a must hold the w1 and w3 halves [R, 2F]")
+    silu_mul_into(a, y)
+
+
+_rope_cache = _Launch("_rope_cache", _rope_cache_launch)
+_attn = _Launch("_attn", _attn_launch)
+_attn_combine = _Launch("_attn_combine", _attn_combine_launch)
+_silu_mul = _Launch("_silu_mul", _silu_mul_launch)

@@ -176,7 +176,8 @@ int hm_frame_commit(const int64_t* tok_out, int64_t* tok_in, int B, int ncb, int
  * _attn + _attn_combine (app/kernels.py:112-167): row r of batch r/S attends
  * cache positions [0, pos[r]] with GQA (no KV copy); split over `nsplit`
  * position ranges, the last CTA of each (row, kv head) merges the partials.
- * q, o fp16 [R, Hq*hd]; kc, vc fp16 [B, Hk, L, hd]; hd in {64, 128, 256, 384}.
+ * q, o fp16 [R, Hq*hd]; kc, vc fp16 [B, Hk, L, hd]; hd in {128, 256, 384} (HM_EARG otherwise);
+ * hd 128 runs the tensor-core kernel, 256 and 384 the CUDA-core one.
  * With pdl = 1 the launch reads `pos` and the cache slots before pos[r] before it
  * waits for the preceding launch (to overlap that launch's tail): the preceding
  * launch may write q and the slot at pos[r] (the fused qkv GEMV does), not those. */
@@ -189,14 +190,19 @@ size_t hm_decode_attn_workspace_bytes(int R, int Hq, int hd, int nsplit);
  * always takes its scratch from the torch allocator).  For callers that cannot
  * allocate device memory while they decode -- a real-time audio thread, where
  * cudaMalloc may synchronise the device and stall, or an application that serves
- * every buffer from its own fixed arena.  Same arguments and results as
- * hm_decode_attn without the workspace: the split partials and merge tickets live
- * in a fixed array inside the library (4 MiB of partials: R*Hq*nsplit*(hd+2) floats
- * <= 1048576, and R*Hk <= 4096 tickets); larger requests return HM_ENOSPACE.  Every
- * GPU that loads the library holds the array until the process exits.  The first
- * call on a device looks up the array's device address (cudaGetSymbolAddress), so
- * make that first call before any stream capture.  All calls share the one array:
- * calls that overlap on the GPU (other streams, other threads) race on it. */
+ * every buffer from its own fixed arena.  Same arguments as hm_decode_attn without
+ * the workspace, and the same results within fp16 rounding: it always runs the
+ * CUDA-core split kernel (also for hd 128, where hm_decode_attn uses the tensor-core
+ * kernel, so the two differ in fp32 summation order).  The split partials and merge
+ * tickets live in a fixed array inside the library (4 MiB of partials:
+ * R*Hq*nsplit*(hd+2) floats <= 1048576, and R*Hk <= 4096 tickets); larger requests
+ * return HM_ENOSPACE.  Every GPU that loads the library holds the array until the
+ * process exits.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and keeps it for the process, so make that first call before
+ * any stream capture; the kept address does not survive cudaDeviceReset (or any other
+ * reset of the device's primary context): after one, do not call this entry point again
+ * in that process.  All calls share the one array: calls that overlap on the GPU (other
+ * streams, other threads) race on it. */
 int hm_decode_attn_noalloc(const void* q, const void* kc, const void* vc, const int64_t* pos, void* o, int R, int S,
                            int Hq, int Hk, int hd, int L, float scale, int nsplit, int* err, hm_stream_t stream);
 
