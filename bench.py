@@ -57,6 +57,9 @@ def args_():
     ap.add_argument("--layers", type=int, default=4, help="backbone layers of the small cases")
     ap.add_argument("--prefill-layers", type=int, default=28, help="backbone layers of the prefill case")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--configs", default="auto", choices=["auto", "all", "none"],
+                    help="also measure BASELINE configs 0/2/3 and the config-4 row sweep (auto: at N=1; config 4 "
+                         "at 16 rows per GPU at every N)")
     return ap.parse_args()
 
 
@@ -200,14 +203,166 @@ def gemv_roofline(m, rt, peak, reps=10):
             "bytes_per_launch": int(per_launch), "us_per_launch": round(sec * 1e6, 3)}
 
 
-def traffic_from_profile():
+def traffic_profile():
+    """DRAM bytes per GEMV launch from the committed ncu capture (profiles/gemv_traffic.json,
+    `bench.py --case gemv` under ncu): a figure from that capture, not from this run."""
     f = ROOT / "profiles" / "gemv_traffic.json"
     if f.exists():
         try:
-            return json.loads(f.read_text()).get("dram_bytes_per_launch")
+            d = json.loads(f.read_text())
+            return {"file": "profiles/gemv_traffic.json", "dram_bytes_per_launch": d.get("dram_bytes_per_launch"),
+                    "command": d.get("command")}
         except Exception:
             return None
     return None
+
+
+def attn_roofline(m, rt, peak, reps=10):
+    """Decode attention of the 28 backbone layers at the runtime's current positions, back to
+    back in a CUDA graph, timed with CUDA events on the launching stream; algorithmic bytes =
+    the K/V of every row over its attended length + q read + o written."""
+    from estudiocanciones_b200.engine import FramePlan
+    bb = rt.bb
+    B = rt.B
+    p = FramePlan(rt.ctx)
+    nbytes = 0
+    lens = (rt.pos + 1).tolist()
+    for b in m.backbone.blocks:
+        p.attn(b, bb.q, bb.o, rt.pos, 1, B, rt.nsplit)
+        nbytes += sum(lens) * b.kvh * b.hd * 2 * 2 + 2 * B * b.h * b.hd * 2
+    p.run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s), capture_no_gc():
+        with torch.cuda.graph(g, stream=s):
+            p.run()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(reps):
+        g.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    del g
+    sec = t0.elapsed_time(t1) / 1000 / (reps * p.n_kernels)
+    per = nbytes / p.n_kernels
+    gbs = per / sec / 1e9
+    return {"bound": "hbm", "kernel": "decode_attn_tc_kernel (28 backbone layers)", "rows": B,
+            "kv_len": int(max(lens)), "nsplit": int(rt.nsplit), "bytes_per_launch": int(per),
+            "us_per_launch": round(sec * 1e6, 3), "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(gbs / peak, 4)}
+
+
+def frame_run(m, takes, cfg_on, prompt, frames, steps=1, warm_frames=50, warm=3):
+    """A song of `frames` frames after a `prompt`-position cache (N(0,1) K/V) with `takes`
+    takes (x 2 CFG rows when cfg_on): one CUDA-graph replay per frame, CUDA events around
+    `steps` whole songs after `warm` shorter warm-up runs.  Returns (us per frame, rows, mean KV)."""
+    dev = m.dev
+    N = takes
+    B = 2 * N if cfg_on else N
+    L = prompt + frames + 2 + 256
+    m.alloc(N, B, L)
+    rt = m._rt
+    g = torch.Generator(device=dev).manual_seed(0)
+    for blk in m.backbone.blocks:
+        blk.kc[:, :, :prompt].normal_(generator=g)
+        blk.vc[:, :, :prompt].normal_(generator=g)
+    rt.tok_in.copy_(torch.randint(0, 8192, (B, 8), generator=g, device=dev))
+    cfg = 1.5 if cfg_on else 1.0
+    rt.pos.fill_(prompt)
+    graph = rt.graph_for(cfg, 50, 1.0)
+
+    def song(nf):
+        rt.pos.fill_(prompt)
+        rt.frame.zero_()
+        for _ in range(nf):
+            graph.replay()
+    for _ in range(warm):
+        song(warm_frames)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        song(frames)
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000 * e0.elapsed_time(e1) / (steps * frames)
+    return us, B, prompt + (frames + 1) / 2
+
+
+def config_entry(m, us, takes, B, mean_len, peak, **extra):
+    fb = frame_bytes(m, B, mean_len)
+    gbs = fb / (us * 1e-6) / 1e9
+    return {"us_per_frame": round(us, 2), "audio_s_per_s_per_gpu": round(takes * 0.08 / (us * 1e-6), 3),
+            "rows": B, "bytes_per_frame": int(fb), "frame_roofline_frac": round(gbs / peak, 4), **extra}
+
+
+def measure_configs(a, m, peak, world, rank):
+    """BASELINE configs besides the headline: 0 (1 row, CFG off, KV from 512), 2 (prefill of
+    8 x 1024 tokens, tensor cores), 3 (8 rows, 3000 frames after a 1024-token prompt), and
+    4 (16 rows per GPU; at N = 1 also the per-GPU sweep of 1/2/4/8/16 rows).  Each song is one
+    timed step after short warm-up runs (timing: CUDA events)."""
+    out = {}
+    if world == 1:
+        us, B, ml = frame_run(m, 1, False, 512, 100, steps=2)
+        out["config0"] = config_entry(m, us, 1, B, ml, peak, workload="1 take, CFG off (1 row), KV 512 -> 612")
+        us, B, ml = frame_run(m, 4, True, 1024, 3000, steps=1)
+        out["config3"] = config_entry(m, us, 4, B, ml, peak,
+                                      workload="4 takes x CFG = 8 rows, 3000 frames after a 1024-token prompt "
+                                               "(KV 1024 -> 4024)")
+        rt = m._rt
+        rt.pos.fill_(4024)
+        out["config3"]["attn_roofline_kv4024"] = attn_roofline(m, rt, peak)
+        sweep = {}
+        for R in (1, 2, 4, 8, 16):
+            takes, cfg_on = (1, False) if R == 1 else (R // 2, True)
+            us, B, ml = frame_run(m, takes, cfg_on, 600, 750, steps=1)
+            sweep[str(R)] = config_entry(m, us, takes, B, ml, peak)
+        out["config4_rows_per_gpu_sweep"] = sweep
+        m.release()
+        out["config2"] = prefill_entry(m, peak_tf=None)
+    else:
+        us, B, ml = frame_run(m, 8, True, 600, 750, steps=1)
+        us = max_over_ranks(us, world)
+        e = config_entry(m, us, 8, B, ml, peak, workload=f"8 takes x CFG = 16 rows per GPU, {world} GPUs, 750 "
+                                                          f"frames after a 600-token prompt (max over ranks)")
+        e["box_audio_s_per_s"] = round(world * 8 * 0.08 / (us * 1e-6), 3)
+        out["config4"] = e
+        m.release()
+    return out
+
+
+def prefill_entry(m, peak_tf=None):
+    """Config 2 on the loaded model: 8 rows x 1024 tokens through the 28 backbone layers."""
+    from estudiocanciones_b200.prefill import prefill_backbone
+    B, P = 8, 1024
+    m.alloc(4, B, P + 256)
+    dev = m.dev
+    h = (torch.randn(B, P, m.backbone.dim, generator=torch.Generator(device=dev).manual_seed(0), device=dev)
+         * 0.05).half()
+    for _ in range(2):
+        prefill_backbone(m, h)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        prefill_backbone(m, h)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    fl = prefill_flops(m, B, P)
+    tf = fl / (ms * 1e-3) / 1e12
+    m.release()
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    burst, sus = pk.get("bf16_tflops", 1590.0), pk.get("bf16_tflops_sustained", 1400.0)
+    return {"workload": "prefill 8 rows x 1024 tokens, 28 backbone layers (tcgen05 GEMMs + causal attention)",
+            "ms": round(ms, 3), "flop": fl, "tflops": round(tf, 1), "frac_of_bf16_burst": round(tf / burst, 4),
+            "frac_of_bf16_sustained": round(tf / sus, 4), "peak_kind": "measured" if pk else "fallback"}
 
 
 def peaks():
@@ -266,7 +421,9 @@ def run_reference(a, world, rank):
            "config": {"workload": "config1: 60 s song, 4 takes x CFG = 8 rows, KV 600->1350 (CPU sample)",
                       "model": "HeartMuLa BASELINE shape (28x3072 backbone, 4x1024 decoder), random int8"},
            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
-                            "sample": sample},
+                            "sample": sample,
+                            "scope": "one host's CPU (rank 0 with every host thread) at every N: at N > 1 the "
+                                     "GPU arm's whole-job value is set against this single-host figure"},
            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -328,14 +485,21 @@ def run_ours(a, world, rank, local):
     mean_len = P + (F_ + 1) / 2
     fb = frame_bytes(m, B, mean_len)
     roof = gemv_roofline(m, rt, peak)
-    roof["traffic"] = traffic_from_profile()
+    roof["traffic"] = None  # no ncu in this run: the committed capture's figure is under traffic_profile
+    roof["traffic_profile"] = traffic_profile()
     roof["peak_kind"] = f"{peak_kind} hbm_gbs (burst)"
+    rt.pos.fill_(P + F_ // 2)
+    attn_roof = attn_roofline(m, rt, peak)
+    attn_roof["peak_kind"] = roof["peak_kind"]
     frame_gbs = fb / (us_frame * 1e-6) / 1e9
     out = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "fp16 activations x int8 weights (fp32 accumulate)", "data": "synthetic",
            "us_per_frame": round(us_frame, 2), "frames_per_s": round(1e6 / us_frame, 1),
            "audio_s_per_s_per_gpu": round(value / world, 3),
+           "value_semantics": "whole job: audio seconds generated per second by all n_gpus GPUs (each GPU "
+                              f"decodes its own {a.takes} takes); the metric's per-GPU figure is "
+                              "audio_s_per_s_per_gpu",
            "config": {"workload": f"config1: 60 s song, {a.takes} takes x CFG = {B} rows per GPU, {F_} frames "
                                   f"after a {P}-token prompt (KV {P}->{P + F_}), one CUDA graph per frame",
                       "model": "HeartMuLa BASELINE shape (28x3072 backbone 24/8 heads, 4x1024 decoder 8/2 heads, "
@@ -344,14 +508,21 @@ def run_ours(a, world, rank, local):
                       "l2": "inputs larger than L2 (3.7 GB weights per frame)",
                       "pdl": not a.no_pdl},
            "roofline": roof,
+           "attn_roofline": attn_roof,
            "frame_roofline": {"bytes_per_frame": int(fb), "achieved": round(frame_gbs, 1), "peak": peak,
                               "unit": "GB/s", "frac": round(frame_gbs / peak, 4)},
            "gpu_launches": int(plan.n_kernels * F_ * a.steps),
            "clocks": clk}
+    # ---- the other BASELINE configs (sub-keys; the headline above is config 1)
+    if a.configs == "all" or (a.configs == "auto"):
+        del graph
+        m.release()
+        rt = None
+        out["configs"] = measure_configs(a, m, peak, world, rank)
     # ---- end to end through the public API: host prompt ids -> generate -> host token streams
     if not a.no_e2e:
         text = torch.randint(0, 128256, (P,), generator=torch.Generator().manual_seed(0)).pin_memory()
-        del rt, graph
+        rt = graph = None
         m.release()
 
         from estudiocanciones_b200.shard import generate_sharded
