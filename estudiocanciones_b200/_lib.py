@@ -65,6 +65,8 @@ SIGNATURES = {
     "hm_decode_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "hm_cfg_topk_sample": (_I, [_P, _I64, _I, _I, _I, _P, _I64, _F, _I, _F, _P, _I64, _I, _P, _I, _P]),
     "hm_gemm_i8w": (_I, [_P, _I64, _P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _P, _P]),
+    "hm_gemm_f16w": (_I, [_P, _I64, _P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _P, _P]),
+    "hm_dequant_i8_f16": (_I, [_P, _P, _I64, _P]),
     "hm_prefill_attn": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P]),
     "hm_device_sm_count": (_I, [_I]),
     "hm_abi_layout": (_SZ, [_I]),

@@ -27,6 +27,14 @@
 //               tcgen05.ld of their 32 TMEM lanes (warp % 4) over half of the
 //               tile's columns each, scale, round, residual/SiLU, store.
 // Every wait is bounded (HM_ERR_TIMEOUT in the caller's error word).
+//
+// fp16-weight variant (hm_gemm_f16w, WF16): the weights come already converted to fp16
+// (exact int8 values, hm_dequant_i8_f16, once per layer and prompt instead of once per
+// CTA that reads a tile), so TMA writes them straight into the K-major 128B-swizzled
+// layout the MMA reads, in a 4-stage ring of 32 KB B tiles (the int8 and converted-tile
+// buffers of the int8 variant, reused), and warps 2-9 only run the epilogue.  Shared-
+// memory traffic per k-block falls from 128 KB (TMA int8 + conversion read and write +
+// MMA reads) to 96 KB; the products and sums are the same, so are the results.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -49,6 +57,17 @@ struct GemmSmem {
   uint8_t bq[NST][kBqBytes];
   uint8_t bh[2][kBhBytes];
   uint64_t full[NST], empty[NST], bh_full[2], bh_empty[2], acc_full;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// fp16-weight variant: a 2-stage ring of A (16 KB) + B (32 KB) tiles, 96 KB, so two CTAs
+// share an SM and one's epilogue overlaps the other's main loop (TMEM: 2 x 256 columns)
+constexpr int NSTF = 2;
+struct GemmSmemF {
+  uint8_t a[NSTF][kABytes];
+  uint8_t b[NSTF][kBhBytes];
+  uint64_t full[NSTF], empty[NSTF], acc_full;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -126,12 +145,20 @@ HM_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 
 HM_DEV float silu_f(float a) { return a / (1.f + expf(-a)); }
 
-template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_constant__ CUtensorMap amap,
+template <int EPI, bool WF16>
+__global__ void __launch_bounds__(kThreads, WF16 ? 2 : 1) gemm_i8w_kernel(const __grid_constant__ CUtensorMap amap,
                                                                const __grid_constant__ CUtensorMap wmap,
                                                                const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
-  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  uint8_t* const sbase = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(sbase);   // int8 weights
+  GemmSmemF& sf = *reinterpret_cast<GemmSmemF*>(sbase);  // fp16 weights
+  constexpr int S = WF16 ? NSTF : NST;                   // ring stages
+  uint64_t* const full = WF16 ? sf.full : sm.full;
+  uint64_t* const empty = WF16 ? sf.empty : sm.empty;
+  uint64_t* const acc_full = WF16 ? &sf.acc_full : &sm.acc_full;
+  uint32_t* const tmem_slot = WF16 ? &sf.tmem_base : &sm.tmem_base;
+  int* const abort_word = WF16 ? &sf.abort_flag : &sm.abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m0 = blockIdx.x * BM;
   const int nt = blockIdx.y;
@@ -140,24 +167,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
   int* const err = P.err;
 
   if (tid == 0) {
-    sm.abort_flag = 0;
-    for (int i = 0; i < NST; ++i) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1 + kConvW);  // MMA commit (A consumed) + the converter warps (int8 tile consumed)
+    *abort_word = 0;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      // MMA commit (A consumed) + the converter warps (int8 tile consumed); fp16 weights: the commit only
+      mbar_init(&empty[i], WF16 ? 1 : 1 + kConvW);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.bh_full[i], kConvW);
-      mbar_init(&sm.bh_empty[i], 1);
-    }
-    mbar_init(&sm.acc_full, 1);
+    if (!WF16)
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&sm.bh_full[i], kConvW);
+        mbar_init(&sm.bh_empty[i], 1);
+      }
+    mbar_init(acc_full, 1);
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(&sm.tmem_base, kTmemCols);
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
-  volatile int* abort_s = &sm.abort_flag;
+  const uint32_t tmem = *tmem_slot;
+  volatile int* abort_s = abort_word;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -167,12 +196,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
       const int r0 = EPI == HM_EPI_SILU ? nt * (BN / 2) : nt * BN;
       const int r1 = EPI == HM_EPI_SILU ? P.wrows_half + nt * (BN / 2) : nt * BN + BN / 2;
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % NST;
-        if (kb >= NST) mbar_wait_ab(&sm.empty[s], ((kb / NST) - 1) & 1, err, abort_s);
-        mbar_arrive_expect_tx(&sm.full[s], kABytes + kBqBytes);
-        tma_load_2d_plain(sm.a[s], &amap, kb * BK, m0, &sm.full[s]);
-        tma_load_2d_plain(sm.bq[s], &wmap, kb * BK, r0, &sm.full[s]);
-        tma_load_2d_plain(sm.bq[s] + kBqBytes / 2, &wmap, kb * BK, r1, &sm.full[s]);
+        const int s = kb % S;
+        if (kb >= S) mbar_wait_ab(&empty[s], ((kb / S) - 1) & 1, err, abort_s);
+        if (WF16) {
+          mbar_arrive_expect_tx(&full[s], kABytes + kBhBytes);
+          tma_load_2d_plain(sf.a[s], &amap, kb * BK, m0, &full[s]);
+          tma_load_2d_plain(sf.b[s], &wmap, kb * BK, r0, &full[s]);
+          tma_load_2d_plain(sf.b[s] + kBhBytes / 2, &wmap, kb * BK, r1, &full[s]);
+        } else {
+          mbar_arrive_expect_tx(&sm.full[s], kABytes + kBqBytes);
+          tma_load_2d_plain(sm.a[s], &amap, kb * BK, m0, &sm.full[s]);
+          tma_load_2d_plain(sm.bq[s], &wmap, kb * BK, r0, &sm.full[s]);
+          tma_load_2d_plain(sm.bq[s] + kBqBytes / 2, &wmap, kb * BK, r1, &sm.full[s]);
+        }
       }
     }
   } else if (warp == 1) {
@@ -180,24 +216,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BM, BN);
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % NST, b = kb & 1;
-        mbar_wait_ab(&sm.full[s], (kb / NST) & 1, err, abort_s);
-        mbar_wait_ab(&sm.bh_full[b], (kb >> 1) & 1, err, abort_s);
+        const int s = kb % S, b = kb & 1;
+        mbar_wait_ab(&full[s], (kb / S) & 1, err, abort_s);
+        if (!WF16) mbar_wait_ab(&sm.bh_full[b], (kb >> 1) & 1, err, abort_s);
         tc_fence_after();
-        const uint64_t ad = sw128_desc(smem_u32(sm.a[s]));
-        const uint64_t bd = sw128_desc(smem_u32(sm.bh[b]));
+        const uint64_t ad = sw128_desc(smem_u32(WF16 ? sf.a[s] : sm.a[s]));
+        const uint64_t bd = sw128_desc(smem_u32(WF16 ? sf.b[s] : sm.bh[b]));
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K=16 step inside the 128-byte swizzle row
           umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
-        umma_commit(&sm.empty[s]);
-        umma_commit(&sm.bh_empty[b]);
+        umma_commit(&empty[s]);
+        if (!WF16) umma_commit(&sm.bh_empty[b]);
       }
-      umma_commit(&sm.acc_full);
+      umma_commit(acc_full);
     }
   } else {
     // ------------------------------------------------------------ converters, then epilogue
     const int ct = tid - 64;  // 0 .. 32 * kConvW - 1
-    for (int kb = 0; kb < nk; ++kb) {
+    for (int kb = 0; kb < (WF16 ? 0 : nk); ++kb) {
       const int s = kb % NST, b = kb & 1;
       mbar_wait_ab(&sm.full[s], (kb / NST) & 1, err, abort_s);
       if (kb >= 2) mbar_wait_ab(&sm.bh_empty[b], ((kb >> 1) - 1) & 1, err, abort_s);
@@ -226,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
     }
     // ---- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 = tile rows, and the
     // (w - 2) / 4 -th part of the tile's columns
-    mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
+    mbar_wait_ab(acc_full, 0, err, abort_s);
     tc_fence_after();
     const int q = warp & 3;
     constexpr int kParts = kConvW / 4;
@@ -366,26 +402,24 @@ bool tile_map(const void* p, int64_t rows, int64_t cols, int64_t ld, int kind, C
   return true;
 }
 
-template <int EPI>
+template <int EPI, bool WF16>
 cudaError_t launch_gemm(const CUtensorMap& am, const CUtensorMap& wm, const GemmParams& p, int ntiles_n,
                         hm_stream_t st) {
-  const size_t smem = sizeof(GemmSmem) + 1024;
+  const size_t smem = (WF16 ? sizeof(GemmSmemF) : sizeof(GemmSmem)) + 1024;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8w_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8w_kernel<EPI, WF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     configured = true;
   }
   const dim3 grid((p.M + BM - 1) / BM, ntiles_n);
-  return hm_launch(gemm_i8w_kernel<EPI>, grid, dim3(kThreads), smem, st, false, am, wm, p);
+  return hm_launch(gemm_i8w_kernel<EPI, WF16>, grid, dim3(kThreads), smem, st, false, am, wm, p);
 }
 
-}  // namespace
-
-extern "C" int hm_gemm_i8w(const void* a, int64_t lda, const int8_t* w, const void* s, const void* res,
-                           int64_t ldr, void* c, int64_t ldc, int M, int N, int K, int epi, int* err,
-                           hm_stream_t stream) {
+// Shared argument checks and launch of both variants (wf16: w holds fp16 [N, K]).
+int gemm_entry(const void* a, int64_t lda, const void* w, bool wf16, const void* s, const void* res, int64_t ldr,
+               void* c, int64_t ldc, int M, int N, int K, int epi, int* err, hm_stream_t stream) {
   if (!a || !w || !s || !c || M < 1 || N < 1 || K < BK || K % BK != 0) return HM_EARG;
   if (epi != HM_EPI_STORE && epi != HM_EPI_SILU) return HM_EARG;
   if (epi == HM_EPI_SILU && (res != nullptr || N % 2 != 0)) return HM_EARG;
@@ -396,7 +430,7 @@ extern "C" int hm_gemm_i8w(const void* a, int64_t lda, const int8_t* w, const vo
   if (res && (ldr % 8 != 0 || ldr < N || (reinterpret_cast<uintptr_t>(res) & 15u))) return HM_EARG;
   if (reinterpret_cast<uintptr_t>(w) & 15u) return HM_EARG;
   CUtensorMap am, wm;
-  if (!tile_map(a, M, K, lda, 0, &am) || !tile_map(w, N, K, K, 1, &wm)) return HM_EARG;
+  if (!tile_map(a, M, K, lda, 0, &am) || !tile_map(w, N, K, K, wf16 ? 0 : 1, &wm)) return HM_EARG;
   GemmParams p;
   p.s = reinterpret_cast<const __half*>(s);
   p.res = reinterpret_cast<const __half*>(res);
@@ -408,10 +442,25 @@ extern "C" int hm_gemm_i8w(const void* a, int64_t lda, const int8_t* w, const vo
   p.K = K;
   p.wrows_half = epi == HM_EPI_SILU ? N / 2 : 0;
   p.err = err;
+  const int tn = epi == HM_EPI_SILU ? (nout + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
   cudaError_t e;
   if (epi == HM_EPI_SILU)
-    e = launch_gemm<HM_EPI_SILU>(am, wm, p, (nout + BN / 2 - 1) / (BN / 2), stream);
+    e = wf16 ? launch_gemm<HM_EPI_SILU, true>(am, wm, p, tn, stream) : launch_gemm<HM_EPI_SILU, false>(am, wm, p, tn, stream);
   else
-    e = launch_gemm<HM_EPI_STORE>(am, wm, p, (N + BN - 1) / BN, stream);
+    e = wf16 ? launch_gemm<HM_EPI_STORE, true>(am, wm, p, tn, stream)
+             : launch_gemm<HM_EPI_STORE, false>(am, wm, p, tn, stream);
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+}  // namespace
+
+extern "C" int hm_gemm_i8w(const void* a, int64_t lda, const int8_t* w, const void* s, const void* res,
+                           int64_t ldr, void* c, int64_t ldc, int M, int N, int K, int epi, int* err,
+                           hm_stream_t stream) {
+  return gemm_entry(a, lda, w, false, s, res, ldr, c, ldc, M, N, K, epi, err, stream);
+}
+
+extern "C" int hm_gemm_f16w(const void* a, int64_t lda, const void* w, const void* s, const void* res, int64_t ldr,
+                            void* c, int64_t ldc, int M, int N, int K, int epi, int* err, hm_stream_t stream) {
+  return gemm_entry(a, lda, w, true, s, res, ldr, c, ldc, M, N, K, epi, err, stream);
 }

@@ -127,3 +127,39 @@ extern "C" int hm_q8_rows(const void* x, int dtype, int64_t N, int64_t K, int64_
   }
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }
+
+// ------------------------------------------------------------------ int8 -> fp16 (exact, unscaled)
+// The prompt prefill multiplies by the weights as fp16 values on the tensor cores; every
+// int8 value is exact in fp16 and the per-row scale is applied to the fp32 sums in the
+// GEMM's epilogue, so converting once per layer and prompt (instead of in every CTA of
+// the GEMM that reads the tile) changes no result.  HBM-bound: 1 byte read and 2 written
+// per element, 16-byte loads and 2 x 16-byte stores, grid-stride.
+namespace {
+__global__ void __launch_bounds__(256) dequant_i8_kernel(const uint4* __restrict__ w, uint4* __restrict__ out,
+                                                         int64_t n16) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 q = __ldcs(w + i);
+    uint4 h0, h1;
+    i8x4_to_h2x2(q.x, h0.x, h0.y);
+    i8x4_to_h2x2(q.y, h0.z, h0.w);
+    i8x4_to_h2x2(q.z, h1.x, h1.y);
+    i8x4_to_h2x2(q.w, h1.z, h1.w);
+    out[2 * i] = h0;
+    out[2 * i + 1] = h1;
+  }
+}
+}  // namespace
+
+extern "C" int hm_dequant_i8_f16(const int8_t* w, void* out, int64_t n, hm_stream_t stream) {
+  if (!w || !out || n < 16 || n % 16 || ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15u))
+    return HM_EARG;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t n16 = n / 16;
+  const int64_t want = (n16 + 255) / 256;
+  const int grid = static_cast<int>(want < 8LL * sms ? want : 8LL * sms);
+  dequant_i8_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const uint4*>(w), reinterpret_cast<uint4*>(out), n16);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}

@@ -207,6 +207,35 @@ def gemm_i8w(a: torch.Tensor, w: torch.Tensor, s: torch.Tensor, res: torch.Tenso
     return out
 
 
+def dequant_i8(w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Exact int8 -> fp16 copy of a weight matrix (no scale), for :func:`gemm_f16w`."""
+    _need_cuda(w, out)
+    if out is None:
+        out = torch.empty(w.shape, device=w.device, dtype=torch.float16)
+    if out.numel() < w.numel() or not w.is_contiguous() or not out.is_contiguous():
+        raise HMError("dequant_i8: contiguous w and an output of at least w's size")
+    check(_lib.lib().hm_dequant_i8_f16(w.data_ptr(), out.data_ptr(), w.numel(), _stream()), "hm_dequant_i8_f16")
+    return out
+
+
+def gemm_f16w(a: torch.Tensor, wh: torch.Tensor, s: torch.Tensor, res: torch.Tensor | None = None,
+              out: torch.Tensor | None = None, silu: bool = False) -> torch.Tensor:
+    """:func:`gemm_i8w` with the weights already dequantised to fp16 (``wh [N, K]``, the exact
+    int8 values): the same result, without a conversion of every weight tile per CTA."""
+    _need_cuda(a, wh, s, res, out)
+    M, K = a.shape
+    N = wh.shape[0]
+    nout = N // 2 if silu else N
+    if out is None:
+        out = torch.empty(M, nout, device=a.device, dtype=torch.float16)
+    check(_lib.lib().hm_gemm_f16w(a.data_ptr(), a.stride(0), wh.data_ptr(), s.data_ptr(),
+                                  res.data_ptr() if res is not None else None, res.stride(0) if res is not None else 0,
+                                  out.data_ptr(), out.stride(0), M, N, K,
+                                  _lib.HM_EPI_SILU if silu else _lib.HM_EPI_STORE,
+                                  error_word(a.device).data_ptr(), _stream()), "hm_gemm_f16w")
+    return out
+
+
 def prefill_attn(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, P: int, o: torch.Tensor | None = None,
                  scale: float | None = None) -> torch.Tensor:
     """Causal attention of a whole prompt: q ``[B*P, Hq*hd]`` (row ``b*P + p``) over

@@ -52,15 +52,23 @@ def prefill_backbone(model, h: torch.Tensor) -> None:
     pos = torch.arange(P, device=dev, dtype=torch.long).repeat(B)
     b0 = stack.blocks[0]
     q = torch.empty(M, b0.h * b0.hd, device=dev, dtype=torch.float16)
+    # each weight is converted to fp16 once for the whole prompt (exact int8 values, into one
+    # scratch reused by every matrix, stream-ordered) so the GEMMs read their tiles as they are
+    wbuf = torch.empty(max(lin.q8.numel() for lin in (b0.qkv, b0.o, b0.w13, b0.w2)), device=dev, dtype=torch.float16)
+
+    def gemm(a, lin, **kw):
+        wh = kernels.dequant_i8(lin.q8, wbuf[:lin.q8.numel()].view(lin.q8.shape))
+        return kernels.gemm_f16w(a, wh, lin.s8, **kw)
+
     for blk in stack.blocks:
         hn = kernels.rms(x, blk.n1)
-        qkv = kernels.gemm_i8w(hn, blk.qkv.q8, blk.qkv.s8)
+        qkv = gemm(hn, blk.qkv)
         kernels.rope_cache(qkv, stack.rope, pos, q, blk.kc, blk.vc, P, blk.h, blk.kvh, L)
         o = kernels.prefill_attn(q, blk.kc, blk.vc, P)
-        kernels.gemm_i8w(o, blk.o.q8, blk.o.s8, res=x, out=x)
+        gemm(o, blk.o, res=x, out=x)
         hn = kernels.rms(x, blk.n2)
-        mm = kernels.gemm_i8w(hn, blk.w13.q8, blk.w13.s8, silu=True)
-        kernels.gemm_i8w(mm, blk.w2.q8, blk.w2.s8, res=x, out=x)
+        mm = gemm(hn, blk.w13, silu=True)
+        gemm(mm, blk.w2, res=x, out=x)
     _rows_to_runtime(rt, x.reshape(B, P, D)[:, P - 1])
 
 

@@ -226,6 +226,18 @@ int hm_cfg_topk_sample(const void* logits, int64_t ld_logits, int B, int N, int 
 int hm_gemm_i8w(const void* a, int64_t lda, const int8_t* w, const void* s, const void* res, int64_t ldr, void* c,
                 int64_t ldc, int M, int N, int K, int epi, int* err, hm_stream_t stream);
 
+/* The same GEMM with the weights already in fp16 (w [N, K] fp16 holding the exact int8
+ * values, from hm_dequant_i8_f16; s, epilogues and limits as hm_gemm_i8w, results
+ * identical): the tensor cores read the weight tiles as TMA writes them, with no
+ * per-tile conversion.  The prompt pass converts each layer's weights once per prompt. */
+int hm_gemm_f16w(const void* a, int64_t lda, const void* w, const void* s, const void* res, int64_t ldr, void* c,
+                 int64_t ldc, int M, int N, int K, int epi, int* err, hm_stream_t stream);
+
+/* out[i] = (fp16) w[i] for n int8 values (exact; no scale): the weights of hm_gemm_f16w.
+ * n % 16 == 0, 16-byte aligned pointers.  The dequantisation of int8_mm's M > 16 branch
+ * (app/kernels.py:46-49) without the scale, which hm_gemm_f16w applies to the sums. */
+int hm_dequant_i8_f16(const int8_t* w, void* out, int64_t n, hm_stream_t stream);
+
 /* Causal GQA attention of a whole prompt over the cache positions [0, P) that the
  * RoPE/KV-write step filled: q, o [B*P, Hq*hd] fp16 (row b*P + p), kc/vc [B, Hk, L, hd].
  * hd == 128, Hq/Hk <= 4.  Replaces the prompt branch of Block.__call__'s attention

@@ -154,3 +154,37 @@ def test_tensor_core_prefill_matches_decode_path_prefill():
     for a, b in zip(kc, (b.kc for b in m.backbone.blocks)):
         torch.testing.assert_close(a.float(), b.float(), atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(x.float(), m._rt.x_bb.float(), atol=5e-2, rtol=2e-2)
+
+
+def test_dequant_i8_is_exact():
+    from estudiocanciones_b200 import kernels
+    g = torch.Generator().manual_seed(17)
+    w = torch.randint(-128, 128, (384, 1040), generator=g, dtype=torch.int8)
+    wh = kernels.dequant_i8(w.to(DEV)).cpu()
+    assert wh.dtype == torch.float16 and torch.equal(wh.float(), w.float())
+
+
+@pytest.mark.parametrize("M,N,K,mode", [(37, 512, 1024, "store"), (128, 256, 3072, "store"), (300, 5120, 512, "res"),
+                                        (200, 2048, 512, "silu"), (130, 16384, 3072, "silu"),
+                                        (64, 3072, 8192, "res")])
+def test_gemm_f16w_equals_gemm_i8w(M, N, K, mode):
+    """Weights converted once (exact) then read as fp16 tiles: the same MMA sequence over
+    the same values, so the results equal the int8-weight GEMM's bit for bit."""
+    from estudiocanciones_b200 import kernels
+    a, w, s = _gemm_case(M * 3 + N + K, M, N, K, scale=0.5 if mode == "silu" else 0.02)
+    a, w, s = a.to(DEV), w.to(DEV), s.to(DEV)
+    wh = kernels.dequant_i8(w)
+    if mode == "silu":
+        x = kernels.gemm_i8w(a, w, s, silu=True)
+        y = kernels.gemm_f16w(a, wh, s, silu=True)
+    elif mode == "res":
+        r = torch.randn(M, N, generator=torch.Generator(device=DEV).manual_seed(2), device=DEV).half()
+        x, y = r.clone(), r.clone()
+        kernels.gemm_i8w(a, w, s, res=x, out=x)
+        kernels.gemm_f16w(a, wh, s, res=y, out=y)
+    else:
+        x = kernels.gemm_i8w(a, w, s)
+        y = kernels.gemm_f16w(a, wh, s)
+    torch.cuda.synchronize()
+    assert kernels.read_errors(DEV) == 0
+    assert torch.equal(x, y)
