@@ -355,13 +355,23 @@ def prefill_entry(m, peak_tf=None):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
+    # the same prompt with the weights converted to fp16 inside the prompt (no kept copies)
+    m.drop_prefill_weights()
+    torch.cuda.synchronize()
+    e0.record()
+    prefill_backbone(m, h, keep_f16=False)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_conv = e0.elapsed_time(e1)
     fl = prefill_flops(m, B, P)
     tf = fl / (ms * 1e-3) / 1e12
     m.release()
     pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     burst, sus = pk.get("bf16_tflops", 1590.0), pk.get("bf16_tflops_sustained", 1400.0)
-    return {"workload": "prefill 8 rows x 1024 tokens, 28 backbone layers (tcgen05 GEMMs + causal attention)",
-            "ms": round(ms, 3), "flop": fl, "tflops": round(tf, 1), "frac_of_bf16_burst": round(tf / burst, 4),
+    return {"workload": "prefill 8 rows x 1024 tokens, 28 backbone layers (tcgen05 GEMMs + causal attention); "
+                        "fp16 copies of the backbone weights kept resident (made by the first, untimed prefill)",
+            "ms": round(ms, 3), "ms_converting_weights_per_prompt": round(ms_conv, 3),
+            "flop": fl, "tflops": round(tf, 1), "frac_of_bf16_burst": round(tf / burst, 4),
             "frac_of_bf16_sustained": round(tf / sus, 4), "peak_kind": "measured" if pk else "fallback"}
 
 
@@ -458,7 +468,7 @@ def run_ours(a, world, rank, local):
         for _ in range(F_):
             graph.replay()
         if world > 1:  # finished token streams of every rank's takes -> rank 0 (NCCL)
-            gather_streams([rt.stream_out[:F_, i].t() for i in range(N)], N * world, world, rank)
+            gather_streams([rt.stream_out[:F_, i].t() for i in range(N)], N * world, world, rank, t_cap=F_, n_cb=8)
 
     for _ in range(a.warmup):
         step()

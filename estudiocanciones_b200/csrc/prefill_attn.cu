@@ -1,244 +1,392 @@
-// Causal GQA prefill attention over the static KV cache (sm_100a tensor cores).
+// Causal GQA prefill attention over the static KV cache on the 5th-generation
+// tensor cores (sm_100a).
 //
 // Replaces the prompt branch of the reference's attention in Block.__call__
 // (app/engine.py:123-153): for a prompt of P positions the reference expands K/V
 // over the query heads (repeat_interleave) and calls SDPA with is_causal.  Here
-// K/V are read once per KV head from the cache the RoPE/KV-write step filled,
-// and shared by the G = Hq/Hk query heads of that KV head (no copy).
+// K/V are read straight from the cache the RoPE/KV-write step filled, by every
+// query head of the KV head's group (through L2; no expanded copy).
 //
 //   o[b*P + p, h*hd + d] = sum_{j <= p} softmax_j(q_p . k_j * scale) v_j[d]
 //
-// One CTA = (64 query positions, one KV head, one batch row); 4 warps per query
-// head, 16 positions each.  K/V tiles of 64 positions x 128 dims arrive by 2-D
-// TMA (128B swizzle) through a 2-stage ring; QK^T and PV are mma.sync m16n8k16
-// (fp16 in, fp32 accumulate), the online softmax stays in registers and the
-// probabilities are rounded to fp16 for PV (FA2 scheme).  Heavy (late) query
-// tiles are scheduled first.
+// Work item = 128 query positions of one query head and batch row; K/V tiles of 128
+// positions.  Persistent CTAs, one per SM (192 KB of shared memory), each walking the
+// items in longest-first order with a stride of the grid; the K/V tile stream, the S
+// buffers and the P tile run on across items, so the next item's Q load and first S
+// MMAs overlap the current item's last tiles and epilogue.  Warp roles (320 threads):
+//   warp 0     TMA producer: each item's Q tile (once the previous item's last S MMA has
+//              read the buffer), then its K and V tiles through two separate 2-stage
+//              rings (a K slot frees when its S MMA completes, a V slot when its PV MMA
+//              does), 128B-swizzled 128 x 64 boxes.
+//   warp 1     allocates 512 TMEM columns; one thread issues
+//                S_g  = Q K_g^T  (M=128, N=128, K=128; columns 128*(g%2), two buffers)
+//                O   += P_g V_g  (M=128, N=128, K=128; columns 256..383; P_g from
+//                                 shared memory, V_g read as an MN-major operand)
+//              over the global tile sequence g: S_0, S_1, then per tile: O += P_g V_g,
+//              S_{g+2} (whatever item it belongs to), so the tensor core computes
+//              S_{g+1} and PV_g while the softmax works on S_g.  Descriptors are made
+//              once; each operand is one of them plus a constant.
+//   warps 2-9  softmax, two threads per query row (TMEM lane = row; warps w and w+4
+//              share a lane quarter and take key columns 0-63 / 64-127): scaled,
+//              causally masked row max (the two halves swap partial maxima through
+//              shared memory) -> p = 2^(s*scale*log2(e) - m) in fp32 (partial row sums
+//              l) -> rounded to fp16 into the 128B-swizzled K-major P tile.  The running
+//              max m is only raised (and O, l rescaled in TMEM by 2^(m_old - m_new))
+//              when the tile's max exceeds it by more than 8 (a factor 2^8): with a
+//              stale m, p <= 2^8 and O / l is the same quantity.  Per item the epilogue:
+//              O / l -> fp16, staged through this warp's own 32 rows x 64 columns of the
+//              P tile, then written as whole 128-byte row segments.
+// Probabilities are rounded to fp16 for the PV product and the row sum is taken over
+// the fp32 values (the FA2 rounding scheme).  Masked keys (causal, and cache slots at
+// or past P in the diagonal tile, whose V rows are zeroed in shared memory) contribute
+// exact zeros, whatever the cache holds there.  Every wait is bounded (HM_ERR_TIMEOUT in
+// the caller's error word); before exit the producer waits for its copies and the MMA
+// thread for its MMAs.
 #include <cudaTypedefs.h>
 
 #include <mutex>
 #include <unordered_map>
 
 #include "hm_common.cuh"
+#include "tcgen05.cuh"
 
 namespace {
 
-constexpr int kPos = 64;    // positions per K/V tile and per query tile
-constexpr int kNst = 2;
-constexpr int kBox = kPos * 128;  // bytes of one 64-position x 64-dim fp16 box
-constexpr int kMaxGq = 4;
+constexpr int kT = 128;            // query positions per CTA = cache positions per K/V tile
+constexpr int kHD = 128;           // head dim
+constexpr int kBox = kT * 128;     // one 128-row x 64-column fp16 box, 16 KB
+constexpr int kSoftW = 8;         // softmax / epilogue warps
+constexpr int kThreads = 64 + 32 * kSoftW;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kOCol = 256;    // O accumulator columns 256..383
+constexpr float kRescale = 8.f;    // log2 of the growth the stale max may absorb
 
-struct PaSmem {
-  uint8_t k[kNst][2][kBox];
-  uint8_t v[kNst][2][kBox];
-  uint64_t bar[kNst];
+struct FaSmem {
+  uint8_t q[2][kBox];     // [hd half][128 rows x 64]
+  uint8_t k[2][2][kBox];  // [stage][hd half]
+  uint8_t v[2][2][kBox];  // [stage][hd half]
+  uint8_t p[2][kBox];     // [key half]
+  float xch[2][2][kT];    // [tile parity][column half][row]: partial row maxima
+  float xl[2][kT];        // [column half][row]: partial row sums at an item's end
+  uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, pv_done, drain;
+  uint32_t tmem_base;
   int abort_flag;
 };
 
-struct PaParams {
-  const __half* q;
+struct FaParams {
   __half* o;
   int B, P, Hq, Hk, L;
-  float scale;
+  int items;         // ceil(P / 128) * Hq * B
+  float scale_log2;  // scale * log2(e)
   int* err;
 };
 
-__device__ __forceinline__ uint32_t swz(const uint8_t* box, int row, int chunk) {
-  return smem_u32(box + row * 128 + ((chunk ^ (row & 7)) << 4));
+// Work item i in longest-first order: query tile qt (its K/V tiles 0 .. qt), head h,
+// batch row b; heads of one KV group adjacent, so their K/V tiles meet in L2.
+struct Item {
+  int qt, h, b, kh, n;
+};
+HM_DEV Item item_of(const FaParams& p, int i) {
+  const int nqt = (p.P + kT - 1) / kT, per = p.Hq * p.B;
+  Item it;
+  it.qt = nqt - 1 - i / per;
+  const int rest = i % per;
+  it.h = rest % p.Hq;
+  it.b = rest / p.Hq;
+  it.kh = it.h / (p.Hq / p.Hk);
+  it.n = it.qt + 1;
+  return it;
 }
 
-template <int G>
-__global__ void __launch_bounds__(G * 128, 1) prefill_attn_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                                  const __grid_constant__ CUtensorMap vmap,
-                                                                  const __grid_constant__ PaParams Pp) {
-  constexpr int HD = 128;
+HM_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                     const __grid_constant__ CUtensorMap kmap,
+                                                                     const __grid_constant__ CUtensorMap vmap,
+                                                                     const __grid_constant__ FaParams Pp) {
   extern __shared__ uint8_t smem_raw[];
-  PaSmem& sm = *reinterpret_cast<PaSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  FaSmem& sm = *reinterpret_cast<FaSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
   const int P = Pp.P, Hq = Pp.Hq, Hk = Pp.Hk, L = Pp.L;
-  const int nqt = (P + kPos - 1) / kPos;
-  const int qt = nqt - 1 - (int)blockIdx.x;  // late (long) query tiles first
-  const int kh = blockIdx.y, b = blockIdx.z;
-  const int head = kh * G + warp / 4;
-  const int qrow0 = qt * kPos + 16 * (warp & 3);  // first query position of this warp
-  const float scale = Pp.scale;
+  const int i0 = static_cast<int>(blockIdx.x), istep = static_cast<int>(gridDim.x), items = Pp.items;
   int* const err = Pp.err;
   volatile int* abort_s = &sm.abort_flag;
 
   if (tid == 0) {
     sm.abort_flag = 0;
-    for (int i = 0; i < kNst; ++i) mbar_init(&sm.bar[i], 1);
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.k_full[i], 1);
+      mbar_init(&sm.k_empty[i], 1);
+      mbar_init(&sm.v_full[i], 1);
+      mbar_init(&sm.v_empty[i], 1);
+      mbar_init(&sm.s_full[i], 1);
+    }
+    mbar_init(&sm.p_full, kSoftW);  // one arrival per softmax warp
+    mbar_init(&sm.pv_done, 1);
+    mbar_init(&sm.drain, 1);
     fence_barrier_init();
-    prefetch_tensormap(&kmap);
-    prefetch_tensormap(&vmap);
   }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, kTmemCols);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
 
-  const int ntile = qt + 1;  // causal: K/V tiles 0 .. qt
-  const int row0 = (b * Hk + kh) * L;
-  auto issue = [&](int tt) {
-    const int st = tt % kNst;
-    const int y = row0 + tt * kPos;
-    mbar_arrive_expect_tx(&sm.bar[st], 4 * kBox);
-    tma_load_2d_plain(sm.k[st][0], &kmap, 0, y, &sm.bar[st]);
-    tma_load_2d_plain(sm.k[st][1], &kmap, 64, y, &sm.bar[st]);
-    tma_load_2d_plain(sm.v[st][0], &vmap, 0, y, &sm.bar[st]);
-    tma_load_2d_plain(sm.v[st][1], &vmap, 64, y, &sm.bar[st]);
-  };
-  if (tid == 0)
-    for (int tt = 0; tt < kNst && tt < ntile; ++tt) issue(tt);
-
-  // q rows qrow0+g and qrow0+g+8 of this warp's head, as A fragments for 8 k-steps
-  uint32_t qa[8][4];
-  {
-    const int64_t ld = (int64_t)Hq * HD;
-    const int pa = qrow0 + g, pb = qrow0 + g + 8;
-    const __half* qa_p = Pp.q + ((int64_t)b * P + pa) * ld + (int64_t)head * HD;
-    const __half* qb_p = Pp.q + ((int64_t)b * P + pb) * ld + (int64_t)head * HD;
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      int g = 0, k = 0;  // global tile, local item count
+      for (int i = i0; i < items; i += istep, ++k) {
+        const Item it = item_of(Pp, i);
+        if (k > 0) mbar_wait_ab(&sm.q_empty, (k - 1) & 1, err, abort_s);  // previous item's S MMAs done
+        mbar_arrive_expect_tx(&sm.q_full, 2 * kBox);
+        const int qrow = it.b * P + it.qt * kT;
+        tma_load_2d_plain(sm.q[0], &qmap, it.h * kHD, qrow, &sm.q_full);
+        tma_load_2d_plain(sm.q[1], &qmap, it.h * kHD + 64, qrow, &sm.q_full);
+        const int krow = (it.b * Hk + it.kh) * L;
+        for (int t = 0; t < it.n; ++t, ++g) {
+          const int s = g & 1;
+          if (g >= 2) mbar_wait_ab(&sm.k_empty[s], ((g >> 1) - 1) & 1, err, abort_s);
+          mbar_arrive_expect_tx(&sm.k_full[s], 2 * kBox);
+          tma_load_2d_plain(sm.k[s][0], &kmap, 0, krow + t * kT, &sm.k_full[s]);
+          tma_load_2d_plain(sm.k[s][1], &kmap, 64, krow + t * kT, &sm.k_full[s]);
+          if (g >= 2) mbar_wait_ab(&sm.v_empty[s], ((g >> 1) - 1) & 1, err, abort_s);
+          mbar_arrive_expect_tx(&sm.v_full[s], 2 * kBox);
+          tma_load_2d_plain(sm.v[s][0], &vmap, 0, krow + t * kT, &sm.v_full[s]);
+          tma_load_2d_plain(sm.v[s][1], &vmap, 64, krow + t * kT, &sm.v_full[s]);
+        }
+      }
+      // every copy issued has landed before the CTA's shared memory can be released
+      if (k > 0) mbar_wait(&sm.q_full, (k - 1) & 1, err);
+      for (int t = g > 2 ? g - 2 : 0; t < g; ++t) {
+        mbar_wait(&sm.k_full[t & 1], (t >> 1) & 1, err);
+        mbar_wait(&sm.v_full[t & 1], (t >> 1) & 1, err);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_qk = idesc_f16(kT, kT);
+      constexpr uint32_t id_pv = idesc_f16(kT, kHD, false, true);  // V: MN-major (hd contiguous)
+      constexpr uint64_t kBoxD = kBox >> 4;                        // one box in the 16-byte address field
+      const uint64_t dq = sw128_desc(smem_u32(sm.q[0])), dk0 = sw128_desc(smem_u32(sm.k[0][0]));
+      const uint64_t dp = sw128_desc(smem_u32(sm.p[0])), dv0 = sw128_mn_desc(smem_u32(sm.v[0][0]), kBox);
+      // S cursor (two tiles ahead of the PV cursor): item, tile in item, global tile, item count
+      int qi = i0, qj = 0, qg = 0, qk_n = 0, qn = qi < items ? item_of(Pp, qi).n : 0;
+      auto issue_s = [&]() {
+        const int s = qg & 1;
+        if (qj == 0) mbar_wait_ab(&sm.q_full, qk_n & 1, err, abort_s);
+        mbar_wait_ab(&sm.k_full[s], (qg >> 1) & 1, err, abort_s);
+        tc_fence_after();
+        const uint64_t dk = dk0 + 2 * s * kBoxD;
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      qa[ks][0] = pa < P ? *reinterpret_cast<const uint32_t*>(qa_p + 16 * ks + 2 * t) : 0u;
-      qa[ks][1] = pb < P ? *reinterpret_cast<const uint32_t*>(qb_p + 16 * ks + 2 * t) : 0u;
-      qa[ks][2] = pa < P ? *reinterpret_cast<const uint32_t*>(qa_p + 16 * ks + 8 + 2 * t) : 0u;
-      qa[ks][3] = pb < P ? *reinterpret_cast<const uint32_t*>(qb_p + 16 * ks + 8 + 2 * t) : 0u;
+        for (int kk = 0; kk < kHD / 16; ++kk)  // +32 bytes per K=16 step inside a 128-byte row
+          umma_f16(tmem + kT * s, dq + (kk >> 2) * kBoxD + 2 * (kk & 3), dk + (kk >> 2) * kBoxD + 2 * (kk & 3), id_qk,
+                   kk != 0);
+        umma_commit(&sm.k_empty[s]);
+        umma_commit(&sm.s_full[s]);
+        ++qg;
+        if (++qj == qn) {  // the item's last S MMA: its Q buffer frees when this completes
+          umma_commit(&sm.q_empty);
+          qj = 0;
+          ++qk_n;
+          qi += istep;
+          qn = qi < items ? item_of(Pp, qi).n : 0;
+        }
+      };
+      if (qn > 0) issue_s();
+      if (qn > 0) issue_s();
+      int pg = 0;
+      for (int i = i0; i < items; i += istep) {
+        const int n = item_of(Pp, i).n;
+        for (int j = 0; j < n; ++j, ++pg) {
+          const int s = pg & 1;
+          mbar_wait_ab(&sm.p_full, pg & 1, err, abort_s);
+          mbar_wait_ab(&sm.v_full[s], (pg >> 1) & 1, err, abort_s);
+          tc_fence_after();
+          const uint64_t dv = dv0 + 2 * s * kBoxD;
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)  // 16 cache positions = 16 V rows of 128 bytes per step
+            umma_f16(tmem + kOCol, dp + (kk >> 2) * kBoxD + 2 * (kk & 3), dv + kk * (2048 >> 4), id_pv,
+                     (j | kk) != 0);
+          umma_commit(&sm.v_empty[s]);
+          umma_commit(&sm.pv_done);
+          if (qn > 0) issue_s();
+        }
+      }
+      umma_commit(&sm.drain);
+      mbar_wait(&sm.drain, 0, err);  // every MMA of this CTA has completed
+    }
+  } else {
+    // ------------------------------------------------------------ softmax, then epilogue
+    const int q4 = warp & 3;            // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // key columns / head dims 64*half .. +63
+    const int r = 32 * q4 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16) + 64 * half;
+    const float sl2 = Pp.scale_log2;
+    uint8_t* const prow = sm.p[half] + r * 128;  // this thread's P row (keys / head dims 64*half ..)
+    int g = 0;
+    for (int i = i0; i < items; i += istep) {
+      const Item it = item_of(Pp, i);
+      float m = -INFINITY, l = 0.f;  // l: this half's partial row sum
+      for (int j = 0; j < it.n; ++j, ++g) {
+        const int s = g & 1;
+        mbar_wait_ab(&sm.s_full[s], (g >> 1) & 1, err, abort_s);
+        tc_fence_after();
+        uint32_t raw[64];
+        tmem_ld32_nowait(trow + kT * s, raw);
+        tmem_ld32_nowait(trow + kT * s + 32, raw + 32);
+        tmem_wait_ld();
+        float x[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(raw[c]);
+        if (j == it.qt) {  // diagonal tile: keys after the query are masked
+          const int lim = r - 64 * half;  // columns c > lim of this half are masked
+#pragma unroll
+          for (int c = 0; c < 64; ++c) x[c] = c > lim ? -INFINITY : x[c];
+        }
+        float mk[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mk[e] = x[e];
+#pragma unroll
+        for (int c = 8; c < 64; ++c) mk[c & 7] = fmaxf(mk[c & 7], x[c]);
+        const float mpart = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
+                                  fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
+        sm.xch[s][half][r] = mpart;
+        named_bar(1 + q4, 64);  // the two warps of this lane quarter
+        // the same max in both halves: max of the two partial maxima in a fixed order
+        const float mx = fmaxf(sm.xch[s][0][r], sm.xch[s][1][r]) * sl2;
+        float alpha = 1.f;
+        if (mx > m + kRescale) {  // also the first tile (m = -inf): alpha = 0
+          alpha = ex2(m - mx);
+          m = mx;
+        }
+        float sk[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          x[c] = ex2(fmaf(x[c], sl2, -m));
+          sk[c & 7] += x[c];
+        }
+        l = l * alpha + (((sk[0] + sk[1]) + (sk[2] + sk[3])) + ((sk[4] + sk[5]) + (sk[6] + sk[7])));
+        if (j > 0) {
+          // PV of the item's previous tile done: the P tile is free and O holds tiles 0 .. j-1
+          // (at j == 0 the previous item's epilogue already waited for its last PV)
+          mbar_wait_ab(&sm.pv_done, (g - 1) & 1, err, abort_s);
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+            for (int c = 0; c < 64; c += 32) {
+              uint32_t o[32];
+              tmem_ld32_nowait(trow + kOCol + c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st32(trow + kOCol + c, o);
+            }
+            tmem_wait_st();
+          }
+        }
+        // P row r, keys 64*half .. +63, into the K-major 128B-swizzled tile (16-byte chunk ch)
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float* e = x + 8 * ch;
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pack_h2(e[0], e[1]), pack_h2(e[2], e[3]), pack_h2(e[4], e[5]), pack_h2(e[6], e[7]));
+        }
+        if (j == it.qt && (j + 1) * kT > P) {
+          // cache slots P .. of the diagonal tile: their probabilities are 0, but 0 times a
+          // non-finite cache value would not be, so zero those V rows (whole 128-byte rows)
+          mbar_wait_ab(&sm.v_full[s], (g >> 1) & 1, err, abort_s);
+          const int nv = P - j * kT, nz = kT - nv;
+          for (int e = tid - 64; e < 2 * nz * 8; e += 32 * kSoftW) {
+            const int box = e / (nz * 8), rem = e % (nz * 8);
+            *reinterpret_cast<uint4*>(sm.v[s][box] + (nv + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full);
+      }
+      // ---- epilogue: O / l -> fp16 rows qt*128 + r, head dims 64*half .. +63
+      sm.xl[half][r] = l;
+      named_bar(1 + q4, 64);
+      const float lt = sm.xl[0][r] + sm.xl[1][r];
+      mbar_wait_ab(&sm.pv_done, (g - 1) & 1, err, abort_s);  // the item's last PV: O complete, P tile free
+      tc_fence_after();
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t o[32];
+        tmem_ld32_nowait(trow + kOCol + c, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {  // 16-byte chunk (c / 8 + e) of this row's 64 head dims
+          const float* f = reinterpret_cast<const float*>(o + 8 * e);
+          const int ch = c / 8 + e;
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pack_h2(f[0] * inv, f[1] * inv), pack_h2(f[2] * inv, f[3] * inv),
+                         pack_h2(f[4] * inv, f[5] * inv), pack_h2(f[6] * inv, f[7] * inv));
+        }
+      }
+      __syncwarp();  // this warp's 32 rows x 64 columns are staged; write them as row segments
+      __half* const obase = Pp.o + (int64_t)it.h * kHD + 64 * half;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int rr = 32 * q4 + 4 * e + (lane >> 3), ch = lane & 7;  // row, 16-byte chunk
+        const int pos = it.qt * kT + rr;
+        const uint4 v = *reinterpret_cast<const uint4*>(sm.p[half] + rr * 128 + ((ch ^ (rr & 7)) << 4));
+        if (pos < P) *reinterpret_cast<uint4*>(obase + ((int64_t)it.b * P + pos) * ((int64_t)Hq * kHD) + 8 * ch) = v;
+      }
+      __syncwarp();  // reads of the staging rows done before this warp writes the next item's P
     }
   }
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  float acc[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  const int mi = lane >> 3, ri = lane & 7;
-
-  for (int tt = 0; tt < ntile; ++tt) {
-    const int st = tt % kNst;
-    mbar_wait_ab(&sm.bar[st], (tt / kNst) & 1, err, abort_s);  // on timeout: carry on, error flagged
-    if (tt * kPos + kPos > P) {
-      // last tile reaches past the prompt: its masked probabilities are 0, but
-      // 0 * (non-finite cache contents) would not be, so zero those V rows
-      const int nv = P - tt * kPos;
-      for (int i = tid; i < 2 * (kPos - nv) * 8; i += G * 128) {
-        const int box = i / ((kPos - nv) * 8), rem = i % ((kPos - nv) * 8);
-        *reinterpret_cast<uint4*>(sm.v[st][box] + (nv + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
-      }
-      __syncthreads();
-    }
-    // ---- S = Q K^T: 16 query rows x 64 keys (8 n-tiles of 8 keys)
-    float s[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      const int kp = np * 16 + (mi >= 2 ? 8 : 0) + ri;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int c = 2 * ks + (mi & 1);
-        uint32_t b00, b01, b10, b11;
-        ldsm_x4(b00, b01, b10, b11, swz(sm.k[st][c >> 3], kp, c & 7));
-        mma_16816(s[2 * np], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b00, b01);
-        mma_16816(s[2 * np + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b10, b11);
-      }
-    }
-    // ---- causal mask, scale, online softmax (rows g: e = 0,1; row g+8: e = 2,3)
-    const int key0 = tt * kPos;
-    float tmax[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = key0 + 8 * n + 2 * t + (e & 1);
-        const int qp = qrow0 + g + (e >= 2 ? 8 : 0);
-        const float v = key <= qp ? s[n][e] * scale : -INFINITY;
-        s[n][e] = v;
-        tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
-      }
-    float alpha[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 1));
-      tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 2));
-      const float m_new = fmaxf(m_run[h], tmax[h]);
-      alpha[h] = (m_new == -INFINITY || m_run[h] == -INFINITY) ? (m_new == -INFINITY ? 1.f : 0.f)
-                                                                : expf(m_run[h] - m_new);
-      m_run[h] = m_new;
-    }
-    float psum[2] = {0.f, 0.f};
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int h = e >> 1;
-        const float p = (s[n][e] == -INFINITY) ? 0.f : expf(s[n][e] - m_run[h]);
-        s[n][e] = p;
-        psum[h] += p;
-      }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + psum[h];  // quad-partial sums
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      acc[i][0] *= alpha[0];
-      acc[i][1] *= alpha[0];
-      acc[i][2] *= alpha[1];
-      acc[i][3] *= alpha[1];
-    }
-    // ---- acc += fp16(P) V over 4 k-steps of 16 keys
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t pa0 = pack_h2(s[2 * kk][0], s[2 * kk][1]);
-      const uint32_t pa1 = pack_h2(s[2 * kk][2], s[2 * kk][3]);
-      const uint32_t pa2 = pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      const uint32_t pa3 = pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-      const int vp = kk * 16 + (mi & 1) * 8 + ri;
-#pragma unroll
-      for (int nd = 0; nd < 8; ++nd) {
-        const int c = 2 * nd + (mi >> 1);
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_t(v0, v1, v2, v3, swz(sm.v[st][c >> 3], vp, c & 7));
-        mma_16816(acc[2 * nd], pa0, pa1, pa2, pa3, v0, v1);
-        mma_16816(acc[2 * nd + 1], pa0, pa1, pa2, pa3, v2, v3);
-      }
-    }
-    __syncthreads();  // every warp is done with stage st
-    if (tid == 0 && tt + kNst < ntile) issue(tt + kNst);
-  }
-
-  // ---- normalise and store rows g and g+8
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
-  }
-  const int64_t ld = (int64_t)Hq * HD;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int p = qrow0 + g + 8 * h;
-    if (p >= P) continue;
-    const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
-    __half* op = Pp.o + ((int64_t)b * P + p) * ld + (int64_t)head * HD;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      *reinterpret_cast<uint32_t*>(op + 8 * i + 2 * t) = pack_h2(acc[i][2 * h] * inv, acc[i][2 * h + 1] * inv);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
-// [rows, 128] fp16 view of a K or V cache, 64-dim x 64-position boxes, 128B swizzle
-bool kv_map(const void* base, int64_t rows, CUtensorMap* out) {
+// [rows, cols] fp16 (row stride ld elements), 64-column x 128-row boxes, 128B swizzle
+bool fa_map(const void* base, int64_t rows, int64_t cols, int64_t ld, CUtensorMap* out) {
+  struct Key {
+    const void* p;
+    int64_t rows, cols, ld;
+    bool operator==(const Key& o) const { return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld; }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.p) ^ (std::hash<int64_t>()(k.rows) * 31) ^ (std::hash<int64_t>()(k.ld) * 17);
+    }
+  };
   static std::mutex mu;
-  static std::unordered_map<const void*, std::pair<int64_t, CUtensorMap>> cache;
+  static std::unordered_map<Key, CUtensorMap, Hash> cache;
+  const Key key{base, rows, cols, ld};
   {
     std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find(base);
-    if (it != cache.end() && it->second.first == rows) {
-      *out = it->second.second;
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
       return true;
     }
   }
   auto enc = hm_encode_fn();
   if (!enc) return false;
   CUtensorMap m;
-  cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {256};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kPos)};
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kT)};
   cuuint32_t es[2] = {1, 1};
   if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -246,54 +394,50 @@ bool kv_map(const void* base, int64_t rows, CUtensorMap* out) {
     return false;
   std::lock_guard<std::mutex> lk(mu);
   if (cache.size() > 4096) cache.clear();
-  cache[base] = {rows, m};
+  cache[key] = m;
   *out = m;
   return true;
-}
-
-template <int G>
-cudaError_t launch_pa(const CUtensorMap& km, const CUtensorMap& vm, const PaParams& p, dim3 grid, hm_stream_t st) {
-  const size_t smem = sizeof(PaSmem) + 1024;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  return hm_launch(prefill_attn_kernel<G>, grid, dim3(128 * G), smem, st, false, km, vm, p);
 }
 
 }  // namespace
 
 extern "C" int hm_prefill_attn(const void* q, const void* kc, const void* vc, void* o, int B, int P, int Hq, int Hk,
                                int hd, int L, float scale, int* err, hm_stream_t stream) {
-  if (!q || !kc || !vc || !o || B < 1 || P < 1 || Hk < 1 || Hq < Hk || Hq % Hk != 0 || hd != 128 || P > L)
+  if (!q || !kc || !vc || !o || B < 1 || P < 1 || Hk < 1 || Hq < Hk || Hq % Hk != 0 || hd != kHD || P > L)
     return HM_EARG;
-  if (Hq / Hk > kMaxGq) return HM_EARG;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(kc) |
        reinterpret_cast<uintptr_t>(vc)) & 15u)
     return HM_EARG;
-  const int64_t rows = (int64_t)B * Hk * L;
-  CUtensorMap km, vm;
-  if (!kv_map(kc, rows, &km) || !kv_map(vc, rows, &vm)) return HM_EARG;
-  PaParams p;
-  p.q = reinterpret_cast<const __half*>(q);
+  const int64_t kv_rows = (int64_t)B * Hk * L, q_rows = (int64_t)B * P;
+  const int64_t nqt = (P + kT - 1) / kT, items = nqt * Hq * B;
+  if (kv_rows + kT > INT32_MAX || q_rows + kT > INT32_MAX || items > INT32_MAX) return HM_EARG;
+  CUtensorMap qm, km, vm;
+  if (!fa_map(q, q_rows, (int64_t)Hq * kHD, (int64_t)Hq * kHD, &qm) || !fa_map(kc, kv_rows, kHD, kHD, &km) ||
+      !fa_map(vc, kv_rows, kHD, kHD, &vm))
+    return HM_EARG;
+  FaParams p;
   p.o = reinterpret_cast<__half*>(o);
   p.B = B;
   p.P = P;
   p.Hq = Hq;
   p.Hk = Hk;
   p.L = L;
-  p.scale = scale;
+  p.items = static_cast<int>(items);
+  p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err;
-  const dim3 grid((P + kPos - 1) / kPos, Hk, B);
-  cudaError_t e;
-  switch (Hq / Hk) {
-    case 1: e = launch_pa<1>(km, vm, p, grid, stream); break;
-    case 2: e = launch_pa<2>(km, vm, p, grid, stream); break;
-    case 3: e = launch_pa<3>(km, vm, p, grid, stream); break;
-    default: e = launch_pa<4>(km, vm, p, grid, stream); break;
+  const size_t smem = sizeof(FaSmem) + 1024;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    configured = true;
   }
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms < 1)
+    return HM_EARG;
+  const unsigned ctas = static_cast<unsigned>(items < sms ? items : sms);  // persistent: one CTA per SM
+  const cudaError_t e = hm_launch(prefill_attn_tc_kernel, dim3(ctas), dim3(kThreads), smem, stream, false, qm, km, vm, p);
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }

@@ -28,19 +28,25 @@
 //               tile's columns each, scale, round, residual/SiLU, store.
 // Every wait is bounded (HM_ERR_TIMEOUT in the caller's error word).
 //
-// fp16-weight variant (hm_gemm_f16w, WF16): the weights come already converted to fp16
-// (exact int8 values, hm_dequant_i8_f16, once per layer and prompt instead of once per
-// CTA that reads a tile), so TMA writes them straight into the K-major 128B-swizzled
-// layout the MMA reads, in a 4-stage ring of 32 KB B tiles (the int8 and converted-tile
-// buffers of the int8 variant, reused), and warps 2-9 only run the epilogue.  Shared-
-// memory traffic per k-block falls from 128 KB (TMA int8 + conversion read and write +
-// MMA reads) to 96 KB; the products and sums are the same, so are the results.
+// fp16-weight variant (hm_gemm_f16w): the weights come already converted to fp16 (exact
+// int8 values, hm_dequant_i8_f16, once per layer and prompt instead of once per CTA that
+// reads a tile), so TMA writes them straight into the layout the MMA reads, and the tile
+// runs on an SM pair: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16).  Each CTA loads its own 128 rows of A and
+// its half (128 rows) of the weight tile; the leader CTA's thread issues the MMAs, which
+// read both CTAs' shared memory, and its commits arrive on both CTAs' barriers.  Per SM
+// that halves the weight bytes fetched from L2 per MMA: a single-SM 128 x 256 tile needs
+// ~94 bytes per clock of L2 -> shared-memory fill at full tensor rate, above the ~80 B/clk
+// per SM that copies reach when every SM streams at once; the pair needs ~62.  Three
+// 32 KB stages per CTA, two CTAs per SM (one's epilogue overlaps the other's main loop).
+// Products and per-element k order are the same as the int8 variant's, so are the results.
 #include <cudaTypedefs.h>
 
 #include <mutex>
 #include <unordered_map>
 
 #include "hm_common.cuh"
+#include "tcgen05.cuh"
 
 namespace {
 
@@ -61,13 +67,12 @@ struct GemmSmem {
   int abort_flag;
 };
 
-// fp16-weight variant: a 2-stage ring of A (16 KB) + B (32 KB) tiles, 96 KB, so two CTAs
-// share an SM and one's epilogue overlaps the other's main loop (TMEM: 2 x 256 columns)
-constexpr int NSTF = 2;
-struct GemmSmemF {
-  uint8_t a[NSTF][kABytes];
-  uint8_t b[NSTF][kBhBytes];
-  uint64_t full[NSTF], empty[NSTF], acc_full;
+// fp16-weight pair variant: per CTA, a ring of A (128 x 64) and weight-half (128 x 64) tiles
+constexpr int NS2 = 3;
+struct GemmSmem2 {
+  uint8_t a[NS2][kABytes];
+  uint8_t b[NS2][kABytes];
+  uint64_t full[NS2], empty[NS2], acc_full;  // full: used in the leader CTA only
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -83,110 +88,157 @@ struct GemmParams {
   int* err;
 };
 
-// ---------------------------------------------------------------- tcgen05 wrappers
-HM_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-HM_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+HM_DEV float silu_f(float a) { return a / (1.f + expf(-a)); }
 
-HM_DEV void tmem_alloc(uint32_t* dst, uint32_t cols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols)
+// ---------------------------------------------------------------- SM-pair (cta_group::2) primitives
+// TMEM allocation of the pair: one warp of each CTA, same warp and destination in both.
+HM_DEV void tmem_alloc_pair(uint32_t* dst, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols)
                : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
-HM_DEV void tmem_dealloc(uint32_t base, uint32_t cols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols) : "memory");
+HM_DEV void tmem_dealloc_pair(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols) : "memory");
 }
-
-// Shared-memory matrix descriptor: K-major operand in the canonical 128B-swizzle
-// layout (8 rows of 128 bytes per 1024-byte atom, atoms 1024 bytes apart).
-HM_DEV uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address
-  d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (unused for swizzled K-major)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
-  d |= static_cast<uint64_t>(1) << 46;                 // descriptor version (sm_100)
-  d |= static_cast<uint64_t>(2) << 61;                 // swizzle: 128B
-  return d;
+// Tiled 2-D load into this CTA's shared memory, completion counted on an mbarrier of
+// either CTA of the pair (`bar`: shared::cluster address).  No multicast.
+HM_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
-
-// Instruction descriptor: f16 x f16 -> f32, both operands K-major, M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
-  return (1u << 4)                                  // D format f32
-         | (0u << 7) | (0u << 10)                   // A, B format f16
-         | (static_cast<uint32_t>(N >> 3) << 17)    // N / 8
-         | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
-}
-
-HM_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// M=256 MMA over the pair: A rows 0-127 / 128-255 and B rows (N) 0-127 / 128-255 from the
+// same shared-memory offsets of CTA 0 / CTA 1; D rows 0-127 / 128-255 in their TMEM.
+HM_DEV void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-
-// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
-HM_DEV void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-HM_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// Arrive on the barrier at `bar`'s offset in both CTAs of the pair once the MMAs issued so
+// far have completed.
+HM_DEV void umma_commit_pair(uint64_t* bar) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
 }
 
-HM_DEV float silu_f(float a) { return a / (1.f + expf(-a)); }
+// ---------------------------------------------------------------- epilogue (both kernels)
+// warp w (2 .. 2+kConvW-1) owns TMEM lanes 32*(w%4) .. +31 = tile rows m_row0 + 32*(w%4) + lane,
+// and the (w - 2) / 4 -th part of the tile's columns; nt: the tile's column block.
+template <int EPI>
+HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane, int m_row0, int nt) {
+  const int q = warp & 3;
+  constexpr int kParts = kConvW / 4;
+  const int part = (warp - 2) / 4;
+  const int m = m_row0 + 32 * q + lane;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
+  const int N = P.N, M = P.M;
+  const __half* const sc = P.s;
+  __half* const C = P.c;
+  const int64_t ldc = P.ldc;
+  if (EPI == HM_EPI_SILU) {
+    const int f0 = nt * (BN / 2);
+    const int wh = P.wrows_half;
+#pragma unroll 1
+    for (int c0 = part * (BN / 2 / kParts); c0 < (part + 1) * (BN / 2 / kParts); c0 += 16) {
+      float va[16], vb[16];
+      tmem_ld16(trow + c0, va);
+      tmem_ld16(trow + BN / 2 + c0, vb);
+      const int f = f0 + c0;
+      if (m < M && f < N) {
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          float y[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float a = __half2float(__float2half_rn(va[i + e] * __half2float(sc[f + i + e])));
+            const float bb = __half2float(__float2half_rn(vb[i + e] * __half2float(sc[wh + f + i + e])));
+            y[e] = __half2float(__float2half_rn(silu_f(a))) * bb;
+          }
+          out[i / 2] = pack_h2(y[0], y[1]);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + f);
+        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+      }
+    }
+  } else {
+    const int n0 = nt * BN;
+    const __half* const R = P.res;
+    const int64_t ldr = P.ldr;
+#pragma unroll 1
+    for (int c0 = part * (BN / kParts); c0 < (part + 1) * (BN / kParts); c0 += 16) {
+      float v[16];
+      tmem_ld16(trow + c0, v);
+      const int n = n0 + c0;
+      if (m < M && n < N) {
+        uint32_t out[8];
+        uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+        if (R) {
+          const uint4* rp = reinterpret_cast<const uint4*>(R + (int64_t)m * ldr + n);
+          r0 = rp[0];
+          r1 = rp[1];
+        }
+        const __half* rh0 = reinterpret_cast<const __half*>(&r0);
+        const __half* rh1 = reinterpret_cast<const __half*>(&r1);
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          float y[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float t = __half2float(__float2half_rn(v[i + e] * __half2float(sc[n + i + e])));
+            if (R) t += __half2float(i + e < 8 ? rh0[i + e] : rh1[i + e - 8]);
+            y[e] = t;
+          }
+          out[i / 2] = pack_h2(y[0], y[1]);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + n);
+        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+      }
+    }
+  }
+}
 
-template <int EPI, bool WF16>
-__global__ void __launch_bounds__(kThreads, WF16 ? 2 : 1) gemm_i8w_kernel(const __grid_constant__ CUtensorMap amap,
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_constant__ CUtensorMap amap,
                                                                const __grid_constant__ CUtensorMap wmap,
                                                                const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* const sbase = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(sbase);   // int8 weights
-  GemmSmemF& sf = *reinterpret_cast<GemmSmemF*>(sbase);  // fp16 weights
-  constexpr int S = WF16 ? NSTF : NST;                   // ring stages
-  uint64_t* const full = WF16 ? sf.full : sm.full;
-  uint64_t* const empty = WF16 ? sf.empty : sm.empty;
-  uint64_t* const acc_full = WF16 ? &sf.acc_full : &sm.acc_full;
-  uint32_t* const tmem_slot = WF16 ? &sf.tmem_base : &sm.tmem_base;
-  int* const abort_word = WF16 ? &sf.abort_flag : &sm.abort_flag;
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m0 = blockIdx.x * BM;
   const int nt = blockIdx.y;
-  const int K = P.K;
-  const int nk = K / BK;
+  const int nk = P.K / BK;
   int* const err = P.err;
 
   if (tid == 0) {
-    *abort_word = 0;
-    for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
-      // MMA commit (A consumed) + the converter warps (int8 tile consumed); fp16 weights: the commit only
-      mbar_init(&empty[i], WF16 ? 1 : 1 + kConvW);
+    sm.abort_flag = 0;
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1 + kConvW);  // MMA commit (A consumed) + the converter warps (int8 tile consumed)
     }
-    if (!WF16)
-      for (int i = 0; i < 2; ++i) {
-        mbar_init(&sm.bh_full[i], kConvW);
-        mbar_init(&sm.bh_empty[i], 1);
-      }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.bh_full[i], kConvW);
+      mbar_init(&sm.bh_empty[i], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) tmem_alloc(&sm.tmem_base, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  volatile int* abort_s = abort_word;
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort_s = &sm.abort_flag;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -196,44 +248,37 @@ __global__ void __launch_bounds__(kThreads, WF16 ? 2 : 1) gemm_i8w_kernel(const 
       const int r0 = EPI == HM_EPI_SILU ? nt * (BN / 2) : nt * BN;
       const int r1 = EPI == HM_EPI_SILU ? P.wrows_half + nt * (BN / 2) : nt * BN + BN / 2;
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S;
-        if (kb >= S) mbar_wait_ab(&empty[s], ((kb / S) - 1) & 1, err, abort_s);
-        if (WF16) {
-          mbar_arrive_expect_tx(&full[s], kABytes + kBhBytes);
-          tma_load_2d_plain(sf.a[s], &amap, kb * BK, m0, &full[s]);
-          tma_load_2d_plain(sf.b[s], &wmap, kb * BK, r0, &full[s]);
-          tma_load_2d_plain(sf.b[s] + kBhBytes / 2, &wmap, kb * BK, r1, &full[s]);
-        } else {
-          mbar_arrive_expect_tx(&sm.full[s], kABytes + kBqBytes);
-          tma_load_2d_plain(sm.a[s], &amap, kb * BK, m0, &sm.full[s]);
-          tma_load_2d_plain(sm.bq[s], &wmap, kb * BK, r0, &sm.full[s]);
-          tma_load_2d_plain(sm.bq[s] + kBqBytes / 2, &wmap, kb * BK, r1, &sm.full[s]);
-        }
+        const int s = kb % NST;
+        if (kb >= NST) mbar_wait_ab(&sm.empty[s], ((kb / NST) - 1) & 1, err, abort_s);
+        mbar_arrive_expect_tx(&sm.full[s], kABytes + kBqBytes);
+        tma_load_2d_plain(sm.a[s], &amap, kb * BK, m0, &sm.full[s]);
+        tma_load_2d_plain(sm.bq[s], &wmap, kb * BK, r0, &sm.full[s]);
+        tma_load_2d_plain(sm.bq[s] + kBqBytes / 2, &wmap, kb * BK, r1, &sm.full[s]);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BM, BN);
+      const uint64_t a0 = sw128_desc(smem_u32(sm.a[0])), b0 = sw128_desc(smem_u32(sm.bh[0]));
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S, b = kb & 1;
-        mbar_wait_ab(&full[s], (kb / S) & 1, err, abort_s);
-        if (!WF16) mbar_wait_ab(&sm.bh_full[b], (kb >> 1) & 1, err, abort_s);
+        const int s = kb % NST, b = kb & 1;
+        mbar_wait_ab(&sm.full[s], (kb / NST) & 1, err, abort_s);
+        mbar_wait_ab(&sm.bh_full[b], (kb >> 1) & 1, err, abort_s);
         tc_fence_after();
-        const uint64_t ad = sw128_desc(smem_u32(WF16 ? sf.a[s] : sm.a[s]));
-        const uint64_t bd = sw128_desc(smem_u32(WF16 ? sf.b[s] : sm.bh[b]));
+        const uint64_t ad = a0 + s * (kABytes >> 4), bd = b0 + b * (kBhBytes >> 4);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K=16 step inside the 128-byte swizzle row
           umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
-        umma_commit(&empty[s]);
-        if (!WF16) umma_commit(&sm.bh_empty[b]);
+        umma_commit(&sm.empty[s]);
+        umma_commit(&sm.bh_empty[b]);
       }
-      umma_commit(acc_full);
+      umma_commit(&sm.acc_full);
     }
   } else {
     // ------------------------------------------------------------ converters, then epilogue
     const int ct = tid - 64;  // 0 .. 32 * kConvW - 1
-    for (int kb = 0; kb < (WF16 ? 0 : nk); ++kb) {
+    for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % NST, b = kb & 1;
       mbar_wait_ab(&sm.full[s], (kb / NST) & 1, err, abort_s);
       if (kb >= 2) mbar_wait_ab(&sm.bh_empty[b], ((kb >> 1) - 1) & 1, err, abort_s);
@@ -260,88 +305,92 @@ __global__ void __launch_bounds__(kThreads, WF16 ? 2 : 1) gemm_i8w_kernel(const 
         mbar_arrive(&sm.empty[s]);
       }
     }
-    // ---- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 = tile rows, and the
-    // (w - 2) / 4 -th part of the tile's columns
-    mbar_wait_ab(acc_full, 0, err, abort_s);
+    mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
     tc_fence_after();
-    const int q = warp & 3;
-    constexpr int kParts = kConvW / 4;
-    const int part = (warp - 2) / 4;
-    const int m = m0 + 32 * q + lane;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
-    const int N = P.N, M = P.M;
-    const __half* const sc = P.s;
-    __half* const C = P.c;
-    const int64_t ldc = P.ldc;
-    if (EPI == HM_EPI_SILU) {
-      const int f0 = nt * (BN / 2);
-      const int wh = P.wrows_half;
-#pragma unroll 1
-      for (int c0 = part * (BN / 2 / kParts); c0 < (part + 1) * (BN / 2 / kParts); c0 += 16) {
-        float va[16], vb[16];
-        tmem_ld16(trow + c0, va);
-        tmem_ld16(trow + BN / 2 + c0, vb);
-        const int f = f0 + c0;
-        if (m < M && f < N) {
-          uint32_t out[8];
-#pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            float y[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float a = __half2float(__float2half_rn(va[i + e] * __half2float(sc[f + i + e])));
-              const float bb = __half2float(__float2half_rn(vb[i + e] * __half2float(sc[wh + f + i + e])));
-              y[e] = __half2float(__float2half_rn(silu_f(a))) * bb;
-            }
-            out[i / 2] = pack_h2(y[0], y[1]);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + f);
-          dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-          dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
-        }
-      }
-    } else {
-      const int n0 = nt * BN;
-      const __half* const R = P.res;
-      const int64_t ldr = P.ldr;
-#pragma unroll 1
-      for (int c0 = part * (BN / kParts); c0 < (part + 1) * (BN / kParts); c0 += 16) {
-        float v[16];
-        tmem_ld16(trow + c0, v);
-        const int n = n0 + c0;
-        if (m < M && n < N) {
-          uint32_t out[8];
-          uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
-          if (R) {
-            const uint4* rp = reinterpret_cast<const uint4*>(R + (int64_t)m * ldr + n);
-            r0 = rp[0];
-            r1 = rp[1];
-          }
-          const __half* rh0 = reinterpret_cast<const __half*>(&r0);
-          const __half* rh1 = reinterpret_cast<const __half*>(&r1);
-#pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            float y[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              float t = __half2float(__float2half_rn(v[i + e] * __half2float(sc[n + i + e])));
-              if (R) t += __half2float(i + e < 8 ? rh0[i + e] : rh1[i + e - 8]);
-              y[e] = t;
-            }
-            out[i / 2] = pack_h2(y[0], y[1]);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + n);
-          dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-          dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
-        }
-      }
-    }
+    epilogue_tile<EPI>(P, tmem, warp, lane, m0, nt);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// fp16 weights on an SM pair (cluster of two CTAs along M): tile rows pair_m0 .. +255,
+// columns nt*256 .. +255 (SiLU: features nt*128 .. +127 of w1 and of w3).
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 2)
+    gemm_f16w_pair_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+                          const __grid_constant__ GemmParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmem2& sm = *reinterpret_cast<GemmSmem2*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int m_row0 = (blockIdx.x >> 1) * 2 * BM + static_cast<int>(rank) * BM;
+  const int nt = blockIdx.y;
+  const int nk = P.K / BK;
+  int* const err = P.err;
+
+  if (tid == 0) {
+    sm.abort_flag = 0;
+    for (int i = 0; i < NS2; ++i) {
+      mbar_init(&sm.full[i], 1);   // the leader's producer (expect_tx) + both CTAs' copies (bytes)
+      mbar_init(&sm.empty[i], 1);  // the leader's MMA commit
+    }
+    mbar_init(&sm.acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(&sm.tmem_base, kTmemCols);
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort_s = &sm.abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      prefetch_tensormap(&amap);
+      prefetch_tensormap(&wmap);
+      const uint32_t full0 = dsmem_addr(&sm.full[0], 0);  // the leader's ring barriers
+      const int brow = EPI == HM_EPI_SILU ? (rank == 0 ? 0 : P.wrows_half) + nt * (BN / 2)
+                                          : nt * BN + static_cast<int>(rank) * (BN / 2);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % NS2;
+        if (kb >= NS2) mbar_wait_ab(&sm.empty[s], ((kb / NS2) - 1) & 1, err, abort_s);
+        if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 4 * kABytes);  // A + B halves of both CTAs
+        tma_load_2d_pair(sm.a[s], &amap, kb * BK, m_row0, full0 + 8 * s);
+        tma_load_2d_pair(sm.b[s], &wmap, kb * BK, brow, full0 + 8 * s);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16(2 * BM, BN);
+      const uint64_t a0 = sw128_desc(smem_u32(sm.a[0])), b0 = sw128_desc(smem_u32(sm.b[0]));
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % NS2;
+        mbar_wait_ab(&sm.full[s], (kb / NS2) & 1, err, abort_s);
+        tc_fence_after();
+        const uint64_t ad = a0 + s * (kABytes >> 4), bd = b0 + s * (kABytes >> 4);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) umma_f16_pair(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        umma_commit_pair(&sm.empty[s]);
+      }
+      umma_commit_pair(&sm.acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs: their 128 rows)
+    mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
+    tc_fence_after();
+    epilogue_tile<EPI>(P, tmem, warp, lane, m_row0, nt);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA leaves while the pair's copies, MMAs or commits may touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -402,19 +451,25 @@ bool tile_map(const void* p, int64_t rows, int64_t cols, int64_t ld, int kind, C
   return true;
 }
 
-template <int EPI, bool WF16>
-cudaError_t launch_gemm(const CUtensorMap& am, const CUtensorMap& wm, const GemmParams& p, int ntiles_n,
+template <int EPI>
+cudaError_t launch_gemm(const CUtensorMap& am, const CUtensorMap& wm, const GemmParams& p, int ntiles_n, bool wf16,
                         hm_stream_t st) {
-  const size_t smem = (WF16 ? sizeof(GemmSmemF) : sizeof(GemmSmem)) + 1024;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8w_kernel<EPI, WF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  const size_t smem = (wf16 ? sizeof(GemmSmem2) : sizeof(GemmSmem)) + 1024;
+  static bool configured[2] = {false, false};
+  if (!configured[wf16]) {
+    cudaError_t e = wf16 ? cudaFuncSetAttribute(gemm_f16w_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(smem))
+                         : cudaFuncSetAttribute(gemm_i8w_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[wf16] = true;
+  }
+  if (wf16) {
+    const dim3 grid(2 * ((p.M + 2 * BM - 1) / (2 * BM)), ntiles_n);  // whole SM pairs
+    return hm_launch(gemm_f16w_pair_kernel<EPI>, grid, dim3(kThreads), smem, st, false, am, wm, p);
   }
   const dim3 grid((p.M + BM - 1) / BM, ntiles_n);
-  return hm_launch(gemm_i8w_kernel<EPI, WF16>, grid, dim3(kThreads), smem, st, false, am, wm, p);
+  return hm_launch(gemm_i8w_kernel<EPI>, grid, dim3(kThreads), smem, st, false, am, wm, p);
 }
 
 // Shared argument checks and launch of both variants (wf16: w holds fp16 [N, K]).
@@ -443,12 +498,8 @@ int gemm_entry(const void* a, int64_t lda, const void* w, bool wf16, const void*
   p.wrows_half = epi == HM_EPI_SILU ? N / 2 : 0;
   p.err = err;
   const int tn = epi == HM_EPI_SILU ? (nout + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
-  cudaError_t e;
-  if (epi == HM_EPI_SILU)
-    e = wf16 ? launch_gemm<HM_EPI_SILU, true>(am, wm, p, tn, stream) : launch_gemm<HM_EPI_SILU, false>(am, wm, p, tn, stream);
-  else
-    e = wf16 ? launch_gemm<HM_EPI_STORE, true>(am, wm, p, tn, stream)
-             : launch_gemm<HM_EPI_STORE, false>(am, wm, p, tn, stream);
+  const cudaError_t e = epi == HM_EPI_SILU ? launch_gemm<HM_EPI_SILU>(am, wm, p, tn, wf16, stream)
+                                           : launch_gemm<HM_EPI_STORE>(am, wm, p, tn, wf16, stream);
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }
 

@@ -35,6 +35,41 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__
     y[(int64_t)r * D + k] = hmul_rn(__float2half_rn(__half2float(xr[k]) * inv), w[k]);
 }
 
+// Same arithmetic on 8-element chunks (16-byte loads and stores): the prompt-prefill
+// shape (thousands of rows of 3072) is pure HBM traffic, read once and written once.
+__global__ void __launch_bounds__(128) rmsnorm8_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
+                                                       __half* __restrict__ y, int D, float eps) {
+  __shared__ float red[4];
+  const int r = blockIdx.x, tid = threadIdx.x, nc = D / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)r * D);
+  float a = 0.f;
+  for (int c = tid; c < nc; c += 128) {
+    const uint4 v = xr[c];
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+      a += f.x * f.x;
+      a += f.y * f.y;
+    }
+  }
+  a = warp_sum(a);
+  if ((tid & 31) == 0) red[tid >> 5] = a;
+  __syncthreads();
+  const float inv = 1.0f / sqrtf((((red[0] + red[1]) + red[2]) + red[3]) / static_cast<float>(D) + eps);
+  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)r * D);
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  for (int c = tid; c < nc; c += 128) {
+    const uint4 v = xr[c], g = w4[c];
+    uint4 o;
+    o.x = rms_h2(v.x, g.x, inv);
+    o.y = rms_h2(v.y, g.y, inv);
+    o.z = rms_h2(v.z, g.z, inv);
+    o.w = rms_h2(v.w, g.w, inv);
+    yr[c] = o;
+  }
+}
+
 // ------------------------------------------------------------------ RMSNorm from sum-of-squares partials
 // out[r, k] = fp16(fp16(x[r, k] * inv_r) * gamma[k]) with inv_r = 1/sqrt(sum_t ss[t, r] / dim + eps),
 // the partials written by the producer of x (16 columns each).  Every CTA reduces the
@@ -127,6 +162,51 @@ __global__ void rope_kv_kernel(const __half* __restrict__ qkv, const float* __re
     const __half* vs = qkv + (int64_t)r * W + (Hq + Hk + kh) * hd + 2 * i;
     vc[dst] = vs[0];
     vc[dst + 1] = vs[1];
+  }
+}
+
+// Same rotation, 8 head dims (4 pairs) per thread: one 16-byte qkv load, two 16-byte
+// table loads, one 16-byte store (and the 16-byte V copy for a K head).  Threads of
+// a row run over its heads' chunks in order, so every load and store is coalesced.
+__device__ __forceinline__ uint32_t rot_h2(uint32_t xv, float c, float sn) {
+  const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&xv));
+  const __half lo = __float2half_rn(__fsub_rn(__fmul_rn(x.x, c), __fmul_rn(x.y, sn)));
+  const __half hi = __float2half_rn(__fadd_rn(__fmul_rn(x.y, c), __fmul_rn(x.x, sn)));
+  return static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+}
+
+__global__ void __launch_bounds__(256) rope_kv8_kernel(const __half* __restrict__ qkv, const float* __restrict__ rope,
+                                                       int rope_rows, const int64_t* __restrict__ pos,
+                                                       __half* __restrict__ q_out, __half* __restrict__ kc,
+                                                       __half* __restrict__ vc, int R, int S, int Hq, int Hk, int hd,
+                                                       int L, int* err) {
+  const int cph = hd / 8, cpr = (Hq + Hk) * cph;
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (idx >= (int64_t)R * cpr) return;
+  const int r = static_cast<int>(idx / cpr), c = static_cast<int>(idx % cpr);
+  const int h = c / cph, j = c % cph;
+  const int64_t p = pos[r];
+  if (p < 0 || p >= L || p >= rope_rows) {
+    if (c == 0) report_error(err, HM_ERR_BADINDEX);
+    return;
+  }
+  const int64_t W = (int64_t)(Hq + 2 * Hk) * hd;
+  const float4* t4 = reinterpret_cast<const float4*>(rope + (p * (hd / 2) + 4 * j) * 2);
+  const float4 t0 = t4[0], t1 = t4[1];  // (cos, sin) of pairs 4j .. 4j+3
+  const uint4 xv = *reinterpret_cast<const uint4*>(qkv + (int64_t)r * W + (int64_t)h * hd + 8 * j);
+  uint4 o;
+  o.x = rot_h2(xv.x, t0.x, t0.y);
+  o.y = rot_h2(xv.y, t0.z, t0.w);
+  o.z = rot_h2(xv.z, t1.x, t1.y);
+  o.w = rot_h2(xv.w, t1.z, t1.w);
+  if (h < Hq) {
+    *reinterpret_cast<uint4*>(q_out + (int64_t)r * Hq * hd + (int64_t)h * hd + 8 * j) = o;
+  } else {
+    const int kh = h - Hq, b = r / S;
+    const int64_t dst = (((int64_t)b * Hk + kh) * L + p) * hd + 8 * j;
+    *reinterpret_cast<uint4*>(kc + dst) = o;
+    *reinterpret_cast<uint4*>(vc + dst) =
+        *reinterpret_cast<const uint4*>(qkv + (int64_t)r * W + (int64_t)(h + Hk) * hd + 8 * j);
   }
 }
 
@@ -223,8 +303,13 @@ __global__ void frame_commit_kernel(const int64_t* __restrict__ tok_out, int64_t
 
 extern "C" int hm_rmsnorm(const void* x, const void* w, void* y, int R, int D, float eps, hm_stream_t stream) {
   if (!x || !w || !y || R < 1 || D < 1) return HM_EARG;
-  rmsnorm_kernel<<<R, 256, 0, stream>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(w),
-                                        reinterpret_cast<__half*>(y), D, eps);
+  if (D % 8 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                       reinterpret_cast<uintptr_t>(y)) & 15u) == 0)
+    rmsnorm8_kernel<<<R, 128, 0, stream>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(w),
+                                           reinterpret_cast<__half*>(y), D, eps);
+  else
+    rmsnorm_kernel<<<R, 256, 0, stream>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(w),
+                                          reinterpret_cast<__half*>(y), D, eps);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }
@@ -250,9 +335,19 @@ extern "C" int hm_rope_kv_write(const void* qkv, const float* rope, int rope_row
   if (!qkv || !rope || !pos || !q_out || !kc || !vc || R < 1 || S < 1 || hd < 2 || hd % 2 || hd > 2048 || Hq < 1 ||
       Hk < 1)
     return HM_EARG;
-  rope_kv_kernel<<<dim3(R, Hq + Hk), hd / 2, 0, stream>>>(
-      reinterpret_cast<const __half*>(qkv), rope, rope_rows, pos, reinterpret_cast<__half*>(q_out),
-      reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), S, Hq, Hk, hd, L, err);
+  const bool vec = hd % 8 == 0 && ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(rope) |
+                                    reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(kc) |
+                                    reinterpret_cast<uintptr_t>(vc)) & 15u) == 0;
+  if (vec) {
+    const int64_t n = (int64_t)R * (Hq + Hk) * (hd / 8);
+    rope_kv8_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const __half*>(qkv), rope, rope_rows, pos, reinterpret_cast<__half*>(q_out),
+        reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), R, S, Hq, Hk, hd, L, err);
+  } else {
+    rope_kv_kernel<<<dim3(R, Hq + Hk), hd / 2, 0, stream>>>(
+        reinterpret_cast<const __half*>(qkv), rope, rope_rows, pos, reinterpret_cast<__half*>(q_out),
+        reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), S, Hq, Hk, hd, L, err);
+  }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
 }

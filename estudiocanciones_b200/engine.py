@@ -48,6 +48,7 @@ class Linear:
     def __init__(self, q8: torch.Tensor, s8: torch.Tensor):
         self.q8 = q8.contiguous()
         self.s8 = s8.to(torch.float16).contiguous()
+        self.f16 = None  # prompt prefill: the exact fp16 values of q8, kept once made
 
     @property
     def N(self):
@@ -439,7 +440,14 @@ class HeartMuLaLite:
         self.graphs.clear()
         self.backbone.free()
         self.decoder.free()
+        self.drop_prefill_weights()
         torch.cuda.empty_cache()
+
+    def drop_prefill_weights(self):
+        """Free the fp16 copies of the backbone matrices that the prompt prefill keeps."""
+        for b in self.backbone.blocks:
+            for lin in (b.qkv, b.o, b.w13, b.w2):
+                lin.f16 = None
 
     def vram_weights(self):
         tot = 0

@@ -36,8 +36,13 @@ def _rows_to_runtime(rt, x_last: torch.Tensor) -> None:
 
 
 @torch.inference_mode()
-def prefill_backbone(model, h: torch.Tensor) -> None:
-    """h ``[B, P, D]`` fp16 prompt embeddings on the device."""
+def prefill_backbone(model, h: torch.Tensor, keep_f16: bool = True) -> None:
+    """h ``[B, P, D]`` fp16 prompt embeddings on the device.
+
+    keep_f16: the GEMMs read fp16 weight tiles (the exact int8 values); with True each
+    backbone matrix is converted once and the copy kept for later prompts (2 bytes per
+    weight: 5.6 GB at the 3B shape, ``model.drop_prefill_weights()`` frees them), with False
+    every prompt converts each matrix again into one scratch buffer."""
     rt = model._rt
     if rt is None:
         raise HMError("alloc() first")
@@ -52,12 +57,18 @@ def prefill_backbone(model, h: torch.Tensor) -> None:
     pos = torch.arange(P, device=dev, dtype=torch.long).repeat(B)
     b0 = stack.blocks[0]
     q = torch.empty(M, b0.h * b0.hd, device=dev, dtype=torch.float16)
-    # each weight is converted to fp16 once for the whole prompt (exact int8 values, into one
-    # scratch reused by every matrix, stream-ordered) so the GEMMs read their tiles as they are
-    wbuf = torch.empty(max(lin.q8.numel() for lin in (b0.qkv, b0.o, b0.w13, b0.w2)), device=dev, dtype=torch.float16)
+    # each weight in fp16 (exact int8 values) so the GEMMs read their tiles as they are: kept
+    # per matrix, or converted for this prompt into one scratch reused by every matrix
+    wbuf = None if keep_f16 else torch.empty(max(lin.q8.numel() for lin in (b0.qkv, b0.o, b0.w13, b0.w2)),
+                                             device=dev, dtype=torch.float16)
 
     def gemm(a, lin, **kw):
-        wh = kernels.dequant_i8(lin.q8, wbuf[:lin.q8.numel()].view(lin.q8.shape))
+        if keep_f16:
+            if lin.f16 is None:
+                lin.f16 = kernels.dequant_i8(lin.q8)
+            wh = lin.f16
+        else:
+            wh = kernels.dequant_i8(lin.q8, wbuf[:lin.q8.numel()].view(lin.q8.shape))
         return kernels.gemm_f16w(a, wh, lin.s8, **kw)
 
     for blk in stack.blocks:

@@ -97,7 +97,8 @@ def _sdpa_ref(q, kc, vc, B, P, Hq, Hk):
 
 
 @pytest.mark.parametrize("B,P,Hq,Hk,L", [(1, 1, 4, 4, 64), (2, 63, 6, 2, 128), (2, 64, 24, 8, 100),
-                                         (1, 200, 8, 2, 300), (3, 129, 3, 3, 129)])
+                                         (1, 200, 8, 2, 300), (3, 129, 3, 3, 129), (1, 300, 10, 2, 300),
+                                         (2, 1024, 24, 8, 1100), (1, 777, 8, 8, 800)])
 def test_prefill_attn(B, P, Hq, Hk, L):
     from estudiocanciones_b200 import kernels
     gen = torch.Generator().manual_seed(P * 31 + Hq)
@@ -126,8 +127,13 @@ def test_prefill_rejects_unsupported_shapes():
                          None, st) == -1
     q = torch.empty(8, 5 * 128, dtype=torch.float16, device=DEV)
     kv = torch.empty(1, 1, 8, 128, dtype=torch.float16, device=DEV)
-    # 5 query heads per KV head is above the supported group size
-    assert L.hm_prefill_attn(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), q.data_ptr(), 1, 8, 5, 1, 128, 8, 0.1,
+    # head dim 64 is not supported; neither is a query head count that is not a multiple of Hk
+    assert L.hm_prefill_attn(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), q.data_ptr(), 1, 8, 10, 1, 64, 8, 0.1,
+                             None, st) == -1
+    assert L.hm_prefill_attn(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), q.data_ptr(), 1, 8, 5, 2, 128, 8, 0.1,
+                             None, st) == -1
+    # a prompt longer than the cache
+    assert L.hm_prefill_attn(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), q.data_ptr(), 1, 9, 5, 1, 128, 8, 0.1,
                              None, st) == -1
 
 

@@ -33,14 +33,21 @@ def _stream(take: int, n_cb: int = 8) -> torch.Tensor:
     return (torch.arange(n_cb * T, dtype=torch.int64).reshape(n_cb, T) * 7 + take * 1000) % 8197
 
 
-def _worker(rank, world, port, n_takes, to_all, errq):
+def _worker(rank, world, port, n_takes, to_all, errq, known_shape=False):
     try:
         import torch.distributed as dist
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world)
         mine = partition(n_takes, world, rank)
-        out = gather_streams([_stream(t) for t in mine], n_takes, world, rank, to_all=to_all)
+        kw = {"t_cap": 3 + 2 * n_takes, "n_cb": 8} if known_shape else {}
+        calls = []
+        for name in ("all_gather", "gather"):
+            fn = getattr(dist, name)
+            setattr(dist, name, lambda *a, _fn=fn, _n=name, **k: (calls.append(_n), _fn(*a, **k))[1])
+        out = gather_streams([_stream(t) for t in mine], n_takes, world, rank, to_all=to_all, **kw)
+        # one collective when the block shape is known up front, sizes + blocks otherwise
+        assert len(calls) == (1 if known_shape else 2), calls
         if rank == 0 or to_all:
             assert out is not None and len(out) == n_takes
             for t, s in enumerate(out):
@@ -60,12 +67,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("n_takes,to_all", [(4, False), (5, True), (1, True)])
-def test_gather_streams_two_gloo_ranks(n_takes, to_all):
+@pytest.mark.parametrize("n_takes,to_all,known_shape", [(4, False, False), (5, True, False), (1, True, False),
+                                                       (4, False, True), (1, False, True), (3, True, True)])
+def test_gather_streams_two_gloo_ranks(n_takes, to_all, known_shape):
+    """known_shape: the frame cap and codebook count are passed, so the exchange is one
+    fixed-shape gather (all_gather with to_all); otherwise the sizes go first."""
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, n_takes, to_all, errq)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, n_takes, to_all, errq, known_shape)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
