@@ -130,80 +130,92 @@ HM_DEV void umma_commit_pair(uint64_t* bar) {
 }
 
 // ---------------------------------------------------------------- epilogue (both kernels)
-// warp w (2 .. 2+kConvW-1) owns TMEM lanes 32*(w%4) .. +31 = tile rows m_row0 + 32*(w%4) + lane,
-// and the (w - 2) / 4 -th part of the tile's columns; nt: the tile's column block.
+// Runs once every MMA of the tile has completed, so the ring buffers are free: `stage`
+// (>= 64.5 KB of them) holds the tile's fp16 results and the column scales.
+// Phase 1: the column scales (256 values) go to shared memory once; warp w (2 .. 9) reads
+// TMEM lanes 32*(w%4) .. +31 (tile rows) over its part (w-2)/4 of the columns, applies
+// scale (and SiLU), rounds to fp16 and stages the values (row r at 512 r bytes, 16-byte
+// chunk c at slot c ^ (r & 7): conflict-free for both phases).  Phase 2: the same warp
+// copies its own 32 rows out as whole 128/256-byte row segments (16-byte lanes along the
+// row), adding the residual there: y = fp16(fp16(acc * s) + r), the same rounding points.
+constexpr int kStageBytes = BM * 512;
 template <int EPI>
-HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane, int m_row0, int nt) {
-  const int q = warp & 3;
-  constexpr int kParts = kConvW / 4;
-  const int part = (warp - 2) / 4;
-  const int m = m_row0 + 32 * q + lane;
-  const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
+HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane, int m_row0, int nt, uint8_t* stage) {
+  __half* const scl = reinterpret_cast<__half*>(stage + kStageBytes);
+  const int et = (warp - 2) * 32 + lane;  // 0 .. 255
   const int N = P.N, M = P.M;
-  const __half* const sc = P.s;
-  __half* const C = P.c;
-  const int64_t ldc = P.ldc;
-  if (EPI == HM_EPI_SILU) {
-    const int f0 = nt * (BN / 2);
-    const int wh = P.wrows_half;
+  {
+    int src;
+    bool ok;
+    if (EPI == HM_EPI_SILU) {  // w1 scales of features nt*128 .., then w3's
+      const int f = nt * (BN / 2) + (et & (BN / 2 - 1));
+      src = (et < BN / 2 ? 0 : P.wrows_half) + f;
+      ok = f < N;
+    } else {
+      src = nt * BN + et;
+      ok = src < N;
+    }
+    scl[et] = ok ? P.s[src] : __float2half_rn(0.f);
+  }
+  named_bar(1, 32 * kConvW);
+  const int q = warp & 3, part = (warp - 2) / 4;
+  const int r = 32 * q + lane;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
+  uint8_t* const srow = stage + r * 512;
+  constexpr int W = EPI == HM_EPI_SILU ? BN / 4 : BN / 2;  // output columns per warp
 #pragma unroll 1
-    for (int c0 = part * (BN / 2 / kParts); c0 < (part + 1) * (BN / 2 / kParts); c0 += 16) {
+  for (int c0 = part * W; c0 < (part + 1) * W; c0 += 16) {
+    uint32_t out[8];
+    if (EPI == HM_EPI_SILU) {
       float va[16], vb[16];
       tmem_ld16(trow + c0, va);
       tmem_ld16(trow + BN / 2 + c0, vb);
-      const int f = f0 + c0;
-      if (m < M && f < N) {
-        uint32_t out[8];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          float y[2];
+      for (int i = 0; i < 16; i += 2) {
+        float y[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float a = __half2float(__float2half_rn(va[i + e] * __half2float(sc[f + i + e])));
-            const float bb = __half2float(__float2half_rn(vb[i + e] * __half2float(sc[wh + f + i + e])));
-            y[e] = __half2float(__float2half_rn(silu_f(a))) * bb;
-          }
-          out[i / 2] = pack_h2(y[0], y[1]);
+        for (int e = 0; e < 2; ++e) {
+          const float a = __half2float(__float2half_rn(va[i + e] * __half2float(scl[c0 + i + e])));
+          const float bb = __half2float(__float2half_rn(vb[i + e] * __half2float(scl[BN / 2 + c0 + i + e])));
+          y[e] = __half2float(__float2half_rn(silu_f(a))) * bb;
         }
-        uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + f);
-        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+        out[i / 2] = pack_h2(y[0], y[1]);
       }
-    }
-  } else {
-    const int n0 = nt * BN;
-    const __half* const R = P.res;
-    const int64_t ldr = P.ldr;
-#pragma unroll 1
-    for (int c0 = part * (BN / kParts); c0 < (part + 1) * (BN / kParts); c0 += 16) {
+    } else {
       float v[16];
       tmem_ld16(trow + c0, v);
-      const int n = n0 + c0;
-      if (m < M && n < N) {
-        uint32_t out[8];
-        uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
-        if (R) {
-          const uint4* rp = reinterpret_cast<const uint4*>(R + (int64_t)m * ldr + n);
-          r0 = rp[0];
-          r1 = rp[1];
-        }
-        const __half* rh0 = reinterpret_cast<const __half*>(&r0);
-        const __half* rh1 = reinterpret_cast<const __half*>(&r1);
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          float y[2];
+      for (int i = 0; i < 16; i += 2)
+        out[i / 2] = pack_h2(v[i] * __half2float(scl[c0 + i]), v[i + 1] * __half2float(scl[c0 + i + 1]));
+    }
+    const int ch = c0 / 8;
+    *reinterpret_cast<uint4*>(srow + ((ch ^ (r & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(srow + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
+  }
+  __syncwarp();  // this warp's 32 rows x W columns are staged
+  constexpr int cpr = W / 8, rpi = 32 / cpr;  // 16-byte chunks per row, rows per instruction
+  const int col0 = EPI == HM_EPI_SILU ? nt * (BN / 2) : nt * BN;
+  const __half* const R = P.res;
+#pragma unroll 4
+  for (int it = 0; it < 32 / rpi; ++it) {
+    const int rr = 32 * q + it * rpi + lane / cpr, ch = part * cpr + lane % cpr;
+    const int m = m_row0 + rr, col = col0 + 8 * ch;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 512 + ((ch ^ (rr & 7)) << 4));
+    if (m < M && col < N) {
+      uint4 y = v;
+      if (EPI != HM_EPI_SILU && R) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(R + (int64_t)m * P.ldr + col);
+        const uint32_t* a = &v.x;
+        const uint32_t* b = &rv.x;
+        uint32_t* o = &y.x;
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            float t = __half2float(__float2half_rn(v[i + e] * __half2float(sc[n + i + e])));
-            if (R) t += __half2float(i + e < 8 ? rh0[i + e] : rh1[i + e - 8]);
-            y[e] = t;
-          }
-          out[i / 2] = pack_h2(y[0], y[1]);
+        for (int e = 0; e < 4; ++e) {
+          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(a + e));
+          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(b + e));
+          o[e] = pack_h2(fa.x + fb.x, fa.y + fb.y);
         }
-        uint4* dst = reinterpret_cast<uint4*>(C + (int64_t)m * ldc + n);
-        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
       }
+      *reinterpret_cast<uint4*>(P.c + (int64_t)m * P.ldc + col) = y;
     }
   }
 }
@@ -307,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
     }
     mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
     tc_fence_after();
-    epilogue_tile<EPI>(P, tmem, warp, lane, m0, nt);
+    epilogue_tile<EPI>(P, tmem, warp, lane, m0, nt, sm.a[0]);
   }
   tc_fence_before();
   __syncthreads();
@@ -384,7 +396,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 2)
     // ------------------------------------------------------------ epilogue (both CTAs: their 128 rows)
     mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
     tc_fence_after();
-    epilogue_tile<EPI>(P, tmem, warp, lane, m_row0, nt);
+    epilogue_tile<EPI>(P, tmem, warp, lane, m_row0, nt, sm.a[0]);
   }
   tc_fence_before();
   cluster_sync_all();  // neither CTA leaves while the pair's copies, MMAs or commits may touch its memory
@@ -393,6 +405,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 2)
     tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
+
+static_assert(sizeof(GemmSmem::a) + sizeof(GemmSmem::bq) >= kStageBytes + 512, "epilogue staging space (int8 kernel)");
+static_assert(sizeof(GemmSmem2::a) + sizeof(GemmSmem2::b) >= kStageBytes + 512, "epilogue staging space (pair kernel)");
 
 // ---------------------------------------------------------------- host side
 struct MapKey {
