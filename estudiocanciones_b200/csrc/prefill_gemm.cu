@@ -88,7 +88,10 @@ struct GemmParams {
   int* err;
 };
 
-HM_DEV float silu_f(float a) { return a / (1.f + expf(-a)); }
+// SiLU with the fast exponential and division (the value is rounded to fp16 next, so
+// these differ from the IEEE forms by at most one fp16 ulp at a rounding boundary; for
+// a < -87 the quotient is 0, which is also the fp16 value of silu(a) there)
+HM_DEV float silu_f(float a) { return __fdividef(a, 1.f + __expf(-a)); }
 
 // ---------------------------------------------------------------- SM-pair (cta_group::2) primitives
 // TMEM allocation of the pair: one warp of each CTA, same warp and destination in both.
@@ -144,6 +147,22 @@ HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane
   __half* const scl = reinterpret_cast<__half*>(stage + kStageBytes);
   const int et = (warp - 2) * 32 + lane;  // 0 .. 255
   const int N = P.N, M = P.M;
+  const int q = warp & 3, part = (warp - 2) / 4;
+  constexpr int W = EPI == HM_EPI_SILU ? BN / 4 : BN / 2;  // output columns per warp
+  constexpr int cpr = W / 8, rpi = 32 / cpr;              // 16-byte chunks per row, rows per copy instruction
+  constexpr int kIt = 32 / rpi, kHalf = kIt / 2;           // copy instructions, in two batches
+  const int col0 = EPI == HM_EPI_SILU ? nt * (BN / 2) : nt * BN;
+  const __half* const R = P.res;
+  // residual chunks of this lane's copy slots (row 32q + it*rpi + lane/cpr, chunk part*cpr + lane%cpr):
+  // the first batch is requested now, so its latency hides behind the TMEM readout
+  auto res_chunk = [&](int it) {
+    const int rr = 32 * q + it * rpi + lane / cpr, m = m_row0 + rr, col = col0 + 8 * (part * cpr + lane % cpr);
+    return (EPI != HM_EPI_SILU && R && m < M && col < N) ? *reinterpret_cast<const uint4*>(R + (int64_t)m * P.ldr + col)
+                                                          : make_uint4(0, 0, 0, 0);
+  };
+  uint4 rv[kHalf];
+#pragma unroll
+  for (int it = 0; it < kHalf; ++it) rv[it] = res_chunk(it);
   {
     int src;
     bool ok;
@@ -158,11 +177,9 @@ HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane
     scl[et] = ok ? P.s[src] : __float2half_rn(0.f);
   }
   named_bar(1, 32 * kConvW);
-  const int q = warp & 3, part = (warp - 2) / 4;
   const int r = 32 * q + lane;
   const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
   uint8_t* const srow = stage + r * 512;
-  constexpr int W = EPI == HM_EPI_SILU ? BN / 4 : BN / 2;  // output columns per warp
 #pragma unroll 1
   for (int c0 = part * W; c0 < (part + 1) * W; c0 += 16) {
     uint32_t out[8];
@@ -193,29 +210,33 @@ HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane
     *reinterpret_cast<uint4*>(srow + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
   }
   __syncwarp();  // this warp's 32 rows x W columns are staged
-  constexpr int cpr = W / 8, rpi = 32 / cpr;  // 16-byte chunks per row, rows per instruction
-  const int col0 = EPI == HM_EPI_SILU ? nt * (BN / 2) : nt * BN;
-  const __half* const R = P.res;
-#pragma unroll 4
-  for (int it = 0; it < 32 / rpi; ++it) {
-    const int rr = 32 * q + it * rpi + lane / cpr, ch = part * cpr + lane % cpr;
-    const int m = m_row0 + rr, col = col0 + 8 * ch;
-    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 512 + ((ch ^ (rr & 7)) << 4));
-    if (m < M && col < N) {
-      uint4 y = v;
-      if (EPI != HM_EPI_SILU && R) {
-        const uint4 rv = *reinterpret_cast<const uint4*>(R + (int64_t)m * P.ldr + col);
-        const uint32_t* a = &v.x;
-        const uint32_t* b = &rv.x;
-        uint32_t* o = &y.x;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(a + e));
-          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(b + e));
-          o[e] = pack_h2(fa.x + fb.x, fa.y + fb.y);
+  for (int b2 = 0; b2 < 2; ++b2) {
+    if (b2 == 1) {
+#pragma unroll
+      for (int it = 0; it < kHalf; ++it) rv[it] = res_chunk(kHalf + it);
+    }
+#pragma unroll
+    for (int i = 0; i < kHalf; ++i) {
+      const int it = b2 * kHalf + i;
+      const int rr = 32 * q + it * rpi + lane / cpr, ch = part * cpr + lane % cpr;
+      const int m = m_row0 + rr, col = col0 + 8 * ch;
+      const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 512 + ((ch ^ (rr & 7)) << 4));
+      if (m < M && col < N) {
+        uint4 y = v;
+        if (EPI != HM_EPI_SILU && R) {
+          const uint32_t* a = &v.x;
+          const uint32_t* b = &rv[i].x;
+          uint32_t* o = &y.x;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(a + e));
+            const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(b + e));
+            o[e] = pack_h2(fa.x + fb.x, fa.y + fb.y);
+          }
         }
+        *reinterpret_cast<uint4*>(P.c + (int64_t)m * P.ldc + col) = y;
       }
-      *reinterpret_cast<uint4*>(P.c + (int64_t)m * P.ldc + col) = y;
     }
   }
 }
