@@ -134,6 +134,23 @@ HM_DEV float ld_dsmem_f32(uint32_t addr) {
 HM_DEV void st_dsmem_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+// The 32-bit word at local shared address `p` in CTAs 0..7 of the cluster, the eight
+// remote loads issued together (their latencies overlap).
+HM_DEV void ld_dsmem_u32_x8(const void* p, uint32_t (&v)[8]) {
+  asm volatile(
+      "{\n\t.reg .u32 a<8>;\n\t"
+      "mapa.shared::cluster.u32 a0, %8, 0;\n\tmapa.shared::cluster.u32 a1, %8, 1;\n\t"
+      "mapa.shared::cluster.u32 a2, %8, 2;\n\tmapa.shared::cluster.u32 a3, %8, 3;\n\t"
+      "mapa.shared::cluster.u32 a4, %8, 4;\n\tmapa.shared::cluster.u32 a5, %8, 5;\n\t"
+      "mapa.shared::cluster.u32 a6, %8, 6;\n\tmapa.shared::cluster.u32 a7, %8, 7;\n\t"
+      "ld.shared::cluster.u32 %0, [a0];\n\tld.shared::cluster.u32 %1, [a1];\n\t"
+      "ld.shared::cluster.u32 %2, [a2];\n\tld.shared::cluster.u32 %3, [a3];\n\t"
+      "ld.shared::cluster.u32 %4, [a4];\n\tld.shared::cluster.u32 %5, [a5];\n\t"
+      "ld.shared::cluster.u32 %6, [a6];\n\tld.shared::cluster.u32 %7, [a7];\n\t}\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+      : "r"(smem_u32(p))
+      : "memory");
+}
 HM_DEV void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 // Arrive (release at cluster scope) on an mbarrier of another CTA of the cluster.
 HM_DEV void mbar_arrive_dsmem(uint32_t remote_bar) {
