@@ -57,6 +57,43 @@ def shard_files(d) -> list[Path]:
     return [d / "model.safetensors"]
 
 
+def convert_entry(k: str, t: torch.Tensor, quant, keep_emb: bool = False) -> dict[str, torch.Tensor]:
+    """The converted form of one checkpoint tensor (``app/convert_final.py:30-47``): dropped
+    (RoPE tables, ``muq_linear.weight``), split per head and quantised (``audio_head``
+    ``[heads, D, V]`` -> ``audio_head.<i>.q8/.s8`` ``[V, D]``), quantised (other 2-D
+    tensors except the unconditional embedding and, with ``keep_emb``, the embedding
+    tables) or kept as bf16."""
+    if "pos_embeddings" in k or k == "muq_linear.weight":
+        return {}
+    out = {}
+    if k == "audio_head":  # [heads, D, V]: one [V, D] matrix per head
+        for i in range(t.shape[0]):
+            out[f"audio_head.{i}.q8"], out[f"audio_head.{i}.s8"] = quant(t[i].t().contiguous())
+    elif t.dim() == 2 and k != "unconditional_text_embedding.weight" and not (keep_emb and "embeddings" in k):
+        out[k + ".q8"], out[k + ".s8"] = quant(t)
+    else:
+        out[k] = t.to(torch.bfloat16).contiguous()
+    return out
+
+
+def quantize_plain(t: dict[str, torch.Tensor], quant=None) -> dict[str, torch.Tensor]:
+    """A loaded checkpoint with every plain (un-quantised) weight converted as the converter
+    would (the reference also loads fp16/bf16 ``Linear`` weights, a bf16 ``audio_head``
+    ``[heads, D, V]`` and bf16 embedding tables: ``app/engine.py:235-260``).  Tensors
+    already in the int8 format pass through; the result is what ``convert_tensors`` makes
+    of the same weights, on the tensors' device."""
+    quant = quant or q8_rows
+    out: dict[str, torch.Tensor] = {}
+    for k, v in t.items():
+        if k.endswith((".q8", ".s8")) or k in ("unconditional_text_embedding.weight", "muq_linear.bias"):
+            out[k] = v
+        elif v.dim() == 1 and not k == "audio_head":  # norm scales, biases
+            out[k] = v
+        else:
+            out.update(convert_entry(k, v, quant))
+    return out
+
+
 def convert_tensors(src, keep_emb: bool = False, device="cuda", quant=None) -> dict[str, torch.Tensor]:
     """Converted tensors (on the host) of the checkpoint directory ``src``.  ``quant``
     replaces the quantiser (default: :func:`q8_rows` on ``device``)."""
@@ -66,19 +103,8 @@ def convert_tensors(src, keep_emb: bool = False, device="cuda", quant=None) -> d
     for sh in shard_files(src):
         with safe_open(str(sh), "pt", device=str(device)) as f:
             for k in f.keys():
-                if "pos_embeddings" in k or k == "muq_linear.weight":
-                    continue
-                t = f.get_tensor(k)
-                if k == "audio_head":  # [heads, D, V]: one [V, D] matrix per head
-                    for i in range(t.shape[0]):
-                        q, s = quant(t[i].t().contiguous())
-                        out[f"audio_head.{i}.q8"], out[f"audio_head.{i}.s8"] = q.cpu(), s.cpu()
-                elif t.dim() == 2 and k != "unconditional_text_embedding.weight" and not (
-                        keep_emb and "embeddings" in k):
-                    q, s = quant(t)
-                    out[k + ".q8"], out[k + ".s8"] = q.cpu(), s.cpu()
-                else:
-                    out[k] = t.to(torch.bfloat16).contiguous().cpu()
+                for kk, v in convert_entry(k, f.get_tensor(k), quant, keep_emb).items():
+                    out[kk] = v.cpu()
     return out
 
 

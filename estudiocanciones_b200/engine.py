@@ -391,7 +391,11 @@ class HeartMuLaLite:
         self.dt = torch.float16
         self.fast = True
         _lib.lib()
-        t = load_tensors(weights, device=self.dev)
+        # plain fp16/bf16 weights (the reference's Linear(w=...) and bf16 audio_head / embedding
+        # branches, app/engine.py:235-260) are quantised on load as the converter would: the
+        # B200 path computes with int8 weights, so such a checkpoint runs as its int8 conversion
+        from .convert import quantize_plain
+        t = quantize_plain(load_tensors(weights, device=self.dev))
         self.shape = shape_from_tensors(t, bb_heads, dec_heads)
 
         def get(name, norm=False):
@@ -418,6 +422,8 @@ class HeartMuLaLite:
     # ------------------------------------------------------------------ runtime state
     def alloc(self, n_takes, B, L):
         """Caches (``app/engine.py:386-388``), frame buffers and the frame plan."""
+        if self.dev.type != "cuda":
+            raise _lib.HMError(f"the weights are on {self.dev}: move the model to a CUDA device (to('cuda')) first")
         self._drop_runtime()
         self.N, self.B = n_takes, B
         self.backbone.alloc(B, L, self.dev)
@@ -442,6 +448,39 @@ class HeartMuLaLite:
         self.decoder.free()
         self.drop_prefill_weights()
         torch.cuda.empty_cache()
+
+    def to(self, device):
+        """Move the weights to ``device`` (``app/engine.py:267-288``), e.g. to the host while
+        the codec uses the GPU and back.  The frame runtime, CUDA graphs, KV caches and the
+        prefill's fp16 weight copies hold device memory and device pointers: they are
+        released first and rebuilt by the next ``alloc``/``generate``.  The engine computes on
+        CUDA devices only; on another device the model just holds its weights."""
+        device = torch.device(device)
+        self._drop_runtime()
+        self.graphs.clear()
+        self.backbone.free()
+        self.decoder.free()
+        self.drop_prefill_weights()
+
+        def mv(o):
+            for k, v in list(vars(o).items()):
+                if torch.is_tensor(v):
+                    setattr(o, k, v.to(device, non_blocking=True))
+                elif isinstance(v, (Linear, Emb, Block, Stack)):
+                    mv(v)
+                elif isinstance(v, list):
+                    for x in v:
+                        if isinstance(x, (Linear, Emb, Block)):
+                            mv(x)
+        for o in (self.backbone, self.decoder, self.text_emb, self.audio_emb, self.projection, self.c0_head,
+                  *self.audio_head):
+            mv(o)
+        self.uncond, self.muq_b, self.cb_off = (x.to(device) for x in (self.uncond, self.muq_b, self.cb_off))
+        self.dev = device
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+        return self
 
     def drop_prefill_weights(self):
         """Free the fp16 copies of the backbone matrices that the prompt prefill keeps."""

@@ -102,3 +102,22 @@ def test_converter_writes_the_checkpoint_format(tmp_path):
 def test_q8_rows_refuses_cpu_tensors():
     with pytest.raises(Exception, match="CUDA"):
         convert.q8_rows(torch.zeros(2, 4))
+
+
+def test_plain_weights_are_quantised_on_load_as_the_converter_would(tmp_path):
+    """A checkpoint with plain fp weights (the reference's Linear(w=...), bf16 audio_head
+    [heads, D, V] and embedding branches) becomes, on load, what the converter makes of it;
+    int8 tensors pass through unchanged."""
+    t = fake_official(tmp_path, sharded=False)
+    conv = convert.convert_tensors(tmp_path, device="cpu", quant=O.q8_rows)
+    loaded = {k: v for k, v in t.items()}
+    got = convert.quantize_plain(loaded, quant=O.q8_rows)
+    for k, v in conv.items():
+        if k.endswith((".q8", ".s8")):
+            assert torch.equal(got[k].view(torch.int8) if got[k].dtype == torch.int8 else got[k].view(torch.int16),
+                               v.view(torch.int8) if v.dtype == torch.int8 else v.view(torch.int16)), k
+    assert "audio_head" not in got and "audio_head.2.q8" in got and "muq_linear.weight" not in got
+    assert "backbone.pos_embeddings.weight" not in got
+    assert torch.equal(got["backbone.layers.0.sa_norm.scale"], t["backbone.layers.0.sa_norm.scale"])
+    again = convert.quantize_plain(got, quant=O.q8_rows)  # already converted: a pass-through
+    assert sorted(again) == sorted(got) and all(again[k] is got[k] for k in got)
