@@ -11,6 +11,11 @@ becomes ``<key>.q8`` int8 ``[N, K]`` + ``<key>.s8`` bf16 ``[N]``; ``audio_head``
 MuQ input is always zero so only the bias counts); everything else is stored as bf16.
 
     python -m estudiocanciones_b200.convert <HeartMuLa dir> <out.safetensors> [--keep-emb-bf16]
+    python -m estudiocanciones_b200.convert <HeartMuLa dir> <HeartCodec dir> <out dir> [--keep-emb-bf16]
+
+The second form is the reference's full command (``app/convert_final.py:60-66``): it
+writes ``mula_int8.safetensors`` and ``codec_bf16.safetensors`` (:func:`convert_codec`)
+into ``<out dir>``.
 """
 from __future__ import annotations
 
@@ -116,10 +121,42 @@ def convert_mula(src, dst, keep_emb: bool = False, device="cuda", quant=None) ->
     return sorted(out)
 
 
+def convert_codec(src, dst) -> list[str]:
+    """The codec's distribution file (``app/convert_final.py:50-58``): every tensor of the
+    HeartCodec checkpoint except the waveform encoder (``scalar_model.encoder.*``, not used
+    to generate), floating tensors cast to bf16, written to ``dst``; the codec's
+    ``config.json`` is copied beside it as ``dst`` with a ``.json`` suffix.  Returns the keys."""
+    import shutil
+    from safetensors import safe_open
+    from safetensors.torch import save_file
+    out: dict[str, torch.Tensor] = {}
+    for sh in shard_files(src):
+        with safe_open(str(sh), "pt") as f:
+            for k in f.keys():
+                if k.startswith("scalar_model.encoder"):
+                    continue
+                t = f.get_tensor(k)
+                out[k] = t.to(torch.bfloat16).contiguous() if t.is_floating_point() else t
+    save_file(out, str(dst))
+    shutil.copy(Path(src) / "config.json", Path(dst).with_suffix(".json"))
+    return sorted(out)
+
+
 if __name__ == "__main__":
-    if len(sys.argv) < 3:
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    if len(args) < 2:
         raise SystemExit(__doc__)
-    dst = Path(sys.argv[2])
-    dst.parent.mkdir(parents=True, exist_ok=True)
-    convert_mula(sys.argv[1], dst, "--keep-emb-bf16" in sys.argv)
-    print(dst.name, round(dst.stat().st_size / 1e9, 2), "GB")
+    keep = "--keep-emb-bf16" in sys.argv
+    if len(args) >= 3:  # <mula dir> <codec dir> <out dir>, as app/convert_final.py
+        outdir = Path(args[2])
+        outdir.mkdir(parents=True, exist_ok=True)
+        convert_mula(args[0], outdir / "mula_int8.safetensors", keep)
+        convert_codec(args[1], outdir / "codec_bf16.safetensors")
+        files = sorted(outdir.glob("*.safetensors"))
+    else:
+        dst = Path(args[1])
+        dst.parent.mkdir(parents=True, exist_ok=True)
+        convert_mula(args[0], dst, keep)
+        files = [dst]
+    for f in files:
+        print(f.name, round(f.stat().st_size / 1e9, 2), "GB")

@@ -121,3 +121,30 @@ def test_plain_weights_are_quantised_on_load_as_the_converter_would(tmp_path):
     assert torch.equal(got["backbone.layers.0.sa_norm.scale"], t["backbone.layers.0.sa_norm.scale"])
     again = convert.quantize_plain(got, quant=O.q8_rows)  # already converted: a pass-through
     assert sorted(again) == sorted(got) and all(again[k] is got[k] for k in got)
+
+
+def test_convert_codec_drops_the_encoder_and_casts_to_bf16(tmp_path):
+    """``convert_codec`` (app/convert_final.py:50-58): encoder keys dropped, floating
+    tensors bf16, integer tensors unchanged, config.json copied beside the output."""
+    from safetensors import safe_open
+    from safetensors.torch import save_file
+    src = tmp_path / "codec"
+    src.mkdir()
+    g = torch.Generator().manual_seed(9)
+    t = {"scalar_model.encoder.conv.weight": torch.randn(4, 3, generator=g),
+         "scalar_model.decoder.conv.weight": torch.randn(4, 3, generator=g),
+         "flow_matching.estimator.proj.weight": torch.randn(2, 5, generator=g, dtype=torch.float64),
+         "quantizer.codebook_size": torch.tensor([8192], dtype=torch.int64)}
+    save_file(t, str(src / "model.safetensors"))
+    (src / "config.json").write_text('{"sample_rate": 48000}')
+    dst = tmp_path / "out" / "codec_bf16.safetensors"
+    dst.parent.mkdir()
+    keys = convert.convert_codec(src, dst)
+    assert keys == sorted(k for k in t if not k.startswith("scalar_model.encoder"))
+    with safe_open(str(dst), "pt") as f:
+        assert f.get_tensor("scalar_model.decoder.conv.weight").dtype == torch.bfloat16
+        assert torch.equal(f.get_tensor("scalar_model.decoder.conv.weight"),
+                           t["scalar_model.decoder.conv.weight"].to(torch.bfloat16))
+        assert f.get_tensor("flow_matching.estimator.proj.weight").dtype == torch.bfloat16
+        assert torch.equal(f.get_tensor("quantizer.codebook_size"), t["quantizer.codebook_size"])
+    assert (tmp_path / "out" / "codec_bf16.json").read_text() == '{"sample_rate": 48000}'
