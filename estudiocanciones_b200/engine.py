@@ -441,12 +441,13 @@ class HeartMuLaLite:
         self._rt = None
 
     def release(self):
-        """Free caches, graphs and buffers (``app/engine.py:463-469``)."""
+        """Free caches, graphs and buffers (``app/engine.py:463-469``).  Weights stay, the
+        prefill's fp16 copies of the backbone matrices included (``drop_prefill_weights``
+        or ``to`` free those)."""
         self._drop_runtime()
         self.graphs.clear()
         self.backbone.free()
         self.decoder.free()
-        self.drop_prefill_weights()
         torch.cuda.empty_cache()
 
     def to(self, device):
