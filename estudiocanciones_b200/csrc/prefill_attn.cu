@@ -20,8 +20,8 @@
 //              does), 128B-swizzled 128 x 64 boxes.
 //   warp 1     allocates 512 TMEM columns; one thread issues
 //                S_g  = Q K_g^T  (M=128, N=128, K=128; columns 128*(g%2), two buffers)
-//                O   += P_g V_g  (M=128, N=128, K=128; columns 256..383; P_g from
-//                                 shared memory, V_g read as an MN-major operand)
+//                O   += P_g V_g  (M=128, N=128, K=128; columns 256..383; P_g read from
+//                                 TMEM columns 384..447, V_g as an MN-major operand)
 //              over the global tile sequence g: S_0, S_1, then per tile: O += P_g V_g,
 //              S_{g+2} (whatever item it belongs to), so the tensor core computes
 //              S_{g+1} and PV_g while the softmax works on S_g.  Descriptors are made
@@ -30,12 +30,12 @@
 //              share a lane quarter and take key columns 0-63 / 64-127): scaled,
 //              causally masked row max (the two halves swap partial maxima through
 //              shared memory) -> p = 2^(s*scale*log2(e) - m) in fp32 (partial row sums
-//              l) -> rounded to fp16 into the 128B-swizzled K-major P tile.  The running
+//              l) -> rounded to fp16 pairs and stored to TMEM (tcgen05.st).  The running
 //              max m is only raised (and O, l rescaled in TMEM by 2^(m_old - m_new))
 //              when the tile's max exceeds it by more than 8 (a factor 2^8): with a
 //              stale m, p <= 2^8 and O / l is the same quantity.  Per item the epilogue:
-//              O / l -> fp16, staged through this warp's own 32 rows x 64 columns of the
-//              P tile, then written as whole 128-byte row segments.
+//              O / l -> fp16, staged through this warp's own 32 rows x 64 columns of a
+//              shared-memory tile, then written as whole 128-byte row segments.
 // Probabilities are rounded to fp16 for the PV product and the row sum is taken over
 // the fp32 values (the FA2 rounding scheme).  Masked keys (causal, and cache slots at
 // or past P in the diagonal tile, whose V rows are zeroed in shared memory) contribute
@@ -59,13 +59,14 @@ constexpr int kSoftW = 8;         // softmax / epilogue warps
 constexpr int kThreads = 64 + 32 * kSoftW;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;    // O accumulator columns 256..383
+constexpr uint32_t kPCol = 384;    // P: fp16 pairs of the 128 keys in columns 384..447
 constexpr float kRescale = 8.f;    // log2 of the growth the stale max may absorb
 
 struct FaSmem {
   uint8_t q[2][kBox];     // [hd half][128 rows x 64]
   uint8_t k[2][2][kBox];  // [stage][hd half]
   uint8_t v[2][2][kBox];  // [stage][hd half]
-  uint8_t p[2][kBox];     // [key half]
+  uint8_t p[2][kBox];     // [head-dim half]: the epilogue's staging of O / l
   float xch[2][2][kT];    // [tile parity][column half][row]: partial row maxima
   float xl[2][kT];        // [column half][row]: partial row sums at an item's end
   uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, pv_done, drain;
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       constexpr uint32_t id_pv = idesc_f16(kT, kHD, false, true);  // V: MN-major (hd contiguous)
       constexpr uint64_t kBoxD = kBox >> 4;                        // one box in the 16-byte address field
       const uint64_t dq = sw128_desc(smem_u32(sm.q[0])), dk0 = sw128_desc(smem_u32(sm.k[0][0]));
-      const uint64_t dp = sw128_desc(smem_u32(sm.p[0])), dv0 = sw128_mn_desc(smem_u32(sm.v[0][0]), kBox);
+      const uint64_t dv0 = sw128_mn_desc(smem_u32(sm.v[0][0]), kBox);
       // S cursor (two tiles ahead of the PV cursor): item, tile in item, global tile, item count
       int qi = i0, qj = 0, qg = 0, qk_n = 0, qn = qi < items ? item_of(Pp, qi).n : 0;
       auto issue_s = [&]() {
@@ -216,8 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
           const uint64_t dv = dv0 + 2 * s * kBoxD;
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)  // 16 cache positions = 16 V rows of 128 bytes per step
-            umma_f16(tmem + kOCol, dp + (kk >> 2) * kBoxD + 2 * (kk & 3), dv + kk * (2048 >> 4), id_pv,
-                     (j | kk) != 0);
+            umma_f16_ts(tmem + kOCol, tmem + kPCol + 8 * kk, dv + kk * (2048 >> 4), id_pv, (j | kk) != 0);
           umma_commit(&sm.v_empty[s]);
           umma_commit(&sm.pv_done);
           if (qn > 0) issue_s();
@@ -233,7 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
     const int r = 32 * q4 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16) + 64 * half;
     const float sl2 = Pp.scale_log2;
-    uint8_t* const prow = sm.p[half] + r * 128;  // this thread's P row (keys / head dims 64*half ..)
+    uint8_t* const prow = sm.p[half] + r * 128;  // this thread's staging row (head dims 64*half ..)
+    const uint32_t tp = tmem + (static_cast<uint32_t>(32 * q4) << 16) + kPCol + 32 * half;  // its P columns
     int g = 0;
     for (int i = i0; i < items; i += istep) {
       const Item it = item_of(Pp, i);
@@ -295,12 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
             tmem_wait_st();
           }
         }
-        // P row r, keys 64*half .. +63, into the K-major 128B-swizzled tile (16-byte chunk ch)
+        {  // P row r, keys 64*half .. +63, as fp16 pairs into TMEM (the A operand of PV)
+          uint32_t pk[32];
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float* e = x + 8 * ch;
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pack_h2(e[0], e[1]), pack_h2(e[2], e[3]), pack_h2(e[4], e[5]), pack_h2(e[6], e[7]));
+          for (int e = 0; e < 32; ++e) pk[e] = pack_h2(x[2 * e], x[2 * e + 1]);
+          tmem_st32(tp, pk);
+          tmem_wait_st();
         }
         if (j == it.qt && (j + 1) * kT > P) {
           // cache slots P .. of the diagonal tile: their probabilities are 0, but 0 times a
@@ -311,8 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
             const int box = e / (nz * 8), rem = e % (nz * 8);
             *reinterpret_cast<uint4*>(sm.v[s][box] + (nv + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
           }
+          fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
         }
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.p_full);
