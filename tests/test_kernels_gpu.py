@@ -355,6 +355,23 @@ def test_sampler_matches_oracle(seed):
     assert torch.equal(out[:, :1].cpu(), ref)
 
 
+@pytest.mark.parametrize("N,cfg,topk,temp", [(8, 1.5, 50, 1.0), (1, 1.0, 50, 1.0), (3, 2.0, 100, 0.9)])
+def test_sampler_cluster_shapes_match_oracle(N, cfg, topk, temp):
+    """The sampler's cluster split at other take counts: config 4's 8 takes x CFG (64 CTAs),
+    one take without CFG, an odd count; vocabularies that do not divide by the cluster."""
+    from estudiocanciones_b200 import kernels
+    for V in (8197, 4099):
+        gen = torch.Generator().manual_seed(N * 1000 + V)
+        B = 2 * N if cfg != 1.0 else N
+        logits = (torch.randn(B, V, generator=gen) * 4).half()
+        noise = torch.empty(N, V).exponential_(1, generator=gen)
+        out = torch.full((B, 8), -1, dtype=torch.long, device=DEV)
+        kernels.sample(logits.to(DEV), N, cfg, topk, temp, noise.to(DEV), out, 5)
+        ref = O.guided_sample(logits, N, cfg, topk, temp, noise)
+        assert torch.equal(out[:, 5:6].cpu(), ref), V
+    assert kernels.read_errors(DEV) == 0
+
+
 def test_rms_apply_equals_fused_rms_prologue():
     """hm_rms_apply (RMSNorm from the producer's sum-of-squares partials, one launch)
     gives exactly the rows the GEMV's fused RMSNorm prologue feeds its MMAs: a GEMV on
