@@ -29,16 +29,16 @@
 // Every wait is bounded (HM_ERR_TIMEOUT in the caller's error word).
 //
 // fp16-weight variant (hm_gemm_f16w): the weights come already converted to fp16 (exact
-// int8 values, hm_dequant_i8_f16, once per layer and prompt instead of once per CTA that
-// reads a tile), so TMA writes them straight into the layout the MMA reads, and the tile
-// runs on an SM pair: a cluster of two CTAs computes a 256 x 256 tile with
+// int8 values, hm_dequant_i8_f16, made once), so TMA writes them straight into the layout
+// the MMA reads, and the tiles run on SM pairs: a cluster of two CTAs computes 256 x 256 tiles with
 // tcgen05.mma.cta_group::2 (M=256, N=256, K=16).  Each CTA loads its own 128 rows of A and
 // its half (128 rows) of the weight tile; the leader CTA's thread issues the MMAs, which
 // read both CTAs' shared memory, and its commits arrive on both CTAs' barriers.  Per SM
 // that halves the weight bytes fetched from L2 per MMA: a single-SM 128 x 256 tile needs
 // ~94 bytes per clock of L2 -> shared-memory fill at full tensor rate, above the ~80 B/clk
-// per SM that copies reach when every SM streams at once; the pair needs ~62.  Three
-// 32 KB stages per CTA, two CTAs per SM (one's epilogue overlaps the other's main loop).
+// per SM that copies reach when every SM streams at once; the pair needs ~62.
+// Persistent: one CTA per SM, five 32 KB stages, two TMEM accumulators per CTA (one
+// tile's epilogue overlaps the next tile's main loop).
 // Products and per-element k order are the same as the int8 variant's, so are the results.
 #include <cudaTypedefs.h>
 
@@ -67,12 +67,17 @@ struct GemmSmem {
   int abort_flag;
 };
 
-// fp16-weight pair variant: per CTA, a ring of A (128 x 64) and weight-half (128 x 64) tiles
-constexpr int NS2 = 3;
+// fp16-weight pair variant (persistent): per CTA, a ring of A (128 x 64) and weight-half
+// (128 x 64) tiles, the epilogue's own staging and two sets of column scales
+constexpr int NS2 = 5;
+constexpr int kStageBytesP = 128 * 512;  // 128 rows x 256 fp16 results
 struct GemmSmem2 {
   uint8_t a[NS2][kABytes];
   uint8_t b[NS2][kABytes];
-  uint64_t full[NS2], empty[NS2], acc_full;  // full: used in the leader CTA only
+  uint8_t stage[kStageBytesP];
+  __half scl[2][256];
+  uint64_t full[NS2], empty[NS2];  // full: used in the leader CTA only
+  uint64_t acc_full[2], acc_empty[2];  // acc_empty: the leader's, 8 warps of each CTA arrive
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -85,6 +90,8 @@ struct GemmParams {
   int64_t ldc;
   int M, N, K;  // N: output columns (features for SiLU)
   int wrows_half;  // SiLU: row offset of w3 inside W (= features)
+  int ntiles;      // tiles along N (the pair kernel's tile loop)
+  int n_fast;      // pair kernel: consecutive tiles walk N (1) or M (0)
   int* err;
 };
 
@@ -133,8 +140,9 @@ HM_DEV void umma_commit_pair(uint64_t* bar) {
 }
 
 // ---------------------------------------------------------------- epilogue (both kernels)
-// Runs once every MMA of the tile has completed, so the ring buffers are free: `stage`
-// (>= 64.5 KB of them) holds the tile's fp16 results and the column scales.
+// Runs once every MMA of the tile has completed: `stage` (64 KB) holds the tile's fp16
+// results, `scl` (256 values) its column scales; `release()` runs once the warp's TMEM
+// reads are complete (the persistent kernel hands the accumulator back to the MMA there).
 // Phase 1: the column scales (256 values) go to shared memory once; warp w (2 .. 9) reads
 // TMEM lanes 32*(w%4) .. +31 (tile rows) over its part (w-2)/4 of the columns, applies
 // scale (and SiLU), rounds to fp16 and stages the values (row r at 512 r bytes, 16-byte
@@ -142,9 +150,9 @@ HM_DEV void umma_commit_pair(uint64_t* bar) {
 // copies its own 32 rows out as whole 128/256-byte row segments (16-byte lanes along the
 // row), adding the residual there: y = fp16(fp16(acc * s) + r), the same rounding points.
 constexpr int kStageBytes = BM * 512;
-template <int EPI>
-HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane, int m_row0, int nt, uint8_t* stage) {
-  __half* const scl = reinterpret_cast<__half*>(stage + kStageBytes);
+template <int EPI, typename Release>
+HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane, int m_row0, int nt, uint8_t* stage,
+                          __half* scl, Release release) {
   const int et = (warp - 2) * 32 + lane;  // 0 .. 255
   const int N = P.N, M = P.M;
   const int q = warp & 3, part = (warp - 2) / 4;
@@ -209,6 +217,7 @@ HM_DEV void epilogue_tile(const GemmParams& P, uint32_t tmem, int warp, int lane
     *reinterpret_cast<uint4*>(srow + ((ch ^ (r & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
     *reinterpret_cast<uint4*>(srow + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
   }
+  release();     // this warp's reads of the accumulator are complete
   __syncwarp();  // this warp's 32 rows x W columns are staged
 #pragma unroll
   for (int b2 = 0; b2 < 2; ++b2) {
@@ -340,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
     }
     mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
     tc_fence_after();
-    epilogue_tile<EPI>(P, tmem, warp, lane, m0, nt, sm.a[0]);
+    epilogue_tile<EPI>(P, tmem, warp, lane, m0, nt, sm.a[0], reinterpret_cast<__half*>(sm.bq[0]), [] {});
   }
   tc_fence_before();
   __syncthreads();
@@ -350,18 +359,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8w_kernel(const __grid_cons
   }
 }
 
-// fp16 weights on an SM pair (cluster of two CTAs along M): tile rows pair_m0 .. +255,
-// columns nt*256 .. +255 (SiLU: features nt*128 .. +127 of w1 and of w3).
+// fp16 weights on SM pairs, persistent: cluster c (two CTAs along M, one per SM) computes
+// the 256 x 256 tiles c, c + clusters, ...; tile t = (M pair, N tile) with consecutive
+// tiles walking N when the activations are the larger operand (the tiles in flight then
+// share a few M pairs of A and all of W, both L2-resident; w2's A is 134 MB at 8 x 1024
+// tokens), else walking M; rows pair*256 + rank*128 .. +127 in CTA `rank`, columns
+// nt*256 .. +255 (SiLU: features nt*128 .. +127 of w1 and of w3).  Two 256-column TMEM
+// accumulators per CTA: the MMA fills one while the epilogue warps of both CTAs drain the
+// other.
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 2)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16w_pair_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
                           const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   GemmSmem2& sm = *reinterpret_cast<GemmSmem2*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_ctarank();
-  const int m_row0 = (blockIdx.x >> 1) * 2 * BM + static_cast<int>(rank) * BM;
-  const int nt = blockIdx.y;
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int mpairs = (P.M + 2 * BM - 1) / (2 * BM), T = mpairs * P.ntiles;
   const int nk = P.K / BK;
   int* const err = P.err;
 
@@ -371,10 +386,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 2)
       mbar_init(&sm.full[i], 1);   // the leader's producer (expect_tx) + both CTAs' copies (bytes)
       mbar_init(&sm.empty[i], 1);  // the leader's MMA commit
     }
-    mbar_init(&sm.acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.acc_full[i], 1);             // the leader's MMA commit
+      mbar_init(&sm.acc_empty[i], 2 * kConvW);   // every epilogue warp of both CTAs
+    }
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc_pair(&sm.tmem_base, kTmemCols);
+  if (warp == 1) tmem_alloc_pair(&sm.tmem_base, 2 * BN);
   tc_fence_before();
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
@@ -387,14 +405,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 2)
       prefetch_tensormap(&amap);
       prefetch_tensormap(&wmap);
       const uint32_t full0 = dsmem_addr(&sm.full[0], 0);  // the leader's ring barriers
-      const int brow = EPI == HM_EPI_SILU ? (rank == 0 ? 0 : P.wrows_half) + nt * (BN / 2)
-                                          : nt * BN + static_cast<int>(rank) * (BN / 2);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % NS2;
-        if (kb >= NS2) mbar_wait_ab(&sm.empty[s], ((kb / NS2) - 1) & 1, err, abort_s);
-        if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 4 * kABytes);  // A + B halves of both CTAs
-        tma_load_2d_pair(sm.a[s], &amap, kb * BK, m_row0, full0 + 8 * s);
-        tma_load_2d_pair(sm.b[s], &wmap, kb * BK, brow, full0 + 8 * s);
+      int g = 0;  // k-blocks over all of this pair's tiles
+      for (int t = pair; t < T; t += npairs) {
+        const int mp = P.n_fast ? t / P.ntiles : t % mpairs, nt = P.n_fast ? t % P.ntiles : t / mpairs;
+        const int m_row0 = mp * 2 * BM + static_cast<int>(rank) * BM;
+        const int brow = EPI == HM_EPI_SILU ? (rank == 0 ? 0 : P.wrows_half) + nt * (BN / 2)
+                                            : nt * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % NS2;
+          if (g >= NS2) mbar_wait_ab(&sm.empty[s], ((g / NS2) - 1) & 1, err, abort_s);
+          if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 4 * kABytes);  // A + B halves of both CTAs
+          tma_load_2d_pair(sm.a[s], &amap, kb * BK, m_row0, full0 + 8 * s);
+          tma_load_2d_pair(sm.b[s], &wmap, kb * BK, brow, full0 + 8 * s);
+        }
       }
     }
   } else if (warp == 1) {
@@ -402,33 +425,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 2)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = idesc_f16(2 * BM, BN);
       const uint64_t a0 = sw128_desc(smem_u32(sm.a[0])), b0 = sw128_desc(smem_u32(sm.b[0]));
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % NS2;
-        mbar_wait_ab(&sm.full[s], (kb / NS2) & 1, err, abort_s);
+      int g = 0, i = 0;
+      for (int t = pair; t < T; t += npairs, ++i) {
+        const int ab = i & 1;
+        // the accumulator's previous tile has been read out by both CTAs' epilogues
+        if (i >= 2 && !*abort_s && !mbar_wait_cluster(&sm.acc_empty[ab], ((i >> 1) - 1) & 1, err)) *abort_s = 1;
         tc_fence_after();
-        const uint64_t ad = a0 + s * (kABytes >> 4), bd = b0 + s * (kABytes >> 4);
+        const uint32_t acc = tmem + ab * BN;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % NS2;
+          mbar_wait_ab(&sm.full[s], (g / NS2) & 1, err, abort_s);
+          tc_fence_after();
+          const uint64_t ad = a0 + s * (kABytes >> 4), bd = b0 + s * (kABytes >> 4);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) umma_f16_pair(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
-        umma_commit_pair(&sm.empty[s]);
+          for (int k = 0; k < BK / 16; ++k) umma_f16_pair(acc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit_pair(&sm.empty[s]);
+        }
+        umma_commit_pair(&sm.acc_full[ab]);
       }
-      umma_commit_pair(&sm.acc_full);
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs: their 128 rows)
-    mbar_wait_ab(&sm.acc_full, 0, err, abort_s);
-    tc_fence_after();
-    epilogue_tile<EPI>(P, tmem, warp, lane, m_row0, nt, sm.a[0]);
+    const uint32_t acc_empty0 = dsmem_addr(&sm.acc_empty[0], 0);  // the leader's
+    int i = 0;
+    for (int t = pair; t < T; t += npairs, ++i) {
+      const int ab = i & 1;
+      const int mp = P.n_fast ? t / P.ntiles : t % mpairs, nt = P.n_fast ? t % P.ntiles : t / mpairs;
+      const int m_row0 = mp * 2 * BM + static_cast<int>(rank) * BM;
+      mbar_wait_ab(&sm.acc_full[ab], (i >> 1) & 1, err, abort_s);
+      tc_fence_after();
+      epilogue_tile<EPI>(P, tmem + ab * BN, warp, lane, m_row0, nt, sm.stage, sm.scl[ab], [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0)
+            mbar_arrive(&sm.acc_empty[ab]);
+          else
+            mbar_arrive_dsmem(acc_empty0 + 8 * ab);
+        }
+      });
+    }
   }
   tc_fence_before();
   cluster_sync_all();  // neither CTA leaves while the pair's copies, MMAs or commits may touch its memory
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem, kTmemCols);
+    tmem_dealloc_pair(tmem, 2 * BN);
   }
 }
 
-static_assert(sizeof(GemmSmem::a) + sizeof(GemmSmem::bq) >= kStageBytes + 512, "epilogue staging space (int8 kernel)");
-static_assert(sizeof(GemmSmem2::a) + sizeof(GemmSmem2::b) >= kStageBytes + 512, "epilogue staging space (pair kernel)");
+static_assert(sizeof(GemmSmem::a) >= kStageBytes && sizeof(GemmSmem::bq) >= 512, "epilogue staging space (int8 kernel)");
+static_assert(kStageBytesP >= kStageBytes, "epilogue staging space (pair kernel)");
 
 // ---------------------------------------------------------------- host side
 struct MapKey {
@@ -500,9 +547,20 @@ cudaError_t launch_gemm(const CUtensorMap& am, const CUtensorMap& wm, const Gemm
     if (e != cudaSuccess) return e;
     configured[wf16] = true;
   }
-  if (wf16) {
-    const dim3 grid(2 * ((p.M + 2 * BM - 1) / (2 * BM)), ntiles_n);  // whole SM pairs
-    return hm_launch(gemm_f16w_pair_kernel<EPI>, grid, dim3(kThreads), smem, st, false, am, wm, p);
+  if (wf16) {  // persistent: one cluster of two CTAs per pair of SMs, at most one per tile
+    static int sms = 0;
+    if (sms == 0) {
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                    cudaSuccess)
+        return cudaErrorInvalidValue;
+    }
+    GemmParams q = p;
+    q.ntiles = ntiles_n;
+    q.n_fast = p.M > (EPI == HM_EPI_SILU ? 2 * p.N : p.N);  // A (M x K) larger than W (rows x K)
+    const int64_t tiles = (int64_t)((p.M + 2 * BM - 1) / (2 * BM)) * ntiles_n;
+    const int pairs = static_cast<int>(tiles < sms / 2 ? tiles : sms / 2);
+    return hm_launch(gemm_f16w_pair_kernel<EPI>, dim3(2 * pairs), dim3(kThreads), smem, st, false, am, wm, q);
   }
   const dim3 grid((p.M + BM - 1) / BM, ntiles_n);
   return hm_launch(gemm_i8w_kernel<EPI>, grid, dim3(kThreads), smem, st, false, am, wm, p);
@@ -532,6 +590,8 @@ int gemm_entry(const void* a, int64_t lda, const void* w, bool wf16, const void*
   p.N = nout;
   p.K = K;
   p.wrows_half = epi == HM_EPI_SILU ? N / 2 : 0;
+  p.ntiles = 0;
+  p.n_fast = 0;
   p.err = err;
   const int tn = epi == HM_EPI_SILU ? (nout + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
   const cudaError_t e = epi == HM_EPI_SILU ? launch_gemm<HM_EPI_SILU>(am, wm, p, tn, wf16, stream)
