@@ -441,14 +441,20 @@ class HeartMuLaLite:
         self._rt = None
 
     def release(self):
-        """Free caches, graphs and buffers (``app/engine.py:463-469``).  Weights stay, the
-        prefill's fp16 copies of the backbone matrices included (``drop_prefill_weights``
-        or ``to`` free those)."""
+        """Free caches, graphs and buffers (``app/engine.py:463-469``) and return the memory
+        to the device.  Weights stay, the prefill's fp16 copies of the backbone matrices
+        included (``drop_prefill_weights`` or ``to`` free those)."""
+        self._release_buffers()
+        torch.cuda.empty_cache()
+
+    def _release_buffers(self):
+        """``release`` without emptying torch's allocator cache: what ``generate`` does at
+        the end of a song, so the next song (or anything else in this process, the codec
+        included) takes the freed blocks without a new device allocation."""
         self._drop_runtime()
         self.graphs.clear()
         self.backbone.free()
         self.decoder.free()
-        torch.cuda.empty_cache()
 
     def to(self, device):
         """Move the weights to ``device`` (``app/engine.py:267-288``), e.g. to the host while
@@ -665,7 +671,7 @@ class HeartMuLaLite:
         if forced:
             self.teacher_logits = rt.rec_tab
         if not keep_state:
-            self.release()
+            self._release_buffers()
         return res[0] if n == 1 else res
 
 
