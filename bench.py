@@ -32,7 +32,7 @@ sys.path.insert(0, str(ROOT))
 
 import torch  # noqa: E402
 
-from estudiocanciones_b200._lib import capture_no_gc  # noqa: E402
+from estudiocanciones_b200._lib import capture_graph  # noqa: E402
 
 METRIC = "audio s/s per GPU at 4 takes+CFG; µs per frame (3B + 7 decoder passes)"
 UNIT = "audio-s/s"
@@ -182,9 +182,8 @@ def gemv_roofline(m, rt, peak, reps=10):
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s), capture_no_gc():
-        with torch.cuda.graph(g, stream=s):
-            p.run()
+    with capture_graph(g, s):
+        p.run()
     torch.cuda.current_stream().wait_stream(s)
     g.replay()
     torch.cuda.synchronize()
@@ -235,9 +234,8 @@ def attn_roofline(m, rt, peak, reps=10):
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s), capture_no_gc():
-        with torch.cuda.graph(g, stream=s):
-            p.run()
+    with capture_graph(g, s):
+        p.run()
     torch.cuda.current_stream().wait_stream(s)
     g.replay()
     torch.cuda.synchronize()
@@ -688,9 +686,8 @@ def run_case(a):
     graph = torch.cuda.CUDAGraph()
     st = torch.cuda.Stream()
     st.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(st), capture_no_gc():
-        with torch.cuda.graph(graph, stream=st):
-            p.run()
+    with capture_graph(graph, st):
+        p.run()
     torch.cuda.current_stream().wait_stream(st)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     graph.replay()

@@ -110,6 +110,27 @@ def capture_no_gc():
             gc.enable()
 
 
+@contextlib.contextmanager
+def capture_graph(g, stream, pool=None):
+    """Capture CUDA work into ``g`` on ``stream`` as ``torch.cuda.graph`` does, minus its
+    entry step that empties torch's device and pinned-host allocator caches: after that,
+    every later allocation goes back to cudaMalloc, which with peer access enabled (an
+    NCCL process group) took up to ~1 s per song on two B200s.  The cyclic collector is
+    off meanwhile (see :func:`capture_no_gc`).  ``pool``: a graph memory pool handle to
+    share between captures (its blocks are then reused instead of allocated anew)."""
+    import torch
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream), capture_no_gc():
+        if pool is None:
+            g.capture_begin(capture_error_mode="global")
+        else:
+            g.capture_begin(pool, capture_error_mode="global")
+        try:
+            yield g
+        finally:
+            g.capture_end()
+
+
 def check(rc: int, what: str) -> None:
     if rc != 0:
         kind = "bad argument" if rc < 0 else f"CUDA error {rc}"

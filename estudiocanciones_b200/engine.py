@@ -26,7 +26,7 @@ from pathlib import Path
 import torch
 
 from . import _lib, kernels
-from ._lib import capture_no_gc as _capture_no_gc
+from ._lib import capture_graph as _capture_graph
 from ._lib import GemvDesc, RowSrc, check, HM_EPI_STORE, HM_EPI_ROPE_KV, HM_EPI_SILU, HM_SRC_F16, HM_SRC_RMS, HM_SRC_EMB
 from .checkpoint import (AUDIO_EOS, AUDIO_VOCAB, FRAME_MS, N_CB, TEXT_BOS, TEXT_EOS, load_tensors,
                          shape_from_tensors)
@@ -553,9 +553,8 @@ class HeartMuLaLite:
             g = torch.cuda.CUDAGraph()
             st = torch.cuda.Stream(device=self.dev)
             st.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(st), _capture_no_gc():
-                with torch.cuda.graph(g, stream=st):
-                    plan.run()
+            with _capture_graph(g, st):
+                plan.run()
             torch.cuda.current_stream().wait_stream(st)
             g.replay()
         else:
@@ -750,9 +749,8 @@ class _Runtime:
             g = torch.cuda.CUDAGraph()
             s = torch.cuda.Stream(device=self.m.dev)
             s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s), _capture_no_gc():
-                with torch.cuda.graph(g, stream=s):
-                    plan.run()
+            with _capture_graph(g, s):
+                plan.run()
             torch.cuda.current_stream().wait_stream(s)
             self.tok_in.copy_(saved[0])
             self.pos.copy_(saved[1])

@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from . import kernels
-from ._lib import HMError, capture_no_gc
+from ._lib import HMError, capture_graph
 
 
 def _rows_to_runtime(rt, x_last: torch.Tensor) -> None:
@@ -117,11 +117,10 @@ def prefill_backbone_steps(model, h: torch.Tensor) -> None:
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream(device=h.device)
     s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s), capture_no_gc():
-        with torch.cuda.graph(g, stream=s):
-            rt.x_bb.copy_(x_in)
-            rt.ss_bb.copy_((x_in.float() ** 2).reshape(B, D // SS_COLS, SS_COLS).sum(-1).t())
-            plan.run()
+    with capture_graph(g, s):
+        rt.x_bb.copy_(x_in)
+        rt.ss_bb.copy_((x_in.float() ** 2).reshape(B, D // SS_COLS, SS_COLS).sum(-1).t())
+        plan.run()
     torch.cuda.current_stream().wait_stream(s)
     for p in range(1, P):
         x_in.copy_(h[:, p])
