@@ -20,6 +20,8 @@ HM_ERR_TIMEOUT, HM_ERR_BADINDEX = 1, 2
 HM_EARG = -1
 HM_DT_F32, HM_DT_BF16, HM_DT_F16 = 0, 1, 2
 HM_ENOSPACE = -2
+HM_ACT_NONE, HM_ACT_PRELU, HM_ACT_SILU = 0, 1, 2
+HM_CEPI_STORE, HM_CEPI_GATED, HM_CEPI_RES, HM_CEPI_SILU, HM_CEPI_ROPE = 0, 1, 2, 3, 4
 
 # Every exported symbol of include/heartmula_b200.h with (restype, argtypes).
 _P, _I, _I64, _F, _SZ = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
@@ -46,6 +48,18 @@ class GemvDesc(C.Structure):
                 ("err", _P), ("kspan", C.c_int), ("pdl", C.c_int), ("l2_keep", C.c_int)]
 
 
+class ConvDesc(C.Structure):
+    """hm_conv_desc: one implicit-GEMM convolution / linear layer of the codec."""
+    _fields_ = [("x", _P), ("x_ld", _I64), ("x_bstride", _I64), ("w", _P), ("bias", _P),
+                ("y", _P), ("y_ld", _I64), ("res", _P), ("res_ld", _I64), ("gate", _P), ("gate_ld", _I64),
+                ("rope", _P), ("err", _P),
+                ("B", C.c_int), ("T", C.c_int), ("tin", C.c_int), ("cin", C.c_int), ("N", C.c_int),
+                ("npad", C.c_int), ("taps", C.c_int), ("off0", C.c_int), ("dil", C.c_int),
+                ("scale", C.c_float), ("prelu", C.c_float),
+                ("act", C.c_int), ("epi", C.c_int), ("y_f32", C.c_int), ("rope_cols", C.c_int), ("hd", C.c_int),
+                ("bn", C.c_int)]
+
+
 SIGNATURES = {
     "hm_gemv_i8": (_I, [_P, _I64, _P, _P, _P, _I64, _P, _I64, _I, _I, _I, _P, _SZ, _P, _I, _P, _I, _I, _P]),
     "hm_gemv_i8_fused": (_I, [C.POINTER(GemvDesc), _P]),
@@ -68,6 +82,15 @@ SIGNATURES = {
     "hm_gemm_f16w": (_I, [_P, _I64, _P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _P, _P]),
     "hm_dequant_i8_f16": (_I, [_P, _P, _I64, _P]),
     "hm_prefill_attn": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P]),
+    "hm_conv1d_gemm": (_I, [C.POINTER(ConvDesc), _P]),
+    "hm_codec_attn": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _I64, _F, _P, _P]),
+    "hm_codec_norm_mod": (_I, [_P, _I64, _P, _P, _P, _I64, _P, _I64, _I, _I, _I, _F, _I, _P]),
+    "hm_codec_vq_embed": (_I, [_P, _I64, _I, _I, _P, _I, _I, _P, _P, _P, _I64, _I, _P]),
+    "hm_codec_upsample_rows": (_I, [_P, _I64, _I, _I, _I, _P, _I64, _P]),
+    "hm_codec_euler": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _F, _F, _F, _I, _P, _I64, _I64, _P]),
+    "hm_codec_band_quant": (_I, [_P, _I, _I, _I, _P, _P]),
+    "hm_codec_temb_post": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
+    "hm_codec_overlap_add": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _I64, _P]),
     "hm_device_sm_count": (_I, [_I]),
     "hm_abi_layout": (_SZ, [_I]),
     "hm_version": (C.c_char_p, []),
@@ -145,5 +168,6 @@ def abi_mismatches() -> list[str]:
     """Compare the ctypes struct layouts with the library's own sizeof/offsetof."""
     L = lib()
     want = {0: C.sizeof(RowSrc), 1: C.sizeof(GemvDesc), 2: GemvDesc.src.offset, 3: GemvDesc.ws.offset,
-            4: GemvDesc.pdl.offset, 5: GemvDesc.l2_keep.offset}
+            4: GemvDesc.pdl.offset, 5: GemvDesc.l2_keep.offset, 6: C.sizeof(ConvDesc), 7: ConvDesc.B.offset,
+            8: ConvDesc.scale.offset, 9: ConvDesc.bn.offset}
     return [f"layout[{k}]: C {L.hm_abi_layout(k)} vs ctypes {v}" for k, v in want.items() if L.hm_abi_layout(k) != v]

@@ -1181,8 +1181,12 @@ extern "C" size_t hm_abi_layout(int which) {
     case 3: return offsetof(hm_gemv_desc, ws);
     case 4: return offsetof(hm_gemv_desc, pdl);
     case 5: return offsetof(hm_gemv_desc, l2_keep);
+    case 6: return sizeof(hm_conv_desc);
+    case 7: return offsetof(hm_conv_desc, B);
+    case 8: return offsetof(hm_conv_desc, scale);
+    case 9: return offsetof(hm_conv_desc, bn);
     default: return 0;
   }
 }
 
-extern "C" const char* hm_version(void) { return "heartmula_b200 0.3 sm_100a"; }
+extern "C" const char* hm_version(void) { return "heartmula_b200 0.4 sm_100a"; }

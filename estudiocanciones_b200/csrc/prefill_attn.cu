@@ -53,7 +53,6 @@
 namespace {
 
 constexpr int kT = 128;            // query positions per CTA = cache positions per K/V tile
-constexpr int kHD = 128;           // head dim
 constexpr int kBox = kT * 128;     // one 128-row x 64-column fp16 box, 16 KB
 constexpr int kSoftW = 8;         // softmax / epilogue warps
 constexpr int kThreads = 64 + 32 * kSoftW;
@@ -62,11 +61,13 @@ constexpr uint32_t kOCol = 256;    // O accumulator columns 256..383
 constexpr uint32_t kPCol = 384;    // P: fp16 pairs of the 128 keys in columns 384..447
 constexpr float kRescale = 8.f;    // log2 of the growth the stale max may absorb
 
+// NB: 64-column boxes per head-dim row (hd = 64 NB)
+template <int NB>
 struct FaSmem {
-  uint8_t q[2][kBox];     // [hd half][128 rows x 64]
-  uint8_t k[2][2][kBox];  // [stage][hd half]
-  uint8_t v[2][2][kBox];  // [stage][hd half]
-  uint8_t p[2][kBox];     // [head-dim half]: the epilogue's staging of O / l
+  uint8_t q[NB][kBox];     // [hd box][128 rows x 64]
+  uint8_t k[2][NB][kBox];  // [stage][hd box]
+  uint8_t v[2][NB][kBox];  // [stage][hd box]
+  uint8_t p[2][kBox];      // the epilogue's staging of O / l (hd 128: per head-dim half)
   float xch[2][2][kT];    // [tile parity][column half][row]: partial row maxima
   float xl[2][kT];        // [column half][row]: partial row sums at an item's end
   uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, pv_done, drain;
@@ -76,14 +77,20 @@ struct FaSmem {
 
 struct FaParams {
   __half* o;
+  int64_t ldo;       // output row stride (elements)
   int B, P, Hq, Hk, L;
   int items;         // ceil(P / 128) * Hq * B
+  int causal;        // 1: keys j <= query p (the prompt pass); 0: all keys j < P (the codec's estimator)
+  // K/V row of (item b, KV head kh, position t): b * kv_b_rows + kh * kv_h_rows + t, its head-dim
+  // columns from kh * kv_h_cols (the cache [B, Hk, L, hd]: Hk*L, L, 0; a fused q|k|v [B*P, ...]:
+  // P, 0, hd)
+  int kv_b_rows, kv_h_rows, kv_h_cols;
   float scale_log2;  // scale * log2(e)
   int* err;
 };
 
-// Work item i in longest-first order: query tile qt (its K/V tiles 0 .. qt), head h,
-// batch row b; heads of one KV group adjacent, so their K/V tiles meet in L2.
+// Work item i in longest-first order: query tile qt (its K/V tiles 0 .. qt when causal, else
+// all of them), head h, batch row b; heads of one KV group adjacent, so their K/V tiles meet in L2.
 struct Item {
   int qt, h, b, kh, n;
 };
@@ -95,7 +102,7 @@ HM_DEV Item item_of(const FaParams& p, int i) {
   it.h = rest % p.Hq;
   it.b = rest / p.Hq;
   it.kh = it.h / (p.Hq / p.Hk);
-  it.n = it.qt + 1;
+  it.n = p.causal ? it.qt + 1 : nqt;
   return it;
 }
 
@@ -105,14 +112,17 @@ HM_DEV float ex2(float x) {
   return y;
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                      const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
                                                                      const __grid_constant__ FaParams Pp) {
+  constexpr int NB = HD / 64;  // head-dim boxes
+  constexpr int CW = HD / 2;   // O columns of one softmax warp (the two warps of a lane quarter split hd)
   extern __shared__ uint8_t smem_raw[];
-  FaSmem& sm = *reinterpret_cast<FaSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  FaSmem<NB>& sm = *reinterpret_cast<FaSmem<NB>*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int P = Pp.P, Hq = Pp.Hq, Hk = Pp.Hk, L = Pp.L;
+  const int P = Pp.P;
   const int i0 = static_cast<int>(blockIdx.x), istep = static_cast<int>(gridDim.x), items = Pp.items;
   int* const err = Pp.err;
   volatile int* abort_s = &sm.abort_flag;
@@ -149,21 +159,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       for (int i = i0; i < items; i += istep, ++k) {
         const Item it = item_of(Pp, i);
         if (k > 0) mbar_wait_ab(&sm.q_empty, (k - 1) & 1, err, abort_s);  // previous item's S MMAs done
-        mbar_arrive_expect_tx(&sm.q_full, 2 * kBox);
+        mbar_arrive_expect_tx(&sm.q_full, NB * kBox);
         const int qrow = it.b * P + it.qt * kT;
-        tma_load_2d_plain(sm.q[0], &qmap, it.h * kHD, qrow, &sm.q_full);
-        tma_load_2d_plain(sm.q[1], &qmap, it.h * kHD + 64, qrow, &sm.q_full);
-        const int krow = (it.b * Hk + it.kh) * L;
+#pragma unroll
+        for (int bx = 0; bx < NB; ++bx) tma_load_2d_plain(sm.q[bx], &qmap, it.h * HD + 64 * bx, qrow, &sm.q_full);
+        const int krow = it.b * Pp.kv_b_rows + it.kh * Pp.kv_h_rows, kcol = it.kh * Pp.kv_h_cols;
         for (int t = 0; t < it.n; ++t, ++g) {
           const int s = g & 1;
           if (g >= 2) mbar_wait_ab(&sm.k_empty[s], ((g >> 1) - 1) & 1, err, abort_s);
-          mbar_arrive_expect_tx(&sm.k_full[s], 2 * kBox);
-          tma_load_2d_plain(sm.k[s][0], &kmap, 0, krow + t * kT, &sm.k_full[s]);
-          tma_load_2d_plain(sm.k[s][1], &kmap, 64, krow + t * kT, &sm.k_full[s]);
+          mbar_arrive_expect_tx(&sm.k_full[s], NB * kBox);
+#pragma unroll
+          for (int bx = 0; bx < NB; ++bx)
+            tma_load_2d_plain(sm.k[s][bx], &kmap, kcol + 64 * bx, krow + t * kT, &sm.k_full[s]);
           if (g >= 2) mbar_wait_ab(&sm.v_empty[s], ((g >> 1) - 1) & 1, err, abort_s);
-          mbar_arrive_expect_tx(&sm.v_full[s], 2 * kBox);
-          tma_load_2d_plain(sm.v[s][0], &vmap, 0, krow + t * kT, &sm.v_full[s]);
-          tma_load_2d_plain(sm.v[s][1], &vmap, 64, krow + t * kT, &sm.v_full[s]);
+          mbar_arrive_expect_tx(&sm.v_full[s], NB * kBox);
+#pragma unroll
+          for (int bx = 0; bx < NB; ++bx)
+            tma_load_2d_plain(sm.v[s][bx], &vmap, kcol + 64 * bx, krow + t * kT, &sm.v_full[s]);
         }
       }
       // every copy issued has landed before the CTA's shared memory can be released
@@ -177,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_qk = idesc_f16(kT, kT);
-      constexpr uint32_t id_pv = idesc_f16(kT, kHD, false, true);  // V: MN-major (hd contiguous)
+      constexpr uint32_t id_pv = idesc_f16(kT, HD, false, true);  // V: MN-major (hd contiguous)
       constexpr uint64_t kBoxD = kBox >> 4;                        // one box in the 16-byte address field
       const uint64_t dq = sw128_desc(smem_u32(sm.q[0])), dk0 = sw128_desc(smem_u32(sm.k[0][0]));
       const uint64_t dv0 = sw128_mn_desc(smem_u32(sm.v[0][0]), kBox);
@@ -188,9 +200,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
         if (qj == 0) mbar_wait_ab(&sm.q_full, qk_n & 1, err, abort_s);
         mbar_wait_ab(&sm.k_full[s], (qg >> 1) & 1, err, abort_s);
         tc_fence_after();
-        const uint64_t dk = dk0 + 2 * s * kBoxD;
+        const uint64_t dk = dk0 + NB * s * kBoxD;
 #pragma unroll
-        for (int kk = 0; kk < kHD / 16; ++kk)  // +32 bytes per K=16 step inside a 128-byte row
+        for (int kk = 0; kk < HD / 16; ++kk)  // +32 bytes per K=16 step inside a 128-byte row
           umma_f16(tmem + kT * s, dq + (kk >> 2) * kBoxD + 2 * (kk & 3), dk + (kk >> 2) * kBoxD + 2 * (kk & 3), id_qk,
                    kk != 0);
         umma_commit(&sm.k_empty[s]);
@@ -214,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
           mbar_wait_ab(&sm.p_full, pg & 1, err, abort_s);
           mbar_wait_ab(&sm.v_full[s], (pg >> 1) & 1, err, abort_s);
           tc_fence_after();
-          const uint64_t dv = dv0 + 2 * s * kBoxD;
+          const uint64_t dv = dv0 + NB * s * kBoxD;
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)  // 16 cache positions = 16 V rows of 128 bytes per step
             umma_f16_ts(tmem + kOCol, tmem + kPCol + 8 * kk, dv + kk * (2048 >> 4), id_pv, (j | kk) != 0);
@@ -229,11 +241,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
   } else {
     // ------------------------------------------------------------ softmax, then epilogue
     const int q4 = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;   // key columns / head dims 64*half .. +63
+    const int half = (warp - 2) >> 2;   // key columns 64*half .. +63 / head dims CW*half .. +CW-1
     const int r = 32 * q4 + lane;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16) + 64 * half;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16) + 64 * half;    // its S columns
+    const uint32_t orow = tmem + (static_cast<uint32_t>(32 * q4) << 16) + kOCol + CW * half;  // its O columns
     const float sl2 = Pp.scale_log2;
-    uint8_t* const prow = sm.p[half] + r * 128;  // this thread's staging row (head dims 64*half ..)
+    // this thread's staging row: hd 128, its own buffer (64 head dims = 8 chunks); hd 64, the
+    // row's 64 head dims in one buffer, this half's 32 at chunks 4*half ..
+    constexpr int kSb = NB == 2 ? 1 : 0;
+    uint8_t* const prow = sm.p[kSb * half] + r * 128;
+    const int cbase = NB == 2 ? 0 : 4 * half;
     const uint32_t tp = tmem + (static_cast<uint32_t>(32 * q4) << 16) + kPCol + 32 * half;  // its P columns
     int g = 0;
     for (int i = i0; i < items; i += istep) {
@@ -250,8 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
         float x[64];
 #pragma unroll
         for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(raw[c]);
-        if (j == it.qt) {  // diagonal tile: keys after the query are masked
-          const int lim = r - 64 * half;  // columns c > lim of this half are masked
+        if (Pp.causal ? j == it.qt : (j == it.n - 1 && (j + 1) * kT > P)) {
+          // causal diagonal tile: keys after the query; non-causal last tile: keys at or past P
+          const int lim = Pp.causal ? r - 64 * half : P - 1 - j * kT - 64 * half;  // columns c > lim masked
 #pragma unroll
           for (int c = 0; c < 64; ++c) x[c] = c > lim ? -INFINITY : x[c];
         }
@@ -285,13 +303,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
           tc_fence_after();
           if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-            for (int c = 0; c < 64; c += 32) {
+            for (int c = 0; c < CW; c += 32) {
               uint32_t o[32];
-              tmem_ld32_nowait(trow + kOCol + c, o);
+              tmem_ld32_nowait(orow + c, o);
               tmem_wait_ld();
 #pragma unroll
               for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-              tmem_st32(trow + kOCol + c, o);
+              tmem_st32(orow + c, o);
             }
             tmem_wait_st();
           }
@@ -303,12 +321,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
           tmem_st32(tp, pk);
           tmem_wait_st();
         }
-        if (j == it.qt && (j + 1) * kT > P) {
-          // cache slots P .. of the diagonal tile: their probabilities are 0, but 0 times a
-          // non-finite cache value would not be, so zero those V rows (whole 128-byte rows)
+        if (j == it.n - 1 && (j + 1) * kT > P) {
+          // key rows P .. of the item's last tile: their probabilities are 0, but 0 times a
+          // non-finite value there would not be, so zero those V rows (whole 128-byte rows)
           mbar_wait_ab(&sm.v_full[s], (g >> 1) & 1, err, abort_s);
           const int nv = P - j * kT, nz = kT - nv;
-          for (int e = tid - 64; e < 2 * nz * 8; e += 32 * kSoftW) {
+          for (int e = tid - 64; e < NB * nz * 8; e += 32 * kSoftW) {
             const int box = e / (nz * 8), rem = e % (nz * 8);
             *reinterpret_cast<uint4*>(sm.v[s][box] + (nv + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
           }
@@ -318,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.p_full);
       }
-      // ---- epilogue: O / l -> fp16 rows qt*128 + r, head dims 64*half .. +63
+      // ---- epilogue: O / l -> fp16 rows qt*128 + r, head dims CW*half .. +CW-1
       sm.xl[half][r] = l;
       named_bar(1 + q4, 64);
       const float lt = sm.xl[0][r] + sm.xl[1][r];
@@ -326,27 +344,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       tc_fence_after();
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
+      for (int c = 0; c < CW; c += 32) {
         uint32_t o[32];
-        tmem_ld32_nowait(trow + kOCol + c, o);
+        tmem_ld32_nowait(orow + c, o);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {  // 16-byte chunk (c / 8 + e) of this row's 64 head dims
+        for (int e = 0; e < 4; ++e) {  // 16-byte chunk (cbase + c / 8 + e) of the staging row
           const float* f = reinterpret_cast<const float*>(o + 8 * e);
-          const int ch = c / 8 + e;
+          const int ch = cbase + c / 8 + e;
           *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
               make_uint4(pack_h2(f[0] * inv, f[1] * inv), pack_h2(f[2] * inv, f[3] * inv),
                          pack_h2(f[4] * inv, f[5] * inv), pack_h2(f[6] * inv, f[7] * inv));
         }
       }
-      __syncwarp();  // this warp's 32 rows x 64 columns are staged; write them as row segments
-      __half* const obase = Pp.o + (int64_t)it.h * kHD + 64 * half;
+      __syncwarp();  // this warp's 32 rows x CW columns are staged; write them as row segments
+      // (hd 128: chunk ch of head dims 64*half ..; hd 64: chunk ch of the head's 64 dims)
+      __half* const obase = Pp.o + (int64_t)it.h * HD + (NB == 2 ? 64 * half : 0);
+      constexpr int kCh = CW / 8;  // 16-byte chunks per row of this warp
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int rr = 32 * q4 + 4 * e + (lane >> 3), ch = lane & 7;  // row, 16-byte chunk
+      for (int e = 0; e < kCh; ++e) {
+        const int rr = 32 * q4 + (32 / kCh) * e + lane / kCh, ch = cbase + lane % kCh;  // row, 16-byte chunk
         const int pos = it.qt * kT + rr;
-        const uint4 v = *reinterpret_cast<const uint4*>(sm.p[half] + rr * 128 + ((ch ^ (rr & 7)) << 4));
-        if (pos < P) *reinterpret_cast<uint4*>(obase + ((int64_t)it.b * P + pos) * ((int64_t)Hq * kHD) + 8 * ch) = v;
+        const uint4 v = *reinterpret_cast<const uint4*>(sm.p[kSb * half] + rr * 128 + ((ch ^ (rr & 7)) << 4));
+        if (pos < P) *reinterpret_cast<uint4*>(obase + ((int64_t)it.b * P + pos) * Pp.ldo + 8 * ch) = v;
       }
       __syncwarp();  // reads of the staging rows done before this warp writes the next item's P
     }
@@ -400,36 +420,13 @@ bool fa_map(const void* base, int64_t rows, int64_t cols, int64_t ld, CUtensorMa
   return true;
 }
 
-}  // namespace
-
-extern "C" int hm_prefill_attn(const void* q, const void* kc, const void* vc, void* o, int B, int P, int Hq, int Hk,
-                               int hd, int L, float scale, int* err, hm_stream_t stream) {
-  if (!q || !kc || !vc || !o || B < 1 || P < 1 || Hk < 1 || Hq < Hk || Hq % Hk != 0 || hd != kHD || P > L)
-    return HM_EARG;
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(kc) |
-       reinterpret_cast<uintptr_t>(vc)) & 15u)
-    return HM_EARG;
-  const int64_t kv_rows = (int64_t)B * Hk * L, q_rows = (int64_t)B * P;
-  const int64_t nqt = (P + kT - 1) / kT, items = nqt * Hq * B;
-  if (kv_rows + kT > INT32_MAX || q_rows + kT > INT32_MAX || items > INT32_MAX) return HM_EARG;
-  CUtensorMap qm, km, vm;
-  if (!fa_map(q, q_rows, (int64_t)Hq * kHD, (int64_t)Hq * kHD, &qm) || !fa_map(kc, kv_rows, kHD, kHD, &km) ||
-      !fa_map(vc, kv_rows, kHD, kHD, &vm))
-    return HM_EARG;
-  FaParams p;
-  p.o = reinterpret_cast<__half*>(o);
-  p.B = B;
-  p.P = P;
-  p.Hq = Hq;
-  p.Hk = Hk;
-  p.L = L;
-  p.items = static_cast<int>(items);
-  p.scale_log2 = scale * 1.4426950408889634f;
-  p.err = err;
-  const size_t smem = sizeof(FaSmem) + 1024;
+template <int HD>
+int launch_attn(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const FaParams& p,
+                hm_stream_t stream) {
+  const size_t smem = sizeof(FaSmem<HD / 64>) + 1024;
   static bool configured = false;
   if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const cudaError_t e = cudaFuncSetAttribute(prefill_attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
     configured = true;
@@ -438,7 +435,73 @@ extern "C" int hm_prefill_attn(const void* q, const void* kc, const void* vc, vo
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
       sms < 1)
     return HM_EARG;
-  const unsigned ctas = static_cast<unsigned>(items < sms ? items : sms);  // persistent: one CTA per SM
-  const cudaError_t e = hm_launch(prefill_attn_tc_kernel, dim3(ctas), dim3(kThreads), smem, stream, false, qm, km, vm, p);
+  const unsigned ctas = static_cast<unsigned>(p.items < sms ? p.items : sms);  // persistent: one CTA per SM
+  const cudaError_t e =
+      hm_launch(prefill_attn_tc_kernel<HD>, dim3(ctas), dim3(kThreads), smem, stream, false, qm, km, vm, p);
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+}
+
+}  // namespace
+
+extern "C" int hm_prefill_attn(const void* q, const void* kc, const void* vc, void* o, int B, int P, int Hq, int Hk,
+                               int hd, int L, float scale, int* err, hm_stream_t stream) {
+  if (!q || !kc || !vc || !o || B < 1 || P < 1 || Hk < 1 || Hq < Hk || Hq % Hk != 0 || hd != 128 || P > L)
+    return HM_EARG;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(kc) |
+       reinterpret_cast<uintptr_t>(vc)) & 15u)
+    return HM_EARG;
+  const int64_t kv_rows = (int64_t)B * Hk * L, q_rows = (int64_t)B * P;
+  const int64_t nqt = (P + kT - 1) / kT, items = nqt * Hq * B;
+  if (kv_rows + kT > INT32_MAX || q_rows + kT > INT32_MAX || items > INT32_MAX) return HM_EARG;
+  CUtensorMap qm, km, vm;
+  if (!fa_map(q, q_rows, (int64_t)Hq * hd, (int64_t)Hq * hd, &qm) || !fa_map(kc, kv_rows, hd, hd, &km) ||
+      !fa_map(vc, kv_rows, hd, hd, &vm))
+    return HM_EARG;
+  FaParams p;
+  p.o = reinterpret_cast<__half*>(o);
+  p.ldo = (int64_t)Hq * hd;
+  p.B = B;
+  p.P = P;
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.L = L;
+  p.items = static_cast<int>(items);
+  p.causal = 1;
+  p.kv_b_rows = Hk * L;
+  p.kv_h_rows = L;
+  p.kv_h_cols = 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = err;
+  return launch_attn<128>(qm, km, vm, p, stream);
+}
+
+extern "C" int hm_codec_attn(const void* q, const void* k, const void* v, void* o, int B, int T, int H, int hd,
+                             int64_t ld, int64_t ldo, float scale, int* err, hm_stream_t stream) {
+  if (!q || !k || !v || !o || B < 1 || T < 1 || H < 1 || (hd != 64 && hd != 128)) return HM_EARG;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v)) & 15u)
+    return HM_EARG;
+  if (ld < (int64_t)H * hd || ld % 8 || ldo < (int64_t)H * hd || ldo % 8) return HM_EARG;
+  const int64_t rows = (int64_t)B * T, nqt = (T + kT - 1) / kT, items = nqt * H * B;
+  if (rows + kT > INT32_MAX || items > INT32_MAX) return HM_EARG;
+  CUtensorMap qm, km, vm;
+  if (!fa_map(q, rows, (int64_t)H * hd, ld, &qm) || !fa_map(k, rows, (int64_t)H * hd, ld, &km) ||
+      !fa_map(v, rows, (int64_t)H * hd, ld, &vm))
+    return HM_EARG;
+  FaParams p;
+  p.o = reinterpret_cast<__half*>(o);
+  p.ldo = ldo;
+  p.B = B;
+  p.P = T;
+  p.Hq = H;
+  p.Hk = H;
+  p.L = T;
+  p.items = static_cast<int>(items);
+  p.causal = 0;
+  p.kv_b_rows = T;
+  p.kv_h_rows = 0;
+  p.kv_h_cols = hd;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = err;
+  return hd == 64 ? launch_attn<64>(qm, km, vm, p, stream) : launch_attn<128>(qm, km, vm, p, stream);
 }

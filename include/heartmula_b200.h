@@ -245,11 +245,110 @@ int hm_dequant_i8_f16(const int8_t* w, void* out, int64_t n, hm_stream_t stream)
 int hm_prefill_attn(const void* q, const void* kc, const void* vc, void* o, int B, int P, int Hq, int Hk, int hd,
                     int L, float scale, int* err, hm_stream_t stream);
 
+/* ------------------------------------------------------------------ HeartCodec detokenize
+ * The codec turns the [8, T] token streams into audio (app/codec_lite.py:63-75 ->
+ * HeartCodec.detokenize, app/heartcodec/modeling_heartcodec.py:57-204): a flow-matching
+ * Euler solve over a LlamaTransformer estimator (models/flow_matching.py:72-210,
+ * models/transformer.py) and the ScalarModel waveform decoder (models/sq_codec.py:506-510).
+ *
+ * hm_conv1d_gemm: every GEMM-shaped codec layer (nn.Linear, Conv1d, causal ConvTranspose1d,
+ * the PostProcessor's repeat + conv) as one implicit-GEMM convolution on the tensor cores:
+ *   acc[b, t, n] = sum_{j < taps} sum_{c < cin} x[b, t + off0 + j*dil, c] * w[j, n, c],
+ * x rows outside [0, tin) reading as zero; then v = act((acc + bias[n]) * scale) and
+ *   HM_CEPI_STORE : y = v                              (fp16, or fp32 with y_f32)
+ *   HM_CEPI_GATED : y = res + gate[b*gate_ld + n] * v   (res, y fp32; y may equal res)
+ *   HM_CEPI_RES   : y = v + res                        (res, y fp16; ResidualUnit's skip)
+ *   HM_CEPI_SILU  : w rows in blocks of 256 (128 gate rows, the same 128 features' up rows),
+ *                   y[f] = silu(v_gate) * v_up, f < N/2 (LlamaMLP; N % 256 == 0)
+ *   HM_CEPI_ROPE  : columns n < rope_cols rotated in pairs (n even, n + 1) by rope[t][(n % hd)/2]
+ *                   = (cos, sin) (LlamaAttention's apply_rope_vec on q and k)
+ * Rows: input item b, row t at x + b*x_bstride + t*x_ld; output row b*T + t at y + row*y_ld
+ * (res the same with res_ld).  cin % 64 == 0, npad % 64 == 0 (w holds npad >= N rows per
+ * tap, the extra rows unused), x_ld/x_bstride % 8 == 0, 16-byte aligned x, w, y.
+ * bn: tile width 64/128/256, 0 = automatic (256 for HM_CEPI_SILU). */
+#define HM_ACT_NONE 0
+#define HM_ACT_PRELU 1
+#define HM_ACT_SILU 2
+#define HM_CEPI_STORE 0
+#define HM_CEPI_GATED 1
+#define HM_CEPI_RES 2
+#define HM_CEPI_SILU 3
+#define HM_CEPI_ROPE 4
+typedef struct {
+  const void* x;
+  int64_t x_ld, x_bstride;
+  const void* w;
+  const float* bias;
+  void* y;
+  int64_t y_ld;
+  const void* res;
+  int64_t res_ld;
+  const float* gate;
+  int64_t gate_ld;
+  const float* rope;
+  int* err;
+  int B, T, tin, cin, N, npad, taps, off0, dil;
+  float scale, prelu;
+  int act, epi, y_f32, rope_cols, hd, bn;
+} hm_conv_desc;
+int hm_conv1d_gemm(const hm_conv_desc* d, hm_stream_t stream);
+
+/* Non-causal multi-head attention of the codec's estimator (LlamaAttention with SDPA,
+ * models/transformer.py:129-145): q, k, v fp16 [B*T, ld] with head h at columns h*hd
+ * (views into one fused q|k|v buffer), o fp16 [B*T, ldo]; hd 64 or 128. */
+int hm_codec_attn(const void* q, const void* k, const void* v, void* o, int B, int T, int H, int hd, int64_t ld,
+                  int64_t ldo, float scale, int* err, hm_stream_t stream);
+
+/* out[b*T + t] = fp16( norm(x[b*T + t]) * (1 + scale[b*mod_ld + :]) + shift[b*mod_ld + :] ):
+ * layer_norm 0: RMSNorm with weight w (models/transformer.py:9-18), 1: LayerNorm without
+ * affine (nn.LayerNorm(elementwise_affine=False), :283-284); the ada-norm modulation of
+ * LlamaTransformerBlock (:185-201) and of the estimator's output norms (:323-331, 345-350). */
+int hm_codec_norm_mod(const float* x, int64_t ldx, const float* w, const float* shift, const float* scale,
+                      int64_t mod_ld, void* out, int64_t ldo, int B, int T, int D, float eps, int layer_norm,
+                      hm_stream_t stream);
+
+/* Residual-VQ code lookup and project_out (models/flow_matching.py:100-104):
+ * out[t] = fp16( proj_w (sum_q codebooks[q][codes[q*ld_codes + t]]) + proj_b ), codes clamped
+ * to [0, K) (app/codec_lite.py:72); codebooks fp32 [nq][K][cd], proj_w fp32 [dim][cd]. */
+int hm_codec_vq_embed(const int64_t* codes, int64_t ld_codes, int nq, int Tc, const float* codebooks, int K, int cd,
+                      const float* proj_w, const float* proj_b, void* out, int64_t ldo, int dim, hm_stream_t stream);
+
+/* dst row rep*t + i = src row t (fp16; nearest upsampling along time, flow_matching.py:108-110). */
+int hm_codec_upsample_rows(const void* src, int64_t lds, int rows, int cols, int rep, void* dst, int64_t ldd,
+                           hm_stream_t stream);
+
+/* One Euler step of solve_euler (models/flow_matching.py:161-210) on the fp32 latents x [T, C]:
+ * v NULL: x = noise; else x += dt * (u + g (c - u)) (nb == 2: v rows [0,T) unconditional,
+ * [T,2T) conditional) or x += dt * v (nb == 1); then rows < L_in = (1 - (1 - 1e-6) t_next)
+ * noise + t_next inc (final: = inc), and unless final, fp16(x) goes to columns [0, C) of
+ * the nb estimator-input items (item b row t at xin + b*xin_bstride + t*ldx); the first call
+ * (v NULL) also writes fp16(inc) rows < L_in, zeros after, to their columns [C, 2C). */
+int hm_codec_euler(const float* v, int nb, float* x, const float* noise, const float* inc, int T, int C, int L_in,
+                   float dt, float g, float t_next, int final, void* xin, int64_t ldx, int64_t xin_bstride,
+                   hm_stream_t stream);
+
+/* Latents [T, nband*Cb] fp32 -> decoder input [nband, T, Cb] fp16, round(9x)/9
+ * (modeling_heartcodec.py:185-193 band split, sq_codec.py:384-393 round_func9). */
+int hm_codec_band_quant(const float* x, int T, int Cb, int nband, void* out, hm_stream_t stream);
+
+/* From the embedded timesteps E [S, D] (fp32): act = fp16(silu(E)), shift = tab[0] + E,
+ * scale = tab[1] + E (AdaLayerNormSingleFlow's SiLU input and the output-norm modulation,
+ * models/transformer.py:323-331, 438-443). */
+int hm_codec_temb_post(const float* E, int S, int D, const float* tab, void* act, float* shift, float* scale,
+                       hm_stream_t stream);
+
+/* Window assembly of detokenize (modeling_heartcodec.py:185-204): out[c][start + i] = cur[c][i],
+ * blended over i < ovlp as out (1 - w_i) + cur w_i with w = linspace(0, 1, ovlp) in fp64. */
+int hm_codec_overlap_add(const float* cur, int64_t cur_ld, float* out, int64_t out_ld, int C, int64_t start, int64_t n,
+                         int64_t ovlp, hm_stream_t stream);
+
 /* ------------------------------------------------------------------ info */
 int hm_device_sm_count(int device);
 /* sizeof / offsetof of the descriptor structs, for bindings to verify their layout:
  * 0 sizeof(hm_row_src), 1 sizeof(hm_gemv_desc), 2 offsetof(hm_gemv_desc, src),
- * 3 offsetof(hm_gemv_desc, ws), 4 offsetof(hm_gemv_desc, pdl), 5 offsetof(hm_gemv_desc, l2_keep). */
+ * 3 offsetof(hm_gemv_desc, ws), 4 offsetof(hm_gemv_desc, pdl), 5 offsetof(hm_gemv_desc, l2_keep),
+ * 6 sizeof(hm_conv_desc), 7 offsetof(hm_conv_desc, B), 8 offsetof(hm_conv_desc, scale),
+ * 9 offsetof(hm_conv_desc, bn). */
 size_t hm_abi_layout(int which);
 const char* hm_version(void);
 
