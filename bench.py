@@ -52,11 +52,19 @@ def args_():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--case", default="frame", choices=["frame", "gemv", "attn", "sampler", "prefill", "q8"],
-                    help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures")
+    ap.add_argument("--case", default="frame",
+                    choices=["frame", "gemv", "attn", "sampler", "prefill", "q8", "codec", "codec-est", "conv"],
+                    help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures; codec: "
+                         "the detokenize timing alone; codec-est: estimator forwards of the full codec shape "
+                         "(--reps of them, for launch lists and captures)")
     ap.add_argument("--layers", type=int, default=4, help="backbone layers of the small cases")
+    ap.add_argument("--conv", default="2,744,1536,4608,1",
+                    help="conv case: items,rows,cin,N,taps (default: the codec estimator's q|k|v GEMM)")
+    ap.add_argument("--conv-bn", type=int, default=0, help="conv case: tile width (0 = automatic)")
     ap.add_argument("--prefill-layers", type=int, default=28, help="backbone layers of the prefill case")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--codec", default="auto", choices=["auto", "none"],
+                    help="also time HeartCodec detokenize of a 60 s song (1 GPU runs)")
     ap.add_argument("--configs", default="auto", choices=["auto", "all", "none"],
                     help="also measure BASELINE configs 0/2/3 and the config-4 row sweep (auto: at N=1; config 4 "
                          "at 16 rows per GPU at every N)")
@@ -373,6 +381,150 @@ def prefill_entry(m, peak_tf=None):
             "frac_of_bf16_sustained": round(tf / sus, 4), "peak_kind": "measured" if pk else "fallback"}
 
 
+def codec_entry(a, dev, cpu_sample=True):
+    """HeartCodec detokenize of a 60 s song (750 frames x 8 codebooks: three 29.76 s windows,
+    10 Euler steps each with CFG 1.25, then the waveform decoder) at the full codec shape with
+    synthetic weights.  Timed with CUDA events: through the public call with host codes in and
+    host audio out (e2e), and the dominant work alone (one window's solve graph: 10 estimator
+    forwards, tensor-core bound) against the measured bf16 peak."""
+    from estudiocanciones_b200.codec import HeartCodecB200, decoder_flops, estimator_flops
+    from estudiocanciones_b200.codec_checkpoint import FULL_CODEC, synthetic_codec_tensors
+    cfg, n_codes, steps, gs = FULL_CODEC, 750, 10, 1.25
+    sd = synthetic_codec_tensors(cfg, 1)
+    c = HeartCodecB200(sd, cfg, device=dev)
+    codes = torch.randint(0, cfg.codebook_size, (cfg.num_quantizers, n_codes),
+                          generator=torch.Generator().manual_seed(0)).pin_memory()
+
+    def song():
+        return c.detokenize(codes, num_steps=steps, guidance_scale=gs).cpu()
+
+    for _ in range(2):
+        wav = song()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        wav = song()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_song = e0.elapsed_time(e1) / reps
+    # the solve of one later window (graph replay, inputs resident)
+    key = next(k for k in c._plans if k[0] == "flow" and k[4] > 0)
+    plan = c._plans[key]
+    T = plan["T"]
+    g = plan["graph"]
+    g.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_win = e0.elapsed_time(e1) / reps
+    fl_win = steps * estimator_flops(cfg, 2, T)
+    tf = fl_win / (ms_win * 1e-3) / 1e12
+    dplan = c._plans[("dec", T)]
+    dplan["graph"].replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        dplan["graph"].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_dec = e0.elapsed_time(e1) / reps
+    tf_dec = decoder_flops(cfg, T) / (ms_dec * 1e-3) / 1e12
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    burst = pk.get("bf16_tflops", 1590.0)
+    nwin = sum(1 for k in c._plans if k[0] == "flow")
+    n_windows = 3
+    launches = n_windows * c.n_launches(key) + n_windows * len(dplan["P"].calls)
+    out = {"workload": "HeartCodec detokenize, 60 s song (750 frames x 8 codebooks, 3 windows of 29.76 s), "
+                       "10 Euler steps with CFG 1.25, full codec shape (24+6-layer estimator 1536/3072 wide, "
+                       "decoder 2048->64 channels), synthetic weights",
+           "ms_per_song": round(ms_song, 2), "audio_s_per_s": round(60.0 / (ms_song * 1e-3), 1),
+           "e2e": {"h2d_bytes_per_step": codes.numel() * 8, "d2h_bytes_per_step": wav.numel() * 4},
+           "window_solve_ms": round(ms_win, 3), "window_solve_tflops": round(tf, 1),
+           "decoder_window_ms": round(ms_dec, 3), "decoder_tflops": round(tf_dec, 1),
+           "roofline": {"bound": "tensor", "kernel": "one window's solve: 10 estimator forwards (conv_gemm_kernel, "
+                                                     "prefill_attn_tc_kernel, norms)",
+                        "achieved": round(tf, 1), "peak": burst, "unit": "TFLOP/s", "frac": round(tf / burst, 4),
+                        "flop_per_launch_group": fl_win, "peak_kind": "measured bf16 burst" if pk else "fallback"},
+           "gpu_launches_per_song": launches, "flow_plans": nwin}
+    if cpu_sample:
+        from oracle.heartcodec_oracle import OracleCodec
+        orc = OracleCodec(sd, cfg)
+        x = torch.randn(2, T, cfg.in_channels)
+        with torch.inference_mode():
+            t0 = time.perf_counter()
+            orc.estimator(x, torch.tensor([0.5, 0.5]))
+            t_est = time.perf_counter() - t0
+            Td = T // 8
+            t0 = time.perf_counter()
+            orc.scalar_decode(torch.randn(2, cfg.latent_hidden_dim, Td))
+            t_dec = (time.perf_counter() - t0) * T / Td
+        sec = n_windows * (steps * t_est + t_dec)
+        out["cpu_baseline"] = {"value": round(60.0 / sec, 4), "unit": "audio-s/s", "cores": torch.get_num_threads(),
+                               "kind": "port",
+                               "sample": f"one estimator forward (2 x {T} frames) and the waveform decoder on "
+                                         f"{Td} frames, CPU oracle fp32, scaled to 3 windows x {steps} steps",
+                               "s_per_song": round(sec, 2)}
+    del c, sd
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_conv_case(a):
+    """One implicit-GEMM conv (hm_conv1d_gemm) of the shape --conv = items,rows,cin,N,taps
+    (centered taps, fp16 output), --reps timed launches after one warm-up."""
+    from estudiocanciones_b200 import _lib as L
+    B, T, cin, N, taps = (int(v) for v in a.conv.split(","))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(B, T, cin, generator=g, device=dev).half()
+    w = (torch.randn(taps, N, cin, generator=g, device=dev) * (taps * cin) ** -0.5).half()
+    y = torch.empty(B * T, N, dtype=torch.float16, device=dev)
+    d = L.ConvDesc()
+    d.x, d.x_ld, d.x_bstride, d.w, d.y, d.y_ld = x.data_ptr(), cin, T * cin, w.data_ptr(), y.data_ptr(), N
+    d.B, d.T, d.tin, d.cin, d.N, d.npad, d.taps, d.off0, d.dil = B, T, T, cin, N, N, taps, -(taps // 2), 1
+    d.scale, d.prelu, d.bn = 1.0, 1.0, a.conv_bn
+    st = torch.cuda.current_stream().cuda_stream
+    L.check(L.lib().hm_conv1d_gemm(d, st), "conv")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.reps):
+        L.lib().hm_conv1d_gemm(d, st)
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000 * e0.elapsed_time(e1) / a.reps
+    fl = 2 * B * T * cin * N * taps
+    print(json.dumps({"case": "conv", "shape": a.conv, "bn": a.conv_bn, "us": round(us, 2),
+                      "tflops": round(fl / us / 1e6, 1)}),
+          flush=True)
+
+
+def run_codec_est_case(a):
+    """--reps estimator forwards of the full codec shape (2 items x 744 frames), eager, after
+    one warm-up forward: a short run for launch lists and kernel captures."""
+    from estudiocanciones_b200.codec import HeartCodecB200, estimator_flops
+    from estudiocanciones_b200.codec_checkpoint import FULL_CODEC, synthetic_codec_tensors
+    dev = torch.device("cuda", 0)
+    c = HeartCodecB200(synthetic_codec_tensors(FULL_CODEC, 1), FULL_CODEC, device=dev)
+    x = torch.randn(2, 744, FULL_CODEC.in_channels, device=dev)
+    c.estimator(x, 0.5)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.reps):
+        c.estimator(x, 0.5)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.reps
+    fl = estimator_flops(FULL_CODEC, 2, 744)
+    print(json.dumps({"case": "codec-est", "ms": round(ms, 3), "tflops": round(fl / ms / 1e9, 1)}), flush=True)
+
+
 def peaks():
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
@@ -559,6 +711,9 @@ def run_ours(a, world, rank, local):
         m.release()
         rt = None
         out["configs"] = measure_configs(a, m, peak, world, rank)
+    # ---- the codec that turns the token streams into audio (the step after decoding), 1 GPU
+    if world == 1 and a.codec != "none":
+        out["codec"] = codec_entry(a, dev, cpu_sample=not a.no_cpu_baseline)
     # ---- CPU baseline: the reference CPU path on this host, rank 0 at N=1
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         tcpu = {k: v.cpu() for k, v in model_tensors(dev, seed=0).items()}
@@ -713,6 +868,15 @@ def main():
         return
     if a.case == "q8":
         run_q8_case(a)
+        return
+    if a.case == "codec":
+        print(json.dumps(codec_entry(a, torch.device("cuda", 0), cpu_sample=not a.no_cpu_baseline)), flush=True)
+        return
+    if a.case == "codec-est":
+        run_codec_est_case(a)
+        return
+    if a.case == "conv":
+        run_conv_case(a)
         return
     if a.case != "frame":
         run_case(a)

@@ -191,8 +191,9 @@ def euler_schedule(num_steps: int):
 class HeartCodecB200:
     """The codec on one B200 (``HeartCodec`` minus its audio encoder)."""
 
-    def __init__(self, tensors: dict, config, device="cuda"):
+    def __init__(self, tensors: dict, config, device="cuda", graphs: bool = True):
         self.cfg = config if isinstance(config, CodecConfig) else CodecConfig.from_dict(config)
+        self.use_graphs = graphs
         self.dev = torch.device(device)
         if self.dev.type != "cuda":
             raise L.HMError("HeartCodecB200 runs on a CUDA device; there is no CPU path")
@@ -225,7 +226,6 @@ class HeartCodecB200:
         self.st2 = _Stage(sd, est, "_2", cfg.num_layers_2, cfg.inner2, H, 2 * hd, dev)
         self._prep_decoder(sd)
         self._plans: dict = {}
-        self._graphs: dict = {}
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
 
     # ------------------------------------------------------------------ decoder weights
@@ -457,7 +457,7 @@ class HeartCodecB200:
         T = latent.shape[0]
         plan = self._decoder_plan(T)
         plan["b"]["xin"].copy_(latent)
-        plan["P"].run(torch.cuda.current_stream(self.dev).cuda_stream)
+        self._exec(plan)
         return plan["b"]["wave"]
 
     def estimator(self, x: torch.Tensor, t: float) -> torch.Tensor:
@@ -541,8 +541,7 @@ class HeartCodecB200:
             b["noise"].copy_(randn((1, T, cfg.out_channels), "device")[0])
             if L_in:
                 b["inc"].copy_(prev[-ovlp_frames:])
-            self._run(plan, ("flow",) + (min_samples, nb, latent_length, L_in, num_steps, float(guidance_scale)),
-                      stream)
+            self._exec(plan)
             lat = b["x"]
             wave = self.scalar_decode(lat)
             n = min(min_audio, wave.shape[1])
@@ -552,13 +551,69 @@ class HeartCodecB200:
             prev = lat.clone() if len(starts) > 1 else lat
         return out[:, :target_len]
 
-    def _run(self, plan: dict, key, stream: int) -> None:
-        plan["P"].run(stream)
+    def _exec(self, plan: dict) -> None:
+        """Run a plan on the current stream: eagerly the first time (library set-up happens
+        outside any capture), then as one CUDA graph captured from it."""
+        stream = torch.cuda.current_stream(self.dev)
+        g = plan.get("graph")
+        if g is not None:
+            g.replay()
+            return
+        plan["P"].run(stream.cuda_stream)
+        if not self.use_graphs:
+            return
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(stream)
+        with L.capture_graph(g, side):
+            plan["P"].run(side.cuda_stream)
+        stream.wait_stream(side)
+        plan["graph"] = g
+
+    def n_launches(self, plan_key) -> int:
+        """Kernels one run of a plan launches."""
+        return len(self._plans[plan_key]["P"].calls)
 
     def release(self) -> None:
-        """Free the per-shape buffers and call lists (weights stay)."""
+        """Free the per-shape buffers, call lists and graphs (weights stay)."""
+        for plan in self._plans.values():
+            plan.pop("graph", None)
         self._plans.clear()
-        self._graphs.clear()
+
+
+def estimator_flops(cfg: CodecConfig, nb: int, T: int) -> int:
+    """Multiply-add FLOPs of one estimator forward over nb items of T frames: every GEMM
+    (ProjectLayer convs and linears, q|k|v, o, gate|up, down) plus attention (QK^T and PV)."""
+    R = nb * T
+    D1, D2, inc, out = cfg.inner, cfg.inner2, cfg.in_channels, cfg.out_channels
+
+    def blocks(n, d, hd):
+        f = CodecConfig.mlp_hidden(d)
+        per = 2 * R * d * (3 * d + d + 2 * f) + 2 * R * f * d + 4 * nb * (d // hd) * T * T * hd
+        return n * per
+
+    fl = 2 * R * inc * D1 * 3 + 2 * R * D1 * D1
+    fl += blocks(cfg.num_layers, D1, cfg.attention_head_dim)
+    fl += 2 * R * (inc + D1) * D2 * 3 + 2 * R * D2 * D2
+    fl += blocks(cfg.num_layers_2, D2, 2 * cfg.attention_head_dim)
+    fl += 2 * R * D2 * out * 3 + 2 * R * out * out
+    return fl
+
+
+def decoder_flops(cfg: CodecConfig, T: int) -> int:
+    """Multiply-add FLOPs of ScalarModel.decode on the two bands of T latent frames."""
+    nb = cfg.out_channels // cfg.latent_hidden_dim
+    ch = cfg.decoder_channels()
+    fl = 2 * nb * T * cfg.latent_hidden_dim * ch[0] * cfg.delay_kernel_size
+    t = T
+    for i, s in enumerate(cfg.upsample_factors):
+        fl += 2 * nb * t * ch[i] * s * ch[i + 1] * 2  # transposed conv: 2 taps per output
+        t *= s
+        fl += 5 * 2 * nb * t * ch[i + 1] * ch[i + 1] * (cfg.res_kernel_size + 1)
+    if cfg.num_samples > 1:
+        fl += 2 * nb * t * cfg.num_samples * cfg.init_channel * cfg.init_channel * cfg.default_kernel_size
+        t *= cfg.num_samples
+    return fl + 2 * nb * t * cfg.init_channel * cfg.num_bands * cfg.default_kernel_size
 
 
 def load_codec(path, dtype=torch.float16, device="cuda", low_vram=None) -> HeartCodecB200:

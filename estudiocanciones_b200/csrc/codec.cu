@@ -377,13 +377,26 @@ cudaError_t launch_conv(const CUtensorMap& xm, const CUtensorMap& wm, ConvP p, h
   return hm_launch(conv_gemm_kernel<BN>, dim3(grid), dim3(kThr), smem, st, 1, xm, wm, p);
 }
 
-// Tile width: the widest that divides npad and still gives every SM a tile; else the narrowest.
+// Tile width by a cost model: waves of tiles over the SMs times the time of one tile's
+// 64-wide k step, relative to bn = 256: 0.68 for bn = 128 and 0.55 for bn = 64 (measured on
+// the codec's shapes, 2 x 744 rows: with a whole wave of tiles each width is bound by its
+// shared-memory fill, bytes per MMA flop falling with the width).  Ties go to the wider tile.
 int pick_bn(const hm_conv_desc* d, int mtiles) {
-  const int sms = sm_count_cached();
+  const int64_t sms = sm_count_cached();
   const int64_t rows = static_cast<int64_t>(d->B) * mtiles;
-  for (int bn : {256, 128, 64})
-    if (d->npad % bn == 0 && rows * (d->npad / bn) >= sms) return bn;
-  return d->npad % 64 == 0 ? 64 : 0;
+  int best = 0;
+  double best_cost = 0.0;
+  for (int bn : {256, 128, 64}) {
+    if (d->npad % bn) continue;
+    const int64_t tiles = rows * (d->npad / bn);
+    const double step = bn == 256 ? 1.0 : (bn == 128 ? 0.68 : 0.55);
+    const double cost = static_cast<double>((tiles + sms - 1) / sms) * step;
+    if (best == 0 || cost < best_cost * 0.999) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 // ---------------------------------------------------------------- small kernels
@@ -433,6 +446,58 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(const float* __restrict__
     if (w) v *= w[i];
     o[i] = __float2half_rn(v * (1.f + sc[i]) + sh[i]);
   }
+}
+
+// The same with the row in registers: D / 8 threads (whole warps), 8 values each (two 16-byte
+// loads of x, one 16-byte store), D % 256 == 0 and 16-byte aligned rows.
+__global__ void __launch_bounds__(1024) norm_mod8_kernel(const float* __restrict__ x, int64_t ldx,
+                                                         const float* __restrict__ w, const float* __restrict__ shift,
+                                                         const float* __restrict__ scale, int64_t mod_ld,
+                                                         __half* __restrict__ out, int64_t ldo, int T, int D,
+                                                         float eps, int layer_norm) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  const int b = static_cast<int>(row / T);
+  const int c0 = 8 * threadIdx.x;
+  __shared__ float red[2][32];
+  const int wid = threadIdx.x >> 5, ln = threadIdx.x & 31, nw = static_cast<int>((blockDim.x + 31) >> 5);
+  const float4* xr = reinterpret_cast<const float4*>(x + row * ldx + c0);
+  const float4 a0 = xr[0], a1 = xr[1];
+  float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  float mean = 0.f;
+  if (layer_norm) {
+    float s1 = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    s1 = warp_sum(s1);
+    if (ln == 0) red[0][wid] = s1;
+    __syncthreads();
+    float t1 = 0.f;
+    for (int k = 0; k < nw; ++k) t1 += red[0][k];
+    mean = t1 / D;
+  }
+  float s2 = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    v[e] -= mean;
+    s2 += v[e] * v[e];
+  }
+  s2 = warp_sum(s2);
+  if (ln == 0) red[1][wid] = s2;
+  __syncthreads();
+  float t2 = 0.f;
+  for (int k = 0; k < nw; ++k) t2 += red[1][k];
+  const float inv = rsqrtf(t2 / D + eps);
+  const float* sh = shift + static_cast<int64_t>(b) * mod_ld + c0;
+  const float* sc = scale + static_cast<int64_t>(b) * mod_ld + c0;
+  float o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float u = v[e] * inv;
+    if (w) u *= w[c0 + e];
+    o[e] = u * (1.f + sc[e]) + sh[e];
+  }
+  *reinterpret_cast<uint4*>(out + row * ldo + c0) =
+      make_uint4(pack_h2(o[0], o[1]), pack_h2(o[2], o[3]), pack_h2(o[4], o[5]), pack_h2(o[6], o[7]));
 }
 
 // Residual-VQ code lookup + project_out: out[t, :] = fp16( W (sum_q cb[q][codes[q, t]]) + bias ).
@@ -645,6 +710,15 @@ extern "C" int hm_codec_norm_mod(const float* x, int64_t ldx, const float* w, co
                                  int64_t mod_ld, void* out, int64_t ldo, int B, int T, int D, float eps,
                                  int layer_norm, hm_stream_t stream) {
   if (!x || !shift || !scale || !out || B < 1 || T < 1 || D < 1 || ldx < D || ldo < D) return HM_EARG;
+  // whole warps (the reductions shuffle over full warps): D % 256 == 0
+  const bool vec = D % 256 == 0 && D / 8 <= 1024 && ldx % 4 == 0 && ldo % 8 == 0 && mod_ld % 4 == 0 && al16(x) &&
+                   al16(out) && al16(shift) && al16(scale);
+  if (vec) {
+    const cudaError_t e = hm_launch(norm_mod8_kernel, dim3(static_cast<unsigned>(B) * T), dim3(D / 8), 0, stream, 1, x,
+                                    ldx, w, shift, scale, mod_ld, reinterpret_cast<__half*>(out), ldo, T, D, eps,
+                                    layer_norm);
+    return e == cudaSuccess ? HM_OK : static_cast<int>(e);
+  }
   const cudaError_t e = hm_launch(norm_mod_kernel, dim3(static_cast<unsigned>(B) * T), dim3(256), 0, stream, 1, x, ldx,
                                   w, shift, scale, mod_ld, reinterpret_cast<__half*>(out), ldo, T, D, eps, layer_norm);
   return e == cudaSuccess ? HM_OK : static_cast<int>(e);

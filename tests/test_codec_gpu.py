@@ -404,3 +404,25 @@ def test_full_width_decoder_matches_oracle(wide):
     assert got.shape == ref.shape == (2, T * cfg.hop)
     e = rel_l2(got, ref)
     assert e < 5e-3, e
+
+
+def test_graph_replay_equals_eager(L, gold):
+    """detokenize's window solves and decoder run as CUDA graphs after their first use: the
+    same noise gives the same audio, bit for bit, as a codec that never captures."""
+    from estudiocanciones_b200.codec import HeartCodecB200
+    from estudiocanciones_b200.codec_checkpoint import TINY_CODEC, synthetic_codec_tensors
+    sd = synthetic_codec_tensors(TINY_CODEC, 4321)
+    codes = torch.from_numpy(gold["detok2_codes"])
+
+    def run(c):
+        g = torch.Generator().manual_seed(13)
+        return c.detokenize(codes, num_steps=2, guidance_scale=1.5,
+                            randn=lambda shape, where: torch.randn(shape, generator=g)).clone()
+
+    eager = HeartCodecB200(sd, TINY_CODEC, device=DEV, graphs=False)
+    graphed = HeartCodecB200(sd, TINY_CODEC, device=DEV)
+    a = run(eager)
+    run(graphed)  # first use of each plan: eager run + capture
+    b = run(graphed)  # replays
+    assert all("graph" in p for k, p in graphed._plans.items() if k[0] in ("flow", "dec"))
+    assert torch.equal(a, b)
