@@ -128,6 +128,80 @@ HM_DEV void store_row32(const ConvP& P, int64_t row, int n0, const float* v) {
   }
 }
 
+// Epilogue of one tile row: this thread's TMEM lane (output row t of item b) over its half h of
+// the tile's columns (SiLU-mul: a quarter of the features), bias / scale / activation and the
+// epilogue variant, then the stores.  Warp-collective (tcgen05.ld): every lane of the warp calls it.
+template <int BN>
+HM_DEV void conv_epilogue(const ConvP& P, uint32_t tb, int nt, int b, int t, int h) {
+  const bool valid = t < P.T;
+  const int64_t row = static_cast<int64_t>(b) * P.T + t;
+  if (P.epi == HM_CEPI_SILU) {
+    // weight rows in blocks of 256: 128 gate rows then the same 128 features' up rows;
+    // this warp: features h*64 .. h*64+63 of the block (BN == 256)
+    for (int f0 = h * (BN / 4); f0 < (h + 1) * (BN / 4); f0 += 16) {
+      float gv[16], uv[16], o[32];
+      tmem_ld16(tb + f0, gv);
+      tmem_ld16(tb + BN / 2 + f0, uv);
+      const int ng = nt * BN + f0, nu = ng + BN / 2;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        float a = gv[e], u = uv[e];
+        if (P.bias) {
+          a += P.bias[ng + e];
+          u += P.bias[nu + e];
+        }
+        o[e] = silu_fast(a * P.scale) * (u * P.scale);
+      }
+      if (valid) {
+        const int f = nt * (BN / 2) + f0;  // output feature
+        __half* y = reinterpret_cast<__half*>(P.y) + row * P.y_ld + f;
+        *reinterpret_cast<uint4*>(y) = make_uint4(pack_h2(o[0], o[1]), pack_h2(o[2], o[3]), pack_h2(o[4], o[5]),
+                                                  pack_h2(o[6], o[7]));
+        *reinterpret_cast<uint4*>(y + 8) = make_uint4(pack_h2(o[8], o[9]), pack_h2(o[10], o[11]),
+                                                      pack_h2(o[12], o[13]), pack_h2(o[14], o[15]));
+      }
+    }
+  } else {
+    for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
+      uint32_t raw[32];
+      tmem_ld32_nowait(tb + c0, raw);
+      tmem_wait_ld();
+      const int n0 = nt * BN + c0;
+      if (!valid || n0 >= P.N) continue;
+      float v[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        float a = __uint_as_float(raw[e]);
+        if (P.bias && n0 + e < P.N) a += P.bias[n0 + e];
+        v[e] = act_of(a * P.scale, P.act, P.prelu);
+      }
+      if (P.epi == HM_CEPI_GATED) {  // y (fp32) = res (fp32) + gate[b, n] * v
+        const float* rs = reinterpret_cast<const float*>(P.res) + row * P.res_ld + n0;
+        const float* gt = P.gate + static_cast<int64_t>(b) * P.gate_ld + n0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (n0 + e < P.N) v[e] = rs[e] + gt[e] * v[e];
+      } else if (P.epi == HM_CEPI_RES) {  // y = v + res (fp16)
+        const __half* rs = reinterpret_cast<const __half*>(P.res) + row * P.res_ld + n0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (n0 + e < P.N) v[e] += __half2float(rs[e]);
+      } else if (P.epi == HM_CEPI_ROPE && n0 < P.rope_cols) {
+        // pairs (n, n+1), n even, rotated by the angle of (t, (n % hd) / 2)
+        const float2* tab = P.rope + static_cast<int64_t>(t) * (P.hd / 2) + (n0 % P.hd) / 2;
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float2 cs = tab[e / 2];
+          const float x1 = v[e], x2 = v[e + 1];
+          v[e] = x1 * cs.x - x2 * cs.y;
+          v[e + 1] = x1 * cs.y + x2 * cs.x;
+        }
+      }
+      store_row32(P, row, n0, v);
+    }
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThr, 1)
     conv_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
@@ -218,76 +292,10 @@ __global__ void __launch_bounds__(kThr, 1)
       const int ab = i & 1;
       const TileIdx ti = tile_of(P, tt);
       const int t = ti.mt * kBM + r;
-      const bool valid = t < P.T;
-      const int64_t row = static_cast<int64_t>(ti.b) * P.T + t;
       mbar_wait_ab(&sm.acc_full[ab], (i >> 1) & 1, err, abort_s);
       tc_fence_after();
       const uint32_t tb = tmem + (static_cast<uint32_t>(32 * q4) << 16) + ab * BN;
-      if (P.epi == HM_CEPI_SILU) {
-        // weight rows in blocks of 256: 128 gate rows then the same 128 features' up rows;
-        // this warp: features h*64 .. h*64+63 of the block (BN == 256)
-        for (int f0 = h * (BN / 4); f0 < (h + 1) * (BN / 4); f0 += 16) {
-          float gv[16], uv[16], o[32];
-          tmem_ld16(tb + f0, gv);
-          tmem_ld16(tb + BN / 2 + f0, uv);
-          const int ng = ti.nt * BN + f0, nu = ng + BN / 2;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float a = gv[e], u = uv[e];
-            if (P.bias) {
-              a += P.bias[ng + e];
-              u += P.bias[nu + e];
-            }
-            o[e] = silu_fast(a * P.scale) * (u * P.scale);
-          }
-          if (valid) {
-            const int f = ti.nt * (BN / 2) + f0;  // output feature
-            __half* y = reinterpret_cast<__half*>(P.y) + row * P.y_ld + f;
-            *reinterpret_cast<uint4*>(y) = make_uint4(pack_h2(o[0], o[1]), pack_h2(o[2], o[3]), pack_h2(o[4], o[5]),
-                                                      pack_h2(o[6], o[7]));
-            *reinterpret_cast<uint4*>(y + 8) = make_uint4(pack_h2(o[8], o[9]), pack_h2(o[10], o[11]),
-                                                          pack_h2(o[12], o[13]), pack_h2(o[14], o[15]));
-          }
-        }
-      } else {
-        for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
-          uint32_t raw[32];
-          tmem_ld32_nowait(tb + c0, raw);
-          tmem_wait_ld();
-          const int n0 = ti.nt * BN + c0;
-          if (!valid || n0 >= P.N) continue;
-          float v[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            float a = __uint_as_float(raw[e]);
-            if (P.bias && n0 + e < P.N) a += P.bias[n0 + e];
-            v[e] = act_of(a * P.scale, P.act, P.prelu);
-          }
-          if (P.epi == HM_CEPI_GATED) {  // y (fp32) = res (fp32) + gate[b, n] * v
-            const float* rs = reinterpret_cast<const float*>(P.res) + row * P.res_ld + n0;
-            const float* gt = P.gate + static_cast<int64_t>(ti.b) * P.gate_ld + n0;
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (n0 + e < P.N) v[e] = rs[e] + gt[e] * v[e];
-          } else if (P.epi == HM_CEPI_RES) {  // y = v + res (fp16)
-            const __half* rs = reinterpret_cast<const __half*>(P.res) + row * P.res_ld + n0;
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (n0 + e < P.N) v[e] += __half2float(rs[e]);
-          } else if (P.epi == HM_CEPI_ROPE && n0 < P.rope_cols) {
-            // pairs (n, n+1), n even, rotated by the angle of (t, (n % hd) / 2)
-            const float2* tab = P.rope + static_cast<int64_t>(t) * (P.hd / 2) + (n0 % P.hd) / 2;
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const float2 cs = tab[e / 2];
-              const float x1 = v[e], x2 = v[e + 1];
-              v[e] = x1 * cs.x - x2 * cs.y;
-              v[e + 1] = x1 * cs.y + x2 * cs.x;
-            }
-          }
-          store_row32(P, row, n0, v);
-        }
-      }
+      conv_epilogue<BN>(P, tb, ti.nt, ti.b, t, h);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
@@ -298,6 +306,151 @@ __global__ void __launch_bounds__(kThr, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+// ---------------------------------------------------------------- SM-pair variant
+// The same GEMM on pairs of SMs (a cluster of two CTAs, tcgen05 cta_group::2): a pair
+// computes 256 output rows x BN columns, each CTA loading its own 128 rows of x and its half
+// (BN/2 rows) of the weight tile by TMA (no multicast), the loads completing on the leader
+// CTA's barriers; the leader's thread issues tcgen05.mma.cta_group::2 (M=256, N=BN, K=16),
+// which reads both CTAs' shared memory, with fp32 accumulators in each CTA's TMEM (its 128
+// rows x BN columns), and its commits (multicast to both CTAs) free the ring slots and
+// signal finished tiles.  Per SM this halves the weight bytes streamed from L2 per MMA flop.
+// Tiles: 256-row blocks of one item (rank r takes rows 128 r .. of the block) x BN columns.
+template <int BN>
+struct PairCfg {
+  static constexpr int kBH = (BN / 2) * kBK * 2;  // this CTA's half of a weight stage
+  static constexpr int NST = kSmemBudget / (kABytes + kBH);  // 8 (bn 128) / 6 (bn 256) stages
+};
+
+template <int BN>
+struct PairSmem {
+  uint8_t a[PairCfg<BN>::NST][kABytes];
+  uint8_t b[PairCfg<BN>::NST][PairCfg<BN>::kBH];
+  uint64_t full[PairCfg<BN>::NST], empty[PairCfg<BN>::NST];  // full: used in the leader only
+  uint64_t acc_full[2], acc_empty[2];  // acc_empty: the leader's, both CTAs' epilogue warps arrive
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+HM_DEV void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThr, 1)
+    conv_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                          const __grid_constant__ ConvP P) {
+  constexpr int NST = PairCfg<BN>::NST;
+  constexpr int kBH = PairCfg<BN>::kBH;
+  extern __shared__ uint8_t smem_raw[];
+  PairSmem<BN>& sm = *reinterpret_cast<PairSmem<BN>*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  int* const err = P.err;
+  const int nk = P.taps * P.nkc;
+
+  if (tid == 0) {
+    sm.abort_flag = 0;
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&sm.full[i], 1);   // the leader's producer (expect_tx) + both CTAs' copies (bytes)
+      mbar_init(&sm.empty[i], 1);  // the leader's MMA commit
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.acc_full[i], 1);            // the leader's MMA commit
+      mbar_init(&sm.acc_empty[i], 2 * kEpiW);   // every epilogue warp of both CTAs
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(&sm.tmem_base, 2 * BN);
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort_s = &sm.abort_flag;
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      prefetch_tensormap(&xmap);
+      prefetch_tensormap(&wmap);
+      const uint32_t full0 = dsmem_addr(&sm.full[0], 0);  // the leader's ring barriers
+      int g = 0;
+      for (int tt = pair; tt < P.tiles; tt += npairs) {
+        const TileIdx ti = tile_of(P, tt);
+        const int t0 = ti.mt * 2 * kBM + static_cast<int>(rank) * kBM;
+        for (int j = 0; j < P.taps; ++j) {
+          const int xrow = t0 + P.off0 + j * P.dil;
+          const int wrow = j * P.npad + ti.nt * BN + static_cast<int>(rank) * (BN / 2);
+          for (int kc = 0; kc < P.nkc; ++kc, ++g) {
+            const int s = g % NST;
+            if (g >= NST) mbar_wait_ab(&sm.empty[s], ((g / NST) - 1) & 1, err, abort_s);
+            if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 2 * (kABytes + kBH));  // both CTAs' loads
+            tma_load_3d_pair(sm.a[s], &xmap, kc * kBK, xrow, ti.b, full0 + 8 * s);
+            tma_load_2d_pair(sm.b[s], &wmap, kc * kBK, wrow, full0 + 8 * s);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16(2 * kBM, BN);
+      const uint64_t a0 = sw128_desc(smem_u32(sm.a[0])), b0 = sw128_desc(smem_u32(sm.b[0]));
+      int g = 0, i = 0;
+      for (int tt = pair; tt < P.tiles; tt += npairs, ++i) {
+        const int ab = i & 1;
+        // the accumulator's previous tile has been read out by both CTAs' epilogues
+        if (i >= 2 && !*abort_s && !mbar_wait_cluster(&sm.acc_empty[ab], ((i >> 1) - 1) & 1, err)) *abort_s = 1;
+        tc_fence_after();
+        const uint32_t acc = tmem + ab * BN;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % NST;
+          mbar_wait_ab(&sm.full[s], (g / NST) & 1, err, abort_s);
+          tc_fence_after();
+          const uint64_t ad = a0 + s * (kABytes >> 4), bd = b0 + s * (kBH >> 4);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) umma_f16_pair(acc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit_pair(&sm.empty[s]);
+        }
+        umma_commit_pair(&sm.acc_full[ab]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs: their 128 rows)
+    const uint32_t acc_empty0 = dsmem_addr(&sm.acc_empty[0], 0);  // the leader's
+    const int q4 = warp & 3, h = (warp - 2) >> 2, r = 32 * q4 + lane;
+    int i = 0;
+    for (int tt = pair; tt < P.tiles; tt += npairs, ++i) {
+      const int ab = i & 1;
+      const TileIdx ti = tile_of(P, tt);
+      const int t = ti.mt * 2 * kBM + static_cast<int>(rank) * kBM + r;
+      mbar_wait_ab(&sm.acc_full[ab], (i >> 1) & 1, err, abort_s);
+      tc_fence_after();
+      const uint32_t tb = tmem + (static_cast<uint32_t>(32 * q4) << 16) + ab * BN;
+      conv_epilogue<BN>(P, tb, ti.nt, ti.b, t, h);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&sm.acc_empty[ab]);
+        else
+          mbar_arrive_dsmem(acc_empty0 + 8 * ab);
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA leaves while the pair's copies, MMAs or commits may touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 2 * BN);
   }
 }
 
@@ -375,6 +528,24 @@ cudaError_t launch_conv(const CUtensorMap& xm, const CUtensorMap& wm, ConvP p, h
   const int sms = sm_count_cached();
   const int grid = p.tiles < sms ? p.tiles : sms;
   return hm_launch(conv_gemm_kernel<BN>, dim3(grid), dim3(kThr), smem, st, 1, xm, wm, p);
+}
+
+template <int BN>
+cudaError_t launch_conv_pair(const CUtensorMap& xm, const CUtensorMap& wm, ConvP p, hm_stream_t st) {
+  const size_t smem = sizeof(PairSmem<BN>) + 1024;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(conv_gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  p.mtiles = (p.T + 2 * kBM - 1) / (2 * kBM);  // 256-row blocks per item
+  p.ntiles = p.npad / BN;
+  p.tiles = p.B * p.mtiles * p.ntiles;
+  const int pairs_avail = sm_count_cached() / 2;
+  const int pairs = p.tiles < pairs_avail ? p.tiles : pairs_avail;
+  return hm_launch(conv_gemm_pair_kernel<BN>, dim3(2 * pairs), dim3(kThr), smem, st, 0, xm, wm, p);
 }
 
 // Tile width by a cost model: waves of tiles over the SMs times the time of one tile's
@@ -654,20 +825,30 @@ extern "C" int hm_conv1d_gemm(const hm_conv_desc* d, hm_stream_t stream) {
   // 16-byte vector stores of whole 32-column groups (outputs of fewer columns are stored per element)
   if (d->y_ld < out_cols || (out_cols >= 32 && d->y_ld % (d->y_f32 ? 4 : 8))) return HM_EARG;
   if (d->epi == HM_CEPI_SILU && d->y_ld % 8) return HM_EARG;
-  if (d->epi == HM_CEPI_SILU && (d->N % 256 || d->npad != d->N || d->y_f32 || d->bn > 0 && d->bn != 256)) return HM_EARG;
+  if (d->epi == HM_CEPI_SILU && (d->N % 256 || d->npad != d->N || d->y_f32)) return HM_EARG;
   if (d->epi == HM_CEPI_GATED && (!d->res || !d->gate || !d->y_f32)) return HM_EARG;
   if (d->epi == HM_CEPI_RES && (!d->res || d->y_f32)) return HM_EARG;
   if (d->epi == HM_CEPI_ROPE && (!d->rope || d->hd < 2 || d->hd % 64 || d->rope_cols % d->hd)) return HM_EARG;
   const int mtiles = (d->T + kBM - 1) / kBM;
-  int bn = d->epi == HM_CEPI_SILU ? 256 : (d->bn > 0 ? d->bn : pick_bn(d, mtiles));
-  if ((bn != 64 && bn != 128 && bn != 256) || d->npad % bn) return HM_EARG;
+  // bn > 0: single-SM tiles of that width; -128 / -256: SM-pair tiles (256 rows) of that width;
+  // 0: SM pairs of 256 columns where they measured faster (K >= 3072 and at least two waves of
+  // pair tiles: the codec's second-stage q|k|v and gate|up, 3-9 %), else the tile-width model
+  bool pair = d->bn < 0;
+  if (d->bn == 0 && d->npad % 256 == 0 && static_cast<int64_t>(d->cin) * d->taps >= 3072) {
+    const int64_t ptiles = static_cast<int64_t>(d->B) * ((d->T + 2 * kBM - 1) / (2 * kBM)) * (d->npad / 256);
+    pair = ptiles >= sm_count_cached();
+  }
+  int bn = d->bn < 0 ? -d->bn
+                     : (pair || d->epi == HM_CEPI_SILU ? 256 : (d->bn > 0 ? d->bn : pick_bn(d, mtiles)));
+  if (pair ? (bn != 128 && bn != 256) : (bn != 64 && bn != 128 && bn != 256)) return HM_EARG;
+  if (d->npad % bn || (d->epi == HM_CEPI_SILU && bn != 256)) return HM_EARG;
   CUtensorMap xm, wm;
   // x as {cin, tin, B} (an item's rows zero-fill past its ends); one item: any valid item stride
   const int64_t xb = d->B > 1 ? d->x_bstride : static_cast<int64_t>(d->tin) * d->x_ld;
   if (d->B > 1 && d->x_bstride < static_cast<int64_t>(d->tin) * d->x_ld) return HM_EARG;
   if (!conv_map(3, d->x, d->cin, d->tin, d->B, d->x_ld * 2, xb * 2, kBM, &xm)) return HM_EARG;
-  if (!conv_map(2, d->w, d->cin, static_cast<int64_t>(d->taps) * d->npad, 1, static_cast<int64_t>(d->cin) * 2, 0, bn,
-                &wm))
+  if (!conv_map(2, d->w, d->cin, static_cast<int64_t>(d->taps) * d->npad, 1, static_cast<int64_t>(d->cin) * 2, 0,
+                pair ? bn / 2 : bn, &wm))
     return HM_EARG;
   ConvP p;
   p.B = d->B;
@@ -697,7 +878,9 @@ extern "C" int hm_conv1d_gemm(const hm_conv_desc* d, hm_stream_t stream) {
   p.y_ld = d->y_ld;
   p.err = d->err;
   cudaError_t e;
-  if (bn == 256)
+  if (pair)
+    e = bn == 256 ? launch_conv_pair<256>(xm, wm, p, stream) : launch_conv_pair<128>(xm, wm, p, stream);
+  else if (bn == 256)
     e = launch_conv<256>(xm, wm, p, stream);
   else if (bn == 128)
     e = launch_conv<128>(xm, wm, p, stream);

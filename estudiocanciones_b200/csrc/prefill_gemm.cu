@@ -100,45 +100,6 @@ struct GemmParams {
 // a < -87 the quotient is 0, which is also the fp16 value of silu(a) there)
 HM_DEV float silu_f(float a) { return __fdividef(a, 1.f + __expf(-a)); }
 
-// ---------------------------------------------------------------- SM-pair (cta_group::2) primitives
-// TMEM allocation of the pair: one warp of each CTA, same warp and destination in both.
-HM_DEV void tmem_alloc_pair(uint32_t* dst, uint32_t cols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-HM_DEV void tmem_dealloc_pair(uint32_t base, uint32_t cols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols) : "memory");
-}
-// Tiled 2-D load into this CTA's shared memory, completion counted on an mbarrier of
-// either CTA of the pair (`bar`: shared::cluster address).  No multicast.
-HM_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-// M=256 MMA over the pair: A rows 0-127 / 128-255 and B rows (N) 0-127 / 128-255 from the
-// same shared-memory offsets of CTA 0 / CTA 1; D rows 0-127 / 128-255 in their TMEM.
-HM_DEV void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive on the barrier at `bar`'s offset in both CTAs of the pair once the MMAs issued so
-// far have completed.
-HM_DEV void umma_commit_pair(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(static_cast<uint16_t>(3))
-      : "memory");
-}
-
 // ---------------------------------------------------------------- epilogue (both kernels)
 // Runs once every MMA of the tile has completed: `stage` (64 KB) holds the tile's fp16
 // results, `scl` (256 values) its column scales; `release()` runs once the warp's TMEM

@@ -265,7 +265,8 @@ int hm_prefill_attn(const void* q, const void* kc, const void* vc, void* o, int 
  * Rows: input item b, row t at x + b*x_bstride + t*x_ld; output row b*T + t at y + row*y_ld
  * (res the same with res_ld).  cin % 64 == 0, npad % 64 == 0 (w holds npad >= N rows per
  * tap, the extra rows unused), x_ld/x_bstride % 8 == 0, 16-byte aligned x, w, y.
- * bn: tile width 64/128/256, 0 = automatic (256 for HM_CEPI_SILU). */
+ * bn: single-SM tile width 64/128/256; -128 / -256: tiles of 256 rows on SM pairs (a cluster of two
+ * CTAs, tcgen05 cta_group::2, same results bit for bit); 0 = automatic. */
 #define HM_ACT_NONE 0
 #define HM_ACT_PRELU 1
 #define HM_ACT_SILU 2

@@ -426,3 +426,38 @@ def test_graph_replay_equals_eager(L, gold):
     b = run(graphed)  # replays
     assert all("graph" in p for k, p in graphed._plans.items() if k[0] in ("flow", "dec"))
     assert torch.equal(a, b)
+
+
+def test_conv_sm_pairs_equal_single_sm(L):
+    """The SM-pair variant (bn -128 / -256: 256-row tiles over two SMs, cta_group::2) gives the
+    single-SM results bit for bit: same products, same k order per element.  Ragged rows (333:
+    the second pair's upper half lies past the item), three taps, two items, and the SiLU-mul,
+    RoPE and gated-residual epilogues."""
+    x = rnd(2, 333, 256, seed=40)
+    w = rnd(3, 512, 256, s=0.05, seed=41)
+    bias = rnd(512, s=0.1, dtype=torch.float32, seed=42)
+    ref = run_conv(L, x, w, off0=-1, bias=bias, bn=256, y_f32=True)
+    for bn in (-128, -256):
+        assert torch.equal(run_conv(L, x, w, off0=-1, bias=bias, bn=bn, y_f32=True), ref), bn
+    ok, err = close(ref.view(2, 333, 512), ref_conv(x, w, -1, 1, 333) + bias.double(), 2e-5)
+    assert ok, err
+    # SiLU-mul (pair tiles of 256: 128 gate rows on one SM, the 128 up rows on the other)
+    xs = rnd(1, 300, 192, seed=43)
+    ws = rnd(1, 512, 192, s=0.07, seed=44)
+    assert torch.equal(run_conv(L, xs, ws, epi=L.HM_CEPI_SILU, bn=-256), run_conv(L, xs, ws, epi=L.HM_CEPI_SILU))
+    # RoPE of q and k
+    hd, D = 64, 128
+    xr = rnd(2, 200, D, seed=45)
+    wr = rnd(1, 3 * D, D, s=D ** -0.5, seed=46)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, dtype=torch.float32, device=DEV) / hd))
+    fr = torch.arange(200, dtype=torch.float32, device=DEV)[:, None] * inv[None]
+    rope = torch.stack([fr.cos(), fr.sin()], -1).contiguous()
+    kw = dict(epi=L.HM_CEPI_ROPE, rope=rope, rope_cols=2 * D, hd=hd)
+    assert torch.equal(run_conv(L, xr, wr, bn=-128, **kw), run_conv(L, xr, wr, bn=128, **kw))
+    # gated residual into an fp32 stream, in place
+    h1 = rnd(2 * 333, 512, dtype=torch.float32, seed=47)
+    h2 = h1.clone()
+    gate = rnd(2, 512, dtype=torch.float32, seed=48)
+    run_conv(L, x, w, off0=-1, epi=L.HM_CEPI_GATED, res=h1, gate=gate, gate_ld=512, y_f32=True, y=h1, bn=256)
+    run_conv(L, x, w, off0=-1, epi=L.HM_CEPI_GATED, res=h2, gate=gate, gate_ld=512, y_f32=True, y=h2, bn=-256)
+    assert torch.equal(h1, h2)
