@@ -461,3 +461,39 @@ def test_conv_sm_pairs_equal_single_sm(L):
     run_conv(L, x, w, off0=-1, epi=L.HM_CEPI_GATED, res=h1, gate=gate, gate_ld=512, y_f32=True, y=h1, bn=256)
     run_conv(L, x, w, off0=-1, epi=L.HM_CEPI_GATED, res=h2, gate=gate, gate_ld=512, y_f32=True, y=h2, bn=-256)
     assert torch.equal(h1, h2)
+
+
+def test_codec_api_surface(L, gold, tmp_path):
+    """load_codec(path) + decode(codec, frames) as app/codec_lite.py calls them: the same audio as
+    the codec built from the tensors; codes outside the codebook are clamped like the reference's
+    decode; abort_signal returns None; a non-default duration runs its own window shape."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from estudiocanciones_b200 import codec as codec_lite
+    from estudiocanciones_b200.codec import HeartCodecB200
+    from estudiocanciones_b200.codec_checkpoint import TINY_CODEC, synthetic_codec_tensors
+    sd = synthetic_codec_tensors(TINY_CODEC, 4321)
+    f = tmp_path / "codec.safetensors"
+    save_file(sd, str(f))
+    f.with_suffix(".json").write_text(json.dumps(TINY_CODEC.to_dict()))
+    c = codec_lite.load_codec(f, torch.float16, device=DEV)
+    ref = HeartCodecB200(sd, TINY_CODEC, device=DEV)
+    codes = torch.from_numpy(gold["detok1_codes"]).clone()
+    torch.manual_seed(12)
+    a = codec_lite.decode(c, codes, steps=2, guidance=1.0).clone()
+    torch.manual_seed(12)
+    b = ref.detokenize(codes, num_steps=2, guidance_scale=1.0).clone()
+    assert torch.equal(a, b)
+    bad = codes.clone()
+    bad[0, 5], bad[3, 9] = -7, TINY_CODEC.codebook_size + 100
+    clamped = bad.clamp(0, TINY_CODEC.codebook_size - 1)
+    torch.manual_seed(12)
+    x = codec_lite.decode(c, bad, steps=2, guidance=1.0).clone()
+    torch.manual_seed(12)
+    y = ref.detokenize(clamped, num_steps=2, guidance_scale=1.0).clone()
+    assert torch.equal(x, y)
+    assert ref.detokenize(codes, abort_signal=lambda: True) is None
+    short = ref.detokenize(codes[:, :100], duration=10.24, num_steps=1, guidance_scale=1.25)
+    assert short.shape == (2, int(100 / 12.5 * TINY_CODEC.sample_rate)) and torch.isfinite(short).all()

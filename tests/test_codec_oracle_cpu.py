@@ -64,3 +64,31 @@ def test_detokenize_matches_reference(gold, oracle, case):
     ref = torch.from_numpy(gold[f"detok{case}_wav"])
     assert wav.shape == ref.shape == (2, int(n / 12.5 * TINY_CODEC.sample_rate))
     assert (wav - ref).abs().max() <= 1e-4 * ref.abs().max()
+
+
+def test_codec_checkpoint_round_trip(tmp_path):
+    """load_codec_tensors reads what the reference's load_codec reads: one .safetensors with its
+    .json beside it, or a directory with config.json and model*.safetensors; the audio
+    encoder's tensors are dropped (app/codec_lite.py:13-26)."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from estudiocanciones_b200.codec_checkpoint import CodecConfig, load_codec_tensors
+    sd = synthetic_codec_tensors(TINY_CODEC, 1)
+    sd_enc = dict(sd)
+    sd_enc["scalar_model.encoder.0.bias"] = torch.zeros(64)
+    f = tmp_path / "codec_bf16.safetensors"
+    save_file({k: v.to(torch.bfloat16) if v.is_floating_point() else v for k, v in sd_enc.items()}, str(f))
+    cfgd = dict(TINY_CODEC.to_dict(), model_type="heartcodec", unknown_key=3)
+    f.with_suffix(".json").write_text(json.dumps(cfgd))
+    t, cfg = load_codec_tensors(f)
+    assert cfg == TINY_CODEC and set(t) == set(sd)
+    assert all(torch.equal(t[k], sd[k].to(torch.bfloat16)) for k in sd)
+    d = tmp_path / "dir"
+    d.mkdir()
+    save_file({k: v for k, v in sd_enc.items()}, str(d / "model.safetensors"))
+    (d / "config.json").write_text(json.dumps(cfgd))
+    t2, cfg2 = load_codec_tensors(d)
+    assert cfg2 == TINY_CODEC and set(t2) == set(sd) and torch.equal(t2[next(iter(sd))], sd[next(iter(sd))])
+    assert CodecConfig.from_dict(None) == CodecConfig()

@@ -6,12 +6,15 @@ device and stall, or an application that serves all device memory from its own
 fixed arena).  It keeps its scratch in a fixed array inside the library instead of
 taking a workspace.  This test calls it through the C ABI twice in a row (the
 array keeps the previous call's contents) and checks it against the allocating
-entry point, `hm_decode_attn`, with the tolerance the other attention tests use.
+entry point, `hm_decode_attn`, and against the oracle's restatement of the
+reference kernel, with the tolerance the other attention tests use.
 """
 import math
 
 import pytest
 import torch
+
+from oracle import heartmula_oracle as O
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -51,6 +54,10 @@ def test_noalloc_attention_matches_allocating_entry_point(lib):
         assert rc == 0
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float(), ref.float(), atol=2e-3, rtol=5e-3)
+        # and directly against the oracle's restatement of the reference kernel (_attn +
+        # _attn_combine, app/kernels.py:112-167) on the host
+        orc = O.decode_attn(q.cpu(), kc.cpu(), vc.cpu(), p.cpu(), S, Hq, Hk)
+        torch.testing.assert_close(out.float().cpu(), orc.float(), atol=2e-3, rtol=5e-3)
     assert kernels.read_errors(DEV) == 0
 
 
