@@ -53,7 +53,8 @@ def args_():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--case", default="frame",
-                    choices=["frame", "gemv", "attn", "sampler", "prefill", "q8", "codec", "codec-est", "conv"],
+                    choices=["frame", "gemv", "attn", "sampler", "prefill", "q8", "codec", "codec-est", "codec-dec",
+                             "conv"],
                     help="frame: the benchmark; gemv/attn: a small single-kernel case for ncu captures; codec: "
                          "the detokenize timing alone; codec-est: estimator forwards of the full codec shape "
                          "(--reps of them, for launch lists and captures)")
@@ -504,6 +505,27 @@ def run_conv_case(a):
           flush=True)
 
 
+def run_codec_dec_case(a):
+    """--reps waveform-decoder runs of one full window (744 latent frames, two bands, full
+    codec shape), eager, after one warm-up run: for launch lists and kernel captures."""
+    from estudiocanciones_b200.codec import HeartCodecB200, decoder_flops
+    from estudiocanciones_b200.codec_checkpoint import FULL_CODEC, synthetic_codec_tensors
+    dev = torch.device("cuda", 0)
+    c = HeartCodecB200(synthetic_codec_tensors(FULL_CODEC, 1), FULL_CODEC, device=dev, graphs=False)
+    lat = torch.randn(744, FULL_CODEC.out_channels, device=dev) * 0.5
+    c.scalar_decode(lat)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.reps):
+        c.scalar_decode(lat)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.reps
+    fl = decoder_flops(FULL_CODEC, 744)
+    print(json.dumps({"case": "codec-dec", "ms": round(ms, 3), "tflops": round(fl / ms / 1e9, 1)}), flush=True)
+
+
 def run_codec_est_case(a):
     """--reps estimator forwards of the full codec shape (2 items x 744 frames), eager, after
     one warm-up forward: a short run for launch lists and kernel captures."""
@@ -877,6 +899,9 @@ def main():
         return
     if a.case == "conv":
         run_conv_case(a)
+        return
+    if a.case == "codec-dec":
+        run_codec_dec_case(a)
         return
     if a.case != "frame":
         run_case(a)

@@ -57,6 +57,7 @@ template <int BN>
 struct ConvSmem {
   uint8_t a[CCfg<BN>::NST][kABytes];
   uint8_t b[CCfg<BN>::NST][CCfg<BN>::kBBytes];
+  float stg[kEpiW][32 * 32];  // per epilogue warp: 32 rows x 32 columns in flight to global memory
   uint64_t full[CCfg<BN>::NST], empty[CCfg<BN>::NST], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -105,26 +106,96 @@ HM_DEV TileIdx tile_of(const ConvP& P, int tt) {
   return r;
 }
 
-// Store 32 consecutive values of one row (fp16 or fp32), columns n0 .. n0+31 masked to N.
-HM_DEV void store_row32(const ConvP& P, int64_t row, int n0, const float* v) {
-  if (P.y_f32) {
-    float* y = reinterpret_cast<float*>(P.y) + row * P.y_ld + n0;
-    if (n0 + 32 <= P.N) {
+// Copy-out of one staged 32 x 32 chunk (rows t0 .. t0+31 of item b, columns n0 .. n0+31) with
+// the residual / gate epilogues, along rows in 16-byte lanes.  Rows past T are skipped; a
+// chunk that crosses N goes per element.
+HM_DEV void conv_copy_out(const ConvP& P, const float* stg, int64_t row0, int t0, int b, int n0) {
+  const int lane = threadIdx.x & 31;
+  const bool full_cols = n0 + 32 <= P.N;
+  if (full_cols) {
+    // whole chunk: the residual (and gate) loads of every pass are issued before any store, so
+    // their latencies overlap (the output may alias the residual, which keeps the compiler from
+    // moving a load above an earlier store)
+    if (P.y_f32) {  // lane = (row 4i + lane/8, columns 4 (lane%8) ..)
+      const int c = (lane & 7) * 4, n = n0 + c;
+      float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (P.epi == HM_CEPI_GATED) gv = *reinterpret_cast<const float4*>(P.gate + static_cast<int64_t>(b) * P.gate_ld + n);
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(y + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-    } else {
-      for (int e = 0; e < 32 && n0 + e < P.N; ++e) y[e] = v[e];
-    }
-  } else {
-    __half* y = reinterpret_cast<__half*>(P.y) + row * P.y_ld + n0;
-    if (n0 + 32 <= P.N) {
+      for (int half = 0; half < 2; ++half) {  // two batches of four passes (registers)
+        float4 rv[4];
+        if (P.epi == HM_CEPI_GATED) {
 #pragma unroll
-      for (int e = 0; e < 32; e += 8)
-        *reinterpret_cast<uint4*>(y + e) = make_uint4(pack_h2(v[e], v[e + 1]), pack_h2(v[e + 2], v[e + 3]),
-                                                      pack_h2(v[e + 4], v[e + 5]), pack_h2(v[e + 6], v[e + 7]));
-    } else {
-      for (int e = 0; e < 32 && n0 + e < P.N; ++e) y[e] = __float2half_rn(v[e]);
+          for (int i = 0; i < 4; ++i) {
+            const int rr = 4 * (4 * half + i) + (lane >> 3);
+            rv[i] = t0 + rr < P.T ? *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P.res) +
+                                                                     (row0 + rr) * P.res_ld + n)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = 4 * (4 * half + i) + (lane >> 3);
+          if (t0 + rr >= P.T) continue;
+          float4 f = *reinterpret_cast<const float4*>(stg + rr * 32 + (((c >> 2) ^ (rr & 7)) << 2));
+          if (P.epi == HM_CEPI_GATED) {
+            f.x = rv[i].x + gv.x * f.x;
+            f.y = rv[i].y + gv.y * f.y;
+            f.z = rv[i].z + gv.z * f.z;
+            f.w = rv[i].w + gv.w * f.w;
+          }
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.y) + (row0 + rr) * P.y_ld + n) = f;
+        }
+      }
+    } else {  // fp16: lane = (row 8i + lane/4, columns 8 (lane%4) ..)
+      const int c = (lane & 3) * 8, n = n0 + c;
+      uint4 rv[4];
+      if (P.epi == HM_CEPI_RES) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = 8 * i + (lane >> 2);
+          rv[i] = t0 + rr < P.T
+                      ? *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(P.res) + (row0 + rr) * P.res_ld + n)
+                      : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rr = 8 * i + (lane >> 2);
+        if (t0 + rr >= P.T) continue;
+        const float* sr = stg + rr * 32;
+        const float4 f0 = *reinterpret_cast<const float4*>(sr + ((((c >> 2)) ^ (rr & 7)) << 2));
+        const float4 f1 = *reinterpret_cast<const float4*>(sr + ((((c >> 2) + 1) ^ (rr & 7)) << 2));
+        float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+        if (P.epi == HM_CEPI_RES) {
+          const __half2* h2 = reinterpret_cast<const __half2*>(&rv[i]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 r2 = __half22float2(h2[e]);
+            v[2 * e] += r2.x;
+            v[2 * e + 1] += r2.y;
+          }
+        }
+        *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(P.y) + (row0 + rr) * P.y_ld + n) =
+            make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+      }
     }
+    return;
+  }
+  // a chunk past N: per element, lane = row, columns n0 .. N-1
+  const int rr = lane;
+  if (t0 + rr >= P.T) return;
+  const int64_t row = row0 + rr;
+  for (int e = 0; e < 32 && n0 + e < P.N; ++e) {
+    float x = stg[rr * 32 + ((((e >> 2)) ^ (rr & 7)) << 2) + (e & 3)];
+    const int n = n0 + e;
+    if (P.epi == HM_CEPI_GATED)
+      x = reinterpret_cast<const float*>(P.res)[row * P.res_ld + n] + P.gate[static_cast<int64_t>(b) * P.gate_ld + n] * x;
+    else if (P.epi == HM_CEPI_RES)
+      x += __half2float(reinterpret_cast<const __half*>(P.res)[row * P.res_ld + n]);
+    if (P.y_f32)
+      reinterpret_cast<float*>(P.y)[row * P.y_ld + n] = x;
+    else
+      reinterpret_cast<__half*>(P.y)[row * P.y_ld + n] = __float2half_rn(x);
   }
 }
 
@@ -132,7 +203,7 @@ HM_DEV void store_row32(const ConvP& P, int64_t row, int n0, const float* v) {
 // the tile's columns (SiLU-mul: a quarter of the features), bias / scale / activation and the
 // epilogue variant, then the stores.  Warp-collective (tcgen05.ld): every lane of the warp calls it.
 template <int BN>
-HM_DEV void conv_epilogue(const ConvP& P, uint32_t tb, int nt, int b, int t, int h) {
+HM_DEV void conv_epilogue(const ConvP& P, uint32_t tb, int nt, int b, int t, int h, float* stg) {
   const bool valid = t < P.T;
   const int64_t row = static_cast<int64_t>(b) * P.T + t;
   if (P.epi == HM_CEPI_SILU) {
@@ -162,12 +233,18 @@ HM_DEV void conv_epilogue(const ConvP& P, uint32_t tb, int nt, int b, int t, int
       }
     }
   } else {
+    // per 32-column chunk: bias, scale, activation and RoPE in registers (this thread's row),
+    // then the chunk goes through the warp's staging buffer so that the residual / gate
+    // reads and the stores run along rows (16-byte lanes), not one row per lane
+    const int lane = threadIdx.x & 31;
+    const int t0 = t - lane;  // the warp's first row
+    const int64_t row0 = static_cast<int64_t>(b) * P.T + t0;
     for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
       uint32_t raw[32];
       tmem_ld32_nowait(tb + c0, raw);
       tmem_wait_ld();
       const int n0 = nt * BN + c0;
-      if (!valid || n0 >= P.N) continue;
+      if (n0 >= P.N) continue;  // uniform over the warp
       float v[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
@@ -175,18 +252,7 @@ HM_DEV void conv_epilogue(const ConvP& P, uint32_t tb, int nt, int b, int t, int
         if (P.bias && n0 + e < P.N) a += P.bias[n0 + e];
         v[e] = act_of(a * P.scale, P.act, P.prelu);
       }
-      if (P.epi == HM_CEPI_GATED) {  // y (fp32) = res (fp32) + gate[b, n] * v
-        const float* rs = reinterpret_cast<const float*>(P.res) + row * P.res_ld + n0;
-        const float* gt = P.gate + static_cast<int64_t>(b) * P.gate_ld + n0;
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (n0 + e < P.N) v[e] = rs[e] + gt[e] * v[e];
-      } else if (P.epi == HM_CEPI_RES) {  // y = v + res (fp16)
-        const __half* rs = reinterpret_cast<const __half*>(P.res) + row * P.res_ld + n0;
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (n0 + e < P.N) v[e] += __half2float(rs[e]);
-      } else if (P.epi == HM_CEPI_ROPE && n0 < P.rope_cols) {
+      if (P.epi == HM_CEPI_ROPE && n0 < P.rope_cols && valid) {
         // pairs (n, n+1), n even, rotated by the angle of (t, (n % hd) / 2)
         const float2* tab = P.rope + static_cast<int64_t>(t) * (P.hd / 2) + (n0 % P.hd) / 2;
 #pragma unroll
@@ -197,7 +263,14 @@ HM_DEV void conv_epilogue(const ConvP& P, uint32_t tb, int nt, int b, int t, int
           v[e + 1] = x1 * cs.y + x2 * cs.x;
         }
       }
-      store_row32(P, row, n0, v);
+      // row `lane` of the chunk: float4 q at slot q ^ (lane & 7) (four lanes per bank group)
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(stg + lane * 32 + ((q ^ (lane & 7)) << 2)) =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      __syncwarp();
+      conv_copy_out(P, stg, row0, t0, b, n0);
+      __syncwarp();
     }
   }
 }
@@ -295,7 +368,7 @@ __global__ void __launch_bounds__(kThr, 1)
       mbar_wait_ab(&sm.acc_full[ab], (i >> 1) & 1, err, abort_s);
       tc_fence_after();
       const uint32_t tb = tmem + (static_cast<uint32_t>(32 * q4) << 16) + ab * BN;
-      conv_epilogue<BN>(P, tb, ti.nt, ti.b, t, h);
+      conv_epilogue<BN>(P, tb, ti.nt, ti.b, t, h, sm.stg[warp - 2]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
@@ -328,6 +401,7 @@ template <int BN>
 struct PairSmem {
   uint8_t a[PairCfg<BN>::NST][kABytes];
   uint8_t b[PairCfg<BN>::NST][PairCfg<BN>::kBH];
+  float stg[kEpiW][32 * 32];  // per epilogue warp: 32 rows x 32 columns in flight to global memory
   uint64_t full[PairCfg<BN>::NST], empty[PairCfg<BN>::NST];  // full: used in the leader only
   uint64_t acc_full[2], acc_empty[2];  // acc_empty: the leader's, both CTAs' epilogue warps arrive
   uint32_t tmem_base;
@@ -435,7 +509,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThr, 1)
       mbar_wait_ab(&sm.acc_full[ab], (i >> 1) & 1, err, abort_s);
       tc_fence_after();
       const uint32_t tb = tmem + (static_cast<uint32_t>(32 * q4) << 16) + ab * BN;
-      conv_epilogue<BN>(P, tb, ti.nt, ti.b, t, h);
+      conv_epilogue<BN>(P, tb, ti.nt, ti.b, t, h, sm.stg[warp - 2]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -828,6 +902,10 @@ extern "C" int hm_conv1d_gemm(const hm_conv_desc* d, hm_stream_t stream) {
   if (d->epi == HM_CEPI_SILU && (d->N % 256 || d->npad != d->N || d->y_f32)) return HM_EARG;
   if (d->epi == HM_CEPI_GATED && (!d->res || !d->gate || !d->y_f32)) return HM_EARG;
   if (d->epi == HM_CEPI_RES && (!d->res || d->y_f32)) return HM_EARG;
+  // 16-byte residual / gate loads along rows (outputs of fewer than 32 columns go per element)
+  if (out_cols >= 32 && d->epi == HM_CEPI_GATED && (!al16(d->res) || d->res_ld % 4 || !al16(d->gate) || d->gate_ld % 4))
+    return HM_EARG;
+  if (out_cols >= 32 && d->epi == HM_CEPI_RES && (!al16(d->res) || d->res_ld % 8)) return HM_EARG;
   if (d->epi == HM_CEPI_ROPE && (!d->rope || d->hd < 2 || d->hd % 64 || d->rope_cols % d->hd)) return HM_EARG;
   const int mtiles = (d->T + kBM - 1) / kBM;
   // bn > 0: single-SM tiles of that width; -128 / -256: SM-pair tiles (256 rows) of that width;
