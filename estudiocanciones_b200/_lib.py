@@ -92,6 +92,8 @@ SIGNATURES = {
     "hm_codec_temb_post": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
     "hm_codec_overlap_add": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _I64, _P]),
     "hm_device_sm_count": (_I, [_I]),
+    "hm_gemv_box_form": (_I, [_P, _I, _I, _I]),
+    "hm_decode_attn_box_form": (_I, [_P, _I64]),
     "hm_abi_layout": (_SZ, [_I]),
     "hm_version": (C.c_char_p, []),
 }

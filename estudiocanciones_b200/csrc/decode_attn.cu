@@ -40,6 +40,7 @@ struct AttnParams {
   int* counters;
   int* err;
   int cluster;  // tensor-core kernel: the nsplit CTAs of a (row, KV head) form a cluster and merge in DSMEM
+  int box3;     // tensor-core kernel: K / V maps are 3-D, one request per tile of each (else two 2-D boxes)
 };
 
 constexpr int kMaxSplit = 64;
@@ -419,10 +420,15 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
     const int st = tt % kTcNst;
     const int y = row0 + tt * kTcPos;
     mbar_arrive_expect_tx(&sm.bar[st], 4 * kTcBox);
-    tma_load_2d_plain(sm.k[st][0], &kmap, 0, y, &sm.bar[st]);
-    tma_load_2d_plain(sm.k[st][1], &kmap, 64, y, &sm.bar[st]);
-    tma_load_2d_plain(sm.v[st][0], &vmap, 0, y, &sm.bar[st]);
-    tma_load_2d_plain(sm.v[st][1], &vmap, 64, y, &sm.bar[st]);
+    if (P.box3) {  // both 64-dim halves of the tile in one request each for K and V
+      tma_load_3d_plain(sm.k[st][0], &kmap, 0, y, 0, &sm.bar[st]);
+      tma_load_3d_plain(sm.v[st][0], &vmap, 0, y, 0, &sm.bar[st]);
+    } else {
+      tma_load_2d_plain(sm.k[st][0], &kmap, 0, y, &sm.bar[st]);
+      tma_load_2d_plain(sm.k[st][1], &kmap, 64, y, &sm.bar[st]);
+      tma_load_2d_plain(sm.v[st][0], &vmap, 0, y, &sm.bar[st]);
+      tma_load_2d_plain(sm.v[st][1], &vmap, 64, y, &sm.bar[st]);
+    }
   };
   const int n_first = min(kTcNst, ntile);
   int n_early = 0;  // leading tiles that end before pos[r]
@@ -675,14 +681,18 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tc_kernel(const __grid_c
   if (tid == 0) *ticket = 0;
 }
 
-// 2-D view [rows = B*Hk*L, 128] of an fp16 cache for the TMA (cached by pointer)
-bool cache_map(const void* base, int64_t rows, CUtensorMap* out) {
+// View of an fp16 cache [rows = B*Hk*L, 128] for the TMA (cached by pointer and kind):
+//  2-D {128, rows}, box 64 dims x 64 positions: two requests per tile;
+//  3-D {64, rows, 2} (dim within a half, position, half; the half stride is 128 bytes),
+//  box {64, 64, 2}: one request per tile, laid out in shared memory as [half][position][128 B],
+//  the two 2-D boxes one after the other.
+bool cache_map(const void* base, int64_t rows, bool three_d, CUtensorMap* out) {
   static std::mutex mu;
-  static std::unordered_map<const void*, std::pair<int64_t, CUtensorMap>> cache;
+  static std::unordered_map<const void*, std::pair<int64_t, CUtensorMap>> cache[2];
   {
     std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find(base);
-    if (it != cache.end() && it->second.first == rows) {
+    auto it = cache[three_d].find(base);
+    if (it != cache[three_d].end() && it->second.first == rows) {
       *out = it->second.second;
       return true;
     }
@@ -690,19 +700,37 @@ bool cache_map(const void* base, int64_t rows, CUtensorMap* out) {
   auto enc = hm_encode_fn();
   if (!enc) return false;
   CUtensorMap m;
-  cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {256};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTcPos)};
-  cuuint32_t es[2] = {1, 1};
-  if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return false;
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r;
+  if (three_d) {
+    cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), 2};
+    cuuint64_t strides[2] = {256, 128};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTcPos), 2};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {256};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTcPos)};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return false;
   std::lock_guard<std::mutex> lk(mu);
-  if (cache.size() > 4096) cache.clear();
-  cache[base] = {rows, m};
+  if (cache[three_d].size() > 4096) cache[three_d].clear();
+  cache[three_d][base] = {rows, m};
   *out = m;
   return true;
+}
+
+int attn_box_on() {
+  static const int on = [] {
+    const char* e = getenv("HM_ATTN_BOX");
+    return e ? atoi(e) : 1;
+  }();
+  return on;
 }
 
 // HM_ATTN_TC=0 selects the CUDA-core kernel for head_dim 128 (comparison runs)
@@ -716,8 +744,12 @@ bool attn_tc_enabled() {
 
 cudaError_t launch_attn_tc(const AttnParams& p, int B, int pdl, cudaStream_t st) {
   const int64_t rows = (int64_t)B * p.Hk * p.L;
+  // one request per K / V tile (HM_ATTN_BOX=1, the default), else two 2-D boxes each: the
+  // same bytes land at the same shared-memory addresses either way
   CUtensorMap km, vm;
-  if (!cache_map(p.kc, rows, &km) || !cache_map(p.vc, rows, &vm)) return cudaErrorInvalidValue;
+  bool three_d = attn_box_on() && cache_map(p.kc, rows, true, &km) && cache_map(p.vc, rows, true, &vm);
+  if (!three_d && (!cache_map(p.kc, rows, false, &km) || !cache_map(p.vc, rows, false, &vm)))
+    return cudaErrorInvalidValue;
   const size_t smem = sizeof(TcSmem) + 1024;  // + slack to align the base to 1024
   static bool configured = false;
   if (!configured) {
@@ -733,6 +765,7 @@ cudaError_t launch_attn_tc(const AttnParams& p, int B, int pdl, cudaStream_t st)
     return e ? atoi(e) : 1;
   }();
   AttnParams q = p;
+  q.box3 = three_d ? 1 : 0;
   q.cluster = clus_on && p.nsplit >= 2 && p.nsplit <= kMaxCluster && p.Hq / p.Hk <= kMaxPushG;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nsplit, p.Hk, p.R);
@@ -773,6 +806,13 @@ cudaError_t launch_attn(const AttnParams& p, int pdl, cudaStream_t st) {
 
 }  // namespace
 
+
+extern "C" int hm_decode_attn_box_form(const void* cache, int64_t rows) {
+  if (!cache || rows < 1 || (reinterpret_cast<uintptr_t>(cache) & 15u)) return HM_EARG;
+  CUtensorMap m;
+  if (attn_box_on() && cache_map(cache, rows, true, &m)) return 1;
+  return cache_map(cache, rows, false, &m) ? 0 : HM_EARG;
+}
 
 extern "C" size_t hm_decode_attn_workspace_bytes(int R, int Hq, int hd, int nsplit) {
   if (nsplit <= 1) return 0;

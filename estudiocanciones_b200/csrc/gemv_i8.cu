@@ -66,6 +66,8 @@ struct GemvParams {
   int nst;      // ring stages: deeper when the CTAs per SM leave shared memory free
   int cluster;  // the nsplit k-ranges of a tile run as one thread-block cluster and reduce in DSMEM
   int groups;   // consumer groups in use (wide kernel): each streams its own tiles through its own ring
+  int box;      // weight map: 0 = 2-D, four 16-row x 128-byte boxes per stage; 1 = one box per stage
+                // (3-D for one row block, 4-D for the w1|w3 pair: the same shared-memory layout)
 };
 
 struct SmemLayout {
@@ -219,10 +221,17 @@ __global__ void __launch_bounds__(threads_of(GR), GR == 1 ? (MT == 1 ? 0 : 2) : 
         const int tile = (int)blockIdx.x + (g + (it / per_tile) * G) * (int)gridDim.x;
         const int kx = k0 + (it % per_tile) * KS;
         mbar_arrive_expect_tx(&gfull[slot], kStage);
+        if (P.box) {  // one request per stage (the TMA unit's cost is per box as much as per byte)
+          if (RT == 1)
+            tma_load_3d(gring + slot * kStage, &wmap, 0, tile * kTileRows, kx / kBox, &gfull[slot], pol);
+          else
+            tma_load_4d(gring + slot * kStage, &wmap, 0, tile * kTileRows, 0, kx / kBox, &gfull[slot], pol);
+        } else {
 #pragma unroll
-        for (int b = 0; b < 4; ++b)
-          tma_load_2d(gring + slot * kStage + b * kBoxBytes, &wmap, kx + (b / RT) * kBox,
-                      (RT == 2 && (b % RT) == 1 ? half_n : 0) + tile * kTileRows, &gfull[slot], pol);
+          for (int b = 0; b < 4; ++b)
+            tma_load_2d(gring + slot * kStage + b * kBoxBytes, &wmap, kx + (b / RT) * kBox,
+                        (RT == 2 && (b % RT) == 1 ? half_n : 0) + tile * kTileRows, &gfull[slot], pol);
+        }
         if (++slot == nst) {
           slot = 0;
           ++round;
@@ -765,19 +774,30 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 struct MapKey {
   const void* p;
-  int n, k;
-  bool operator==(const MapKey& o) const { return p == o.p && n == o.n && k == o.k; }
+  int n, k, kind;
+  bool operator==(const MapKey& o) const { return p == o.p && n == o.n && k == o.k && kind == o.kind; }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
-    return std::hash<const void*>()(k.p) ^ (static_cast<size_t>(k.n) * 1000003u) ^ (static_cast<size_t>(k.k) << 20);
+    return std::hash<const void*>()(k.p) ^ (static_cast<size_t>(k.n) * 1000003u) ^ (static_cast<size_t>(k.k) << 20) ^
+           (static_cast<size_t>(k.kind) << 40);
   }
 };
 
-bool weight_map(const int8_t* w, int N, int K, CUtensorMap* out) {
+// Tensor map of the int8 weights [N, K] (row pitch K bytes), 128B swizzle.
+//  kind 0: 2-D {K, N}, box 128 x 16 (2 KB): four requests per 8 KB stage.
+//  kind 1: 3-D {128, N, K/128} (k within a 128-byte chunk, row, chunk; the chunk stride is
+//          128 bytes), box {128, 16, 4}: one request per stage, laid out in shared memory as
+//          [chunk][row][128 bytes] -- the four 2-D boxes of kind 0, in the same order.
+//  kind 2: 4-D {128, N/2, 2, K/128} for the fused w1|w3 matrix (row within a half, half,
+//          chunk), box {128, 16, 2, 2}: [chunk][half][row][128 bytes], again kind 0's layout
+//          for the SiLU epilogue (w1 rows, w3 rows of the same k chunk side by side).
+// Kinds 1 and 2 need K % 128 == 0 (a chunk must not run into the next row: out-of-range
+// k would otherwise read the next row's bytes instead of the zero fill).
+bool weight_map(const int8_t* w, int N, int K, int kind, CUtensorMap* out) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  const MapKey key{w, N, K};
+  const MapKey key{w, N, K, kind};
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -788,14 +808,33 @@ bool weight_map(const int8_t* w, int N, int K, CUtensorMap* out) {
   }
   auto enc = get_encode_fn();
   if (!enc) return false;
+  if (kind != 0 && (K % kBox || (kind == 2 && N % (2 * kTileRows)))) return false;
   CUtensorMap m;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
-  cuuint32_t box[2] = {kBox, kTileRows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const cuuint64_t k = static_cast<cuuint64_t>(K), n = static_cast<cuuint64_t>(N);
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r;
+  if (kind == 0) {
+    cuuint64_t dims[2] = {k, n};
+    cuuint64_t strides[1] = {k};
+    cuuint32_t box[2] = {kBox, kTileRows};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (kind == 1) {
+    cuuint64_t dims[3] = {kBox, n, k / kBox};
+    cuuint64_t strides[2] = {k, kBox};
+    cuuint32_t box[3] = {kBox, kTileRows, 4};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[4] = {kBox, n / 2, 2, k / kBox};
+    cuuint64_t strides[3] = {k, (n / 2) * k, kBox};
+    cuuint32_t box[4] = {kBox, kTileRows, 2, 2};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return false;
   std::lock_guard<std::mutex> lk(mu);
   if (cache.size() > 4096) cache.clear();
@@ -1040,7 +1079,19 @@ cudaError_t launch_mt(int mt, const CUtensorMap& map, const GemvParams& p, cudaS
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+int gemv_box_on() {
+  static const int on = static_cast<int>(env_or("HM_GEMV_BOX", 1));
+  return on;
+}
+
 }  // namespace
+
+extern "C" int hm_gemv_box_form(const int8_t* w, int N, int K, int epi) {
+  if (!w || N < 1 || K < 16 || K % 16 || (epi == HM_EPI_SILU && N % (2 * kTileRows))) return HM_EARG;
+  CUtensorMap m;
+  if (gemv_box_on() && weight_map(w, N, K, epi == HM_EPI_SILU ? 2 : 1, &m)) return 1;
+  return weight_map(w, N, K, 0, &m) ? 0 : HM_EARG;
+}
 
 
 extern "C" int hm_gemv_pick_kspan(int M, int N, int K, int epi, int kspan) {
@@ -1121,8 +1172,15 @@ extern "C" int hm_gemv_i8_fused(const hm_gemv_desc* d, hm_stream_t stream) {
         d->ws_bytes < hm_gemv_workspace_bytes(d->M, d->N, d->K, d->epi, p.kspan))
       return HM_EARG;
   }
+  // one weight request per stage (HM_GEMV_BOX=1, the default) where the map allows it,
+  // else four 2-D boxes; both fill the ring identically, so the results are the same
   CUtensorMap map;
-  if (!weight_map(d->w, d->N, d->K, &map)) return HM_EARG;
+  p.box = 0;
+  if (gemv_box_on() && weight_map(d->w, d->N, d->K, d->epi == HM_EPI_SILU ? 2 : 1, &map)) {
+    p.box = 1;
+  } else if (!weight_map(d->w, d->N, d->K, 0, &map)) {
+    return HM_EARG;
+  }
   const int mt = d->M <= 8 ? 1 : (d->M <= 16 ? 2 : 4);
   cudaError_t e;
   static const int generic = static_cast<int>(env_or("HM_GEMV_ONE_KERNEL", 1));

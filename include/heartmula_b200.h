@@ -345,6 +345,13 @@ int hm_codec_overlap_add(const float* cur, int64_t cur_ld, float* out, int64_t o
 
 /* ------------------------------------------------------------------ info */
 int hm_device_sm_count(int device);
+/* Form of the TMA requests a launch would use (no counterpart in the reference, whose Triton
+ * kernels load with plain pointer arithmetic): 1 = one 3-D / 4-D box per 8 KB GEMV weight stage
+ * (K % 128 == 0) or per 16 KB K / V tile of the tensor-core decode attention, 0 = several 2-D
+ * boxes (HM_GEMV_BOX=0 / HM_ATTN_BOX=0 in the environment, or a shape the 3-D map cannot
+ * describe), HM_EARG for bad arguments.  Both forms fill shared memory identically. */
+int hm_gemv_box_form(const int8_t* w, int N, int K, int epi);
+int hm_decode_attn_box_form(const void* cache, int64_t rows);
 /* sizeof / offsetof of the descriptor structs, for bindings to verify their layout:
  * 0 sizeof(hm_row_src), 1 sizeof(hm_gemv_desc), 2 offsetof(hm_gemv_desc, src),
  * 3 offsetof(hm_gemv_desc, ws), 4 offsetof(hm_gemv_desc, pdl), 5 offsetof(hm_gemv_desc, l2_keep),
