@@ -184,20 +184,21 @@ __global__ void __launch_bounds__(threads_of(GR), GR == 1 ? (MT == 1 ? 0 : 2) : 
     if (tid == 0) report_error(d.err, HM_ERR_TIMEOUT);
     return;
   }
+  // ring barriers initialised one per thread (one thread takes ~1 us for the ~100 of the
+  // wide kernel, on the way to the dependency wait); each thread fences its own
+  for (int i = tid; i < G * nst; i += static_cast<int>(blockDim.x)) {
+    mbar_init(&full[(i / nst) * kMaxNST + i % nst], 1);
+    mbar_init(&empty[(i / nst) * kMaxNST + i % nst], kGW);
+  }
   if (tid == 0) {
     *abort_s = 0;
-    for (int g = 0; g < G; ++g)
-      for (int i = 0; i < nst; ++i) {
-        mbar_init(&full[g * kMaxNST + i], 1);
-        mbar_init(&empty[g * kMaxNST + i], kGW);
-      }
     mbar_init(xbar, 1);
     if (P.cluster) {
       mbar_init(cready, P.nsplit - 1);
       mbar_init(cdone, 1);
     }
-    fence_barrier_init();
   }
+  fence_barrier_init();
   __syncthreads();
   if (P.cluster) cluster_sync_all();  // every CTA's split barriers exist before any remote arrival
 
@@ -349,8 +350,9 @@ __global__ void __launch_bounds__(threads_of(GR), GR == 1 ? (MT == 1 ? 0 : 2) : 
   const int er = gtid & 15, em0 = gtid >> 4;
   const int half_n = RT == 2 ? N / 2 : 0;
   int nn = ((int)blockIdx.x + grp * (int)gridDim.x) * kTileRows + er;  // row of the next tile's scale
-  float sc0n = tiles_g > 0 && nn < N ? __half2float(scales[nn]) : 0.f;
-  float sc1n = RT == 2 && tiles_g > 0 && half_n + nn < N ? __half2float(scales[half_n + nn]) : 0.f;
+  // (kept in fp16 until first used, so the loads stay in flight across the dependency wait)
+  __half sc0n = tiles_g > 0 && nn < N ? scales[nn] : __ushort_as_half(0);
+  __half sc1n = RT == 2 && tiles_g > 0 && half_n + nn < N ? scales[half_n + nn] : __ushort_as_half(0);
 
   pdl_wait();  // activations, tokens and sums of squares come from earlier launches
 
@@ -526,11 +528,11 @@ __global__ void __launch_bounds__(threads_of(GR), GR == 1 ? (MT == 1 ? 0 : 2) : 
   for (int ti = 0; ti < tiles_g; ++ti) {
     const int tile = (int)blockIdx.x + (grp + ti * G) * (int)gridDim.x;
     const int n0 = tile * kTileRows + er;
-    const float sc0 = sc0n, sc1 = sc1n;
+    const float sc0 = __half2float(sc0n), sc1 = __half2float(sc1n);
     if (ti + 1 < tiles_g) {
       nn += G * (int)gridDim.x * kTileRows;
-      sc0n = nn < N ? __half2float(scales[nn]) : 0.f;
-      if (RT == 2) sc1n = half_n + nn < N ? __half2float(scales[half_n + nn]) : 0.f;
+      sc0n = nn < N ? scales[nn] : __ushort_as_half(0);
+      if (RT == 2) sc1n = half_n + nn < N ? scales[half_n + nn] : __ushort_as_half(0);
     }
     float acc[MT][4];
 #pragma unroll
