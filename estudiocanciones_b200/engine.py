@@ -116,13 +116,16 @@ class Stack:
         self.dim = self.norm.numel()
         self.hd = self.blocks[0].hd
         self.rope = None
+        self._decode_plans = {}  # decode(): launch plans and buffers per (rows, S, splits, device)
 
     def alloc(self, B, L, dev):
+        self._decode_plans = {}
         self.rope = rope_table(self.hd, max(L, 16)).to(dev)
         for b in self.blocks:
             b.alloc(B, L, dev)
 
     def free(self):
+        self._decode_plans = {}
         for b in self.blocks:
             b.kc = b.vc = None
 
@@ -136,17 +139,27 @@ class Stack:
         pos ``[R]`` int64 on the device.  Returns ``rms(x_out, norm)``; caches are updated in place."""
         R = x.shape[0]
         ns = nsplit or default_nsplit(R, self.blocks[0].kvh, self.L)
-        L = _lib.lib()
-        g = max(max(L.hm_gemv_workspace_bytes(R, b.qkv.N, b.qkv.K, HM_EPI_ROPE_KV, 0),
-                    L.hm_gemv_workspace_bytes(R, b.o.N, b.o.K, HM_EPI_STORE, 0),
-                    L.hm_gemv_workspace_bytes(R, b.w13.N, b.w13.K, HM_EPI_SILU, 0),
-                    L.hm_gemv_workspace_bytes(R, b.w2.N, b.w2.K, HM_EPI_STORE, 0)) for b in self.blocks)
-        ctx = _Ctx(x.device, g, L.hm_decode_attn_workspace_bytes(R, self.blocks[0].h, self.hd, ns))
-        bufs = StackBuffers(self, R, x.device)
+        # The launch plan (descriptors with raw pointers), its buffers and scratch are built
+        # once per shape and reused: a call copies x and pos into the plan's buffers and
+        # replays it.  alloc() / free() (and so to()) drop the plans with the caches.
+        key = (R, S, ns, str(x.device), self.blocks[0].kc.data_ptr())
+        st = self._decode_plans.get(key)
+        if st is None:
+            L = _lib.lib()
+            g = max(max(L.hm_gemv_workspace_bytes(R, b.qkv.N, b.qkv.K, HM_EPI_ROPE_KV, 0),
+                        L.hm_gemv_workspace_bytes(R, b.o.N, b.o.K, HM_EPI_STORE, 0),
+                        L.hm_gemv_workspace_bytes(R, b.w13.N, b.w13.K, HM_EPI_SILU, 0),
+                        L.hm_gemv_workspace_bytes(R, b.w2.N, b.w2.K, HM_EPI_STORE, 0)) for b in self.blocks)
+            ctx = _Ctx(x.device, g, L.hm_decode_attn_workspace_bytes(R, self.blocks[0].h, self.hd, ns))
+            bufs = StackBuffers(self, R, x.device)
+            pos_buf = torch.zeros(R, dtype=torch.long, device=x.device)
+            plan = FramePlan(ctx)
+            plan.sumsq(bufs.x, bufs.ss, R)
+            plan.stack(self, bufs, pos_buf, S, R, ns)
+            st = self._decode_plans[key] = (plan, bufs, pos_buf)
+        plan, bufs, pos_buf = st
         bufs.x.copy_(x)
-        plan = FramePlan(ctx)
-        plan.sumsq(bufs.x, bufs.ss, R)
-        plan.stack(self, bufs, pos, S, R, ns)
+        pos_buf.copy_(pos)
         plan.run()
         return kernels.rms(bufs.x, self.norm)
 

@@ -106,3 +106,33 @@ def test_torch_library_operators_match_kernels():
     O.attn(q, kc, vc, pos, o1, 1, 8, 2, 200, 1.0 / math.sqrt(128), 4)
     K.attn(q, kc, vc, pos, o2, 1, 8, 2, 200, 1.0 / math.sqrt(128), nsplit=4)
     assert torch.equal(o1, o2)
+
+
+def test_stack_decode_reuses_its_plan_with_new_inputs(model):
+    """Stack.decode keeps its launch plan per shape: a second call with other rows and
+    positions (copied into the plan's buffers) gives what the reference loop gives."""
+    from estudiocanciones_b200 import kernels as K
+    st = model.backbone
+    R, S, L, p = 8, 1, 640, 300
+    st.alloc(R, L, torch.device(DEV))
+    gen = torch.Generator(device=DEV).manual_seed(77)
+    for b in st.blocks:
+        b.kc[:, :, :p + 8].normal_(generator=gen)
+        b.vc[:, :, :p + 8].normal_(generator=gen)
+    x1 = (torch.randn(R, st.dim, generator=gen, device=DEV) * 0.5).half()
+    st.decode(x1, torch.full((R,), p, dtype=torch.long, device=DEV), S)
+    assert len(st._decode_plans) == 1
+    kv0 = [(b.kc.clone(), b.vc.clone()) for b in st.blocks]
+    x2 = (torch.randn(R, st.dim, generator=gen, device=DEV) * 0.5).half()
+    pos2 = torch.arange(R, device=DEV) + p - 3
+    ours = st.decode(x2, pos2, S)
+    assert len(st._decode_plans) == 1
+    for b, (kc, vc) in zip(st.blocks, kv0):
+        b.kc.copy_(kc)
+        b.vc.copy_(vc)
+    theirs = reference_style_decode(K, st, x2, pos2, S)
+    torch.cuda.synchronize()
+    assert K.read_errors(DEV) == 0
+    torch.testing.assert_close(theirs.float(), ours.float(), atol=2e-2, rtol=2e-2)
+    st.free()
+    assert not st._decode_plans
