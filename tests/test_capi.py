@@ -63,6 +63,13 @@ def test_host_argument_validation_without_gpu(lib):
     assert lib.hm_q8_rows(1, 0, 4, 16, 16, 1, 8, 1, None) == -1      # ldq < K
     assert lib.hm_q8_rows(1, 9, 4, 16, 16, 1, 16, 1, None) == -1     # no such element type
     assert lib.hm_q8_rows(1, 0, 0, 16, 16, 1, 16, 1, None) == -1     # no rows
+    # TMA request-form queries: argument checks come before any tensor-map encoding
+    assert lib.hm_gemv_box_form(None, 64, 128, 0) == -1
+    assert lib.hm_gemv_box_form(16, 64, 100, 0) == -1                 # K not a multiple of 16
+    assert lib.hm_gemv_box_form(16, 48, 128, 2) == -1                 # SiLU: N not a multiple of 32
+    assert lib.hm_decode_attn_box_form(None, 64) == -1
+    assert lib.hm_decode_attn_box_form(24, 64) == -1                  # cache not 16-byte aligned
+    assert lib.hm_decode_attn_box_form(16, 0) == -1
 
 
 def test_workspace_sizing_is_consistent(lib):
