@@ -81,3 +81,21 @@ def test_graph_capture_keeps_the_cyclic_collector_off():
         assert not gc.isenabled()  # a caller that had it off keeps it off
     finally:
         (gc.enable if was else gc.disable)()
+
+
+def test_stack_decode_plans_dropped_with_the_caches():
+    """Stack.decode's per-shape launch plans hold raw pointers into the caches and weights:
+    alloc() and free() (which the model's to() calls) drop them.  On the CPU, no launch."""
+    from estudiocanciones_b200.engine import Linear, Stack
+    t = synthetic_tensors(TINY_SHAPE, seed=5)
+
+    def get(name, norm=False):
+        return t[name].to(torch.float16) if norm else Linear(t[name + ".q8"], t[name + ".s8"])
+    st = Stack(get, "backbone", TINY_SHAPE.bb_heads, t)
+    st.alloc(2, 32, torch.device("cpu"))
+    st._decode_plans["stale"] = object()
+    st.alloc(2, 48, torch.device("cpu"))
+    assert not st._decode_plans and st.L == 48
+    st._decode_plans["stale"] = object()
+    st.free()
+    assert not st._decode_plans and st.blocks[0].kc is None
